@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""FP8 MoE layer benchmark (decode step at 64 tokens per GPU).
+
+Workload per step (one GPU): the decode projections and MoE layer of the
+benchmark geometry H=2048, E=128, I=768, top-8, FP8-E4M3 with 128x128 fp32
+block scales:
+    qkv = fp8_gemv(x, Wqkv [4096,2048])             dense weight-only FP8
+    o   = fp8_gemv(qkv[:, :2048], Wo [2048,2048])   (o_proj input stand-in)
+    y   = moe_layer(o)  router -> top-8 -> routed + shared experts -> combine
+Synthetic seeded weights (N(0,0.02) quantised per 128x128 block), bf16 N(0,1)
+inputs. Steps rotate over `--layers` independent weight sets (4 x ~620 MB by
+default, > 2x the 126 MB L2), so weights stream from HBM every step.
+
+With torchrun (N > 1) every rank runs the same per-GPU workload on its own
+replica of the layer ("replicas"); the expert-parallel layer is measured by
+`--ep`. Timing: CUDA events on the launching stream, barrier + synchronize on
+both sides, max over ranks.
+
+--impl reference times the reference's arithmetic on the host CPU (the oracle
+port of src/drama3/kernels.py et al.; the reference itself has no CPU path and
+cannot run on this box's GPU tooling), one bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "drama-3-single-b300-inference_b200"
+sys.path.insert(0, str(PKG))
+
+E, I, H, TOPK = 128, 768, 2048, 8
+N_QKV, N_O = 4096, 2048
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic_bytes(ids_host, T: int) -> dict:
+    """Bytes a step must move at minimum (weights of the U distinct selected
+    experts + shared expert + router + dense projections + activations)."""
+    import numpy as np
+
+    U = len(np.unique(ids_host))
+    w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
+    w2 = H * I + (H // 128) * (I // 128) * 4
+    R = T * TOPK + T
+    gate_up = (U + 1) * w13 + R * (H + H // 128 * 4) + R * (I + I // 128 * 4)
+    down = (U + 1) * w2 + R * (I + I // 128 * 4) + R * H * 4
+    router = (E + 1) * H * 2 + T * H * 2
+    dense = N_QKV * H + (N_QKV // 128) * (H // 128) * 4 + N_O * H + (N_O // 128) * (H // 128) * 4
+    dense += T * H * 2 * 2 + T * (N_QKV + N_O) * 2
+    total = gate_up + down + router + dense + T * H * 2
+    return {"U": U, "gate_up": gate_up, "down": down, "dense": dense, "total": total}
+
+
+def cpu_baseline(T: int, seconds: float, weights_cpu) -> dict:
+    """Oracle port on the host cores: whole decode steps (dense projections +
+    MoE layer) until `seconds` of work have been done (at least one step)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import moe_oracle as O
+
+    rng = np.random.default_rng(0)
+    (wqkv, sqkv, wo, so, router, ex, sh) = weights_cpu
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        x = O.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        qkv = O.fp8_gemv(x, wqkv, sqkv)
+        o = O.fp8_gemv(qkv[:, :H], wo, so)
+        O.moe_layer(o, router, ex, sh, TOPK)
+        steps += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    threads = int(os.environ.get("OMP_NUM_THREADS", "0")) or os.cpu_count()
+    return {"value": T * steps / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} decode step(s) of T={T}: fp8 QKV+o_proj GEMV + full MoE layer "
+                      f"(numpy, BLAS threads={threads}), {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    """--impl reference: the oracle port on host cores, bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import moe_oracle as O
+
+    T = args.tokens
+    rng = np.random.default_rng(1)
+    # CPU synthetic layer (hashed uniform weights quantised per 128x128 block)
+    ex = O.Experts(*[{} for _ in range(4)])
+    for e in range(E):
+        ex.w13[e], ex.s13[e] = O.synth_expert(21, e, 2 * I, H, amp=0.035)
+        ex.w2[e], ex.s2[e] = O.synth_expert(22, e, H, I, amp=0.035)
+    sh = O.Experts({0: None}, {0: None}, {0: None}, {0: None})
+    sh.w13[0], sh.s13[0] = O.synth_expert(23, 0, 2 * I, H, amp=0.035)
+    sh.w2[0], sh.s2[0] = O.synth_expert(24, 0, H, I, amp=0.035)
+    router = O.bf16_round((O.hash_uniform(25, (E + 1, H)) * 0.035).astype(np.float32))
+    wqkv, sqkv = O.synth_expert(26, 0, N_QKV, H, amp=0.035)
+    wo, so = O.synth_expert(27, 0, N_O, H, amp=0.035)
+
+    def step():
+        x = O.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        qkv = O.fp8_gemv(x, wqkv, sqkv)
+        o = O.fp8_gemv(qkv[:, :H], wo, so)
+        O.moe_layer(o, router, ex, sh, TOPK)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = T * args.steps / dt
+    threads = int(os.environ.get("OMP_NUM_THREADS", "0")) or os.cpu_count()
+    line = {
+        "impl": "reference", "metric": "fp8_moe_layer_decode_tokens_per_s", "value": value,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8_e4m3 x fp8_e4m3 -> f32", "data": "synthetic",
+        "config": {"workload": f"decode T={T}: FP8 QKV+o_proj GEMV + MoE layer (H=2048,E=128,I=768,top-8)",
+                   "tokens_per_step": T},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full decode steps of T={T} on host cores "
+                                   "(numpy oracle port of the reference arithmetic)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU per step")
+    ap.add_argument("--layers", type=int, default=4, help="weight sets rotated across steps")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from d3moe import _lib, ops, synth
+
+    T = args.tokens
+    lib = _lib.load()
+    layers, dense = [], []
+    for li in range(args.layers):
+        seed = 1000 * rank + li
+        layers.append(synth.make_layer(E, I, H, seed=seed, device=dev))
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed + 77)
+        wq, sq = synth.block_quantize(torch.randn((N_QKV, H), generator=g, device=dev) * 0.02)
+        wo, so = synth.block_quantize(torch.randn((N_O, H), generator=g, device=dev) * 0.02)
+        dense.append((wq, sq, wo, so))
+    views = [(ops.ExpertView(l.experts), ops.ExpertView(l.shared)) for l in layers]
+    ws_moe = ops.moe_workspace(T, TOPK, E, I, H, True, dev)
+    nb = ctypes.c_size_t()
+    lib.d3_fp8_gemv_workspace_size(T, H, ctypes.byref(nb))
+    ws_dense = torch.empty(nb.value, dtype=torch.uint8, device=dev)
+    nsteps_total = args.warmup + args.steps
+    gin = torch.Generator(device=dev)
+    gin.manual_seed(4242 + rank)
+    xs = torch.randn((args.layers * 4, T, H), generator=gin, device=dev).to(torch.bfloat16)
+    qkv = torch.empty((T, N_QKV), dtype=torch.bfloat16, device=dev)
+    o = torch.empty((T, N_O), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    ids_all = torch.empty((args.steps, T, TOPK), dtype=torch.int64, device=dev)
+    wts = torch.empty((T, TOPK), dtype=torch.bfloat16, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    def gemv(x, x_ld, wq, sq, n, out):
+        _lib.call("d3_fp8_gemv", x.data_ptr(), x_ld, wq.data_ptr(), sq.data_ptr(), T, n, H,
+                  out.data_ptr(), out.stride(0), ws_dense.data_ptr(), ws_dense.numel(),
+                  status.data_ptr(), sptr)
+
+    def step(i: int, x: torch.Tensor, ids_buf):
+        li = i % args.layers
+        wq, sq, wo_, so_ = dense[li]
+        gemv(x, x.stride(0), wq, sq, N_QKV, qkv)
+        gemv(qkv, qkv.stride(0), wo_, so_, N_O, o)  # first 2048 columns of qkv, row stride 4096
+        lw = layers[li]
+        ev, sv = views[li]
+        _lib.call("d3_moe_layer", o.data_ptr(), o.stride(0), lw.router.data_ptr(), None, T, TOPK,
+                  ctypes.byref(ev.struct), ctypes.byref(sv.struct), y.data_ptr(),
+                  None if ids_buf is None else ids_buf.data_ptr(), wts.data_ptr(),
+                  ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), sptr)
+
+    launches_per_step = 2 * 2 + 7  # (act prep + engine) x 2 GEMVs; router, route, permute, gather, gate_up, down, combine
+
+    # per-step stage events (gate_up / down engine launches) inside the timed region
+    stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    for evs in stage_events:
+        for e in evs:
+            e.record(stream)  # materialise the cudaEvent_t handles
+    stage_arrays = [(ctypes.c_void_p * 5)(*[e._as_parameter_.value for e in evs]) for evs in stage_events]
+
+    for i in range(args.warmup):
+        step(i, xs[i % len(xs)], None)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            lib.d3_set_stage_events(stage_arrays[i], 5)
+            step(args.warmup + i, xs[(args.warmup + i) % len(xs)], ids_all[i])
+            lib.d3_set_stage_events(None, 0)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    gate_ms = [evs[1].elapsed_time(evs[2]) for evs in stage_events]
+    down_ms = [evs[2].elapsed_time(evs[3]) for evs in stage_events]
+    moe_ms = [evs[0].elapsed_time(evs[4]) for evs in stage_events]
+    ids_host = ids_all.cpu().numpy()
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status word {int(status.item())}: a bounded wait timed out")
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ---- end-to-end through the C ABI with host buffers (pinned H2D + D2H per step)
+    hx = torch.randn((T, H)).to(torch.bfloat16).pin_memory()
+    hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    for i in range(3):
+        dx.copy_(hx, non_blocking=True)
+        step(i, dx, None)
+        hy.copy_(y, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        step(i, dx, None)
+        hy.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    pk = peaks()
+    per_step = [algorithmic_bytes(ids_host[i], T) for i in range(args.steps)]
+    gate_bytes = statistics.mean(p["gate_up"] for p in per_step)
+    down_bytes = statistics.mean(p["down"] for p in per_step)
+    total_bytes = statistics.mean(p["total"] for p in per_step)
+    gate_avg = statistics.mean(gate_ms)
+    down_avg = statistics.mean(down_ms)
+    achieved = gate_bytes / (gate_avg * 1e-3) / 1e9
+    line = {
+        "metric": "fp8_moe_layer_decode_tokens_per_s",
+        "value": T * world / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8_e4m3 x fp8_e4m3 -> f32 (experts); fp8 weights x bf16 (dense)",
+        "data": "synthetic",
+        "config": {
+            "workload": f"decode T={T}/GPU: FP8 QKV[4096x2048] + o_proj[2048x2048] weight-only GEMV + "
+                        "MoE layer (H=2048, E=128, I=768, top-8, shared expert), 128x128 fp32 block scales",
+            "tokens_per_gpu": T, "weight_sets_rotated": args.layers,
+            "l2": f"inputs larger than L2: {args.layers} weight sets x "
+                  f"{layers[0].nbytes() / 1e6:.0f} MB rotated per step",
+            "parallelism": "replicas" if world > 1 else "single",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "expert_gemv_kernel<EPI_GATE_UP> (gate_up + SiLU*mul + FP8 requant)",
+            "achieved": achieved,
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "traffic": None,
+            "algorithmic_bytes_per_launch": gate_bytes,
+            "avg_launch_ms": gate_avg,
+            "down_kernel": {"achieved": down_bytes / (down_avg * 1e-3) / 1e9, "avg_launch_ms": down_avg,
+                            "algorithmic_bytes_per_launch": down_bytes},
+            "moe_layer_ms": statistics.mean(moe_ms),
+            "step_bytes": total_bytes,
+            "step_achieved_gbs": total_bytes / (ms * 1e-3) / 1e9,
+            "mean_active_experts": statistics.mean(p["U"] for p in per_step),
+        },
+        "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT))
+        from oracle import moe_oracle as O
+
+        def cpu_ex(ex):
+            return O.Experts(ex.w13_weight.view(torch.uint8).cpu().numpy(), ex.w13_scale_inv.cpu().numpy(),
+                             ex.w2_weight.view(torch.uint8).cpu().numpy(), ex.w2_scale_inv.cpu().numpy())
+
+        wq, sq, wo_, so_ = dense[0]
+        weights_cpu = (wq.view(torch.uint8).cpu().numpy(), sq.cpu().numpy(), wo_.view(torch.uint8).cpu().numpy(),
+                       so_.cpu().numpy(), layers[0].router.float().cpu().numpy(), cpu_ex(layers[0].experts),
+                       cpu_ex(layers[0].shared))
+        line["cpu_baseline"] = cpu_baseline(T, args.cpu_seconds, weights_cpu)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

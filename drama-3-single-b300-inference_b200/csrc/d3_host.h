@@ -1,0 +1,41 @@
+// Host-side helpers shared by the C-ABI translation units: error reporting,
+// argument checks and TMA tensor-map encoding through the driver entry point.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/d3moe.h"
+
+namespace d3 {
+
+// Records a printf-style message as this thread's last error and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+// Checks the launch that was just enqueued.
+int check_launch(const char* what);
+
+// Encodes a 2-D tiled tensor map over a row-major [rows, cols] tensor of
+// `elem_bytes`-byte elements with row pitch `pitch_bytes`, a box of
+// [box_rows, box_cols] and 128-byte swizzle. Returns D3_OK or an error.
+int encode_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t cols,
+                   uint64_t rows, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace d3
+
+#define D3_REQUIRE(cond, ...)                                  \
+  do {                                                         \
+    if (!(cond)) return ::d3::set_error(D3_EINVAL, __VA_ARGS__); \
+  } while (0)

@@ -1,0 +1,43 @@
+// Launchers shared between translation units (not part of the public C ABI).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace d3 {
+
+// x rows -> e4m3 rows gathered in expert-sorted order. Row r < P takes token
+// sorted_pairs[r] / k (a sentinel >= P gives a zero row); rows P..P+T-1 (when
+// with_shared) take tokens 0..T-1 for the shared expert.
+void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
+                         const int32_t* sorted_pairs, int P, int with_shared, uint8_t* xq,
+                         float* sx, cudaStream_t s);
+
+// Weight-only GEMV activation prep: x bf16 [T,K] -> f16 [T,K] scaled by a
+// power of two per 1x128 group (exact), inv f32 [T,K/128] = the inverse factor.
+void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
+                           cudaStream_t s);
+
+// Final combine of the expert rows (see d3_moe_experts / d3_moe_layer).
+//   routed[t] = bf16(sum_r w[t,r] * d[inv_rows[t*k+r]])
+//   shared[t] = bf16(d[P+t])                                   (when with_shared)
+//   out[t]    = routed + bf16(shared * bf16(sigmoid(gate[t]))) (when gate != null)
+void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,
+                         int T, int k, int with_shared, const void* gate, int64_t gate_stride,
+                         void* routed_out, void* shared_out, void* out, cudaStream_t s);
+
+void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
+                          int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
+                          cudaStream_t s);
+
+void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
+                       const float* bias, int64_t* ids, void* weights, int weights_dtype,
+                       cudaStream_t s);
+
+int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
+                   int32_t* starts, int32_t* total, int32_t* sorted_ids, int32_t* expert_ids,
+                   int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,
+                   cudaStream_t s);
+
+}  // namespace d3

@@ -1,0 +1,465 @@
+// Bandwidth-bound row kernels of the MoE path: activation FP8 quantisation
+// (plain, fused with router-logit conversion, and gathered into expert order),
+// SiLU*mul (+ requant), routed/shared combine, 128x128 weight quantisation and
+// the f16 activation prep of the weight-only dense GEMV.
+//
+// Layout rule for all of them: one warp owns one row; a half-warp owns one
+// 128-element quantisation group, each lane 8 consecutive elements (16-byte
+// loads), so the group amax is a 4-step shuffle inside the half-warp.
+#include "d3_common.cuh"
+#include "d3_host.h"
+#include "d3_internal.h"
+
+namespace d3 {
+
+namespace {
+
+constexpr int kRowWarps = 8;  // rows per 256-thread CTA
+
+__device__ __forceinline__ void unpack_bf16x8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint2 quant8(const float (&f)[8], float scale) {
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) lo |= static_cast<uint32_t>(act_quant(f[i], scale)) << (8 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hi |= static_cast<uint32_t>(act_quant(f[4 + i], scale)) << (8 * i);
+  return make_uint2(lo, hi);
+}
+
+__device__ __forceinline__ float half_warp_max(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Quantise one bf16 row of G groups (warp-cooperative). scale for group g goes
+// to s[g * s_step].
+__device__ __forceinline__ void quant_row(const __nv_bfloat16* x, int G, uint8_t* q, float* s,
+                                          int64_t s_step) {
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  for (int g0 = 0; g0 < G; g0 += 2) {
+    const int g = g0 + half;
+    const bool valid = g < G;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid) v = *reinterpret_cast<const uint4*>(x + g * 128 + hl * 8);
+    float f[8];
+    unpack_bf16x8(v, f);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    amax = half_warp_max(amax);
+    const float scale = act_scale_from_amax(amax);
+    if (valid) {
+      *reinterpret_cast<uint2*>(q + g * 128 + hl * 8) = quant8(f, scale);
+      if (hl == 0) s[g * s_step] = scale;
+    }
+  }
+}
+
+__global__ void quant_act_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
+                                 int H, uint8_t* __restrict__ q, float* __restrict__ scales,
+                                 int transposed) {
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int G = H / 128;
+  float* s = transposed ? scales + row : scales + static_cast<int64_t>(row) * G;
+  quant_row(x + row * x_stride, G, q + static_cast<int64_t>(row) * H, s, transposed ? T : 1);
+}
+
+__global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                               const __nv_bfloat16* __restrict__ router, int64_t router_stride,
+                               int T, int H, int E, const void* row_slots, int slots64,
+                               int64_t padding_start, uint8_t* __restrict__ q,
+                               float* __restrict__ scales_t, float* __restrict__ logits) {
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int G = H / 128;
+  quant_row(x + row * x_stride, G, q + static_cast<int64_t>(row) * H, scales_t + row, T);
+  int router_row = row;
+  if (padding_start > 0 && row_slots) {
+    const int64_t slot = slots64 ? static_cast<const int64_t*>(row_slots)[row]
+                                 : static_cast<const int32_t*>(row_slots)[row];
+    if (slot >= padding_start) router_row = 0;
+  }
+  const __nv_bfloat16* r = router + router_row * router_stride;
+  for (int e = threadIdx.x & 31; e < E; e += 32)
+    logits[static_cast<int64_t>(row) * E + e] = __bfloat162float(r[e]);
+}
+
+__global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
+                                    int H, int k, const int32_t* __restrict__ sorted_pairs, int P,
+                                    int rows, uint8_t* __restrict__ xq, float* __restrict__ sx) {
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int G = H / 128;
+  int token;
+  if (row < P) {
+    const int p = sorted_pairs[row];
+    token = (p >= 0 && p < P) ? p / k : -1;
+  } else {
+    token = row - P;
+  }
+  uint8_t* qrow = xq + static_cast<int64_t>(row) * H;
+  float* srow = sx + static_cast<int64_t>(row) * G;
+  if (token < 0 || token >= T) {
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < H / 16; i += 32) reinterpret_cast<uint4*>(qrow)[i] = make_uint4(0, 0, 0, 0);
+    for (int g = lane; g < G; g += 32) srow[g] = 0.f;
+    return;
+  }
+  quant_row(x + token * x_stride, G, qrow, srow, 1);
+}
+
+// Exact bf16 -> f16 transfer: each 128-group is multiplied by 2^s with s chosen
+// so that the group amax lands in [2^14, 2^15); the GEMV multiplies by 2^-s.
+__global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
+                                      int K, __half* __restrict__ xh, float* __restrict__ inv) {
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int G = K / 128;
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  for (int g0 = 0; g0 < G; g0 += 2) {
+    const int g = g0 + half;
+    const bool valid = g < G;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid) v = *reinterpret_cast<const uint4*>(x + row * x_stride + g * 128 + hl * 8);
+    float f[8];
+    unpack_bf16x8(v, f);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    amax = half_warp_max(amax);
+    int e = 0;
+    if (amax > 0.f && isfinite(amax)) {
+      frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+      e = 15 - e;        // scaled amax in [2^14, 2^15)
+    }
+    const float mul = ldexpf(1.0f, e);
+    if (valid) {
+      uint32_t h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __half2 p = __floats2half2_rn(f[2 * i] * mul, f[2 * i + 1] * mul);
+        h[i] = *reinterpret_cast<uint32_t*>(&p);
+      }
+      *reinterpret_cast<uint4*>(xh + static_cast<int64_t>(row) * K + g * 128 + hl * 8) =
+          make_uint4(h[0], h[1], h[2], h[3]);
+      if (hl == 0) inv[static_cast<int64_t>(row) * G + g] = ldexpf(1.0f, -e);
+    }
+  }
+}
+
+__device__ __forceinline__ float silu_bf16(float gate_bf16) {
+  // silu(g) = g * sigmoid(g), rounded to bf16 like the reference kernel.
+  return bf16_round(gate_bf16 * (1.0f / (1.0f + expf(-gate_bf16))));
+}
+
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride, int rows,
+                                int W, __nv_bfloat16* __restrict__ out) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = W / 8;
+  if (idx >= static_cast<int64_t>(rows) * per_row) return;
+  const int row = static_cast<int>(idx / per_row), c = static_cast<int>(idx % per_row) * 8;
+  const __nv_bfloat16* r = in + row * in_stride;
+  float g[8], u[8];
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(r + c), g);
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(r + W + c), u);
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 p = __floats2bfloat162_rn(silu_bf16(g[2 * i]) * u[2 * i],
+                                             silu_bf16(g[2 * i + 1]) * u[2 * i + 1]);
+    o[i] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * W + c) =
+      make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride,
+                                      int rows, int W, uint8_t* __restrict__ q,
+                                      float* __restrict__ scales) {
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int G = W / 128;
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  const __nv_bfloat16* r = in + row * in_stride;
+  for (int g0 = 0; g0 < G; g0 += 2) {
+    const int g = g0 + half;
+    const bool valid = g < G;
+    float a[8];
+    if (valid) {
+      float gt[8], up[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(r + g * 128 + hl * 8), gt);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(r + W + g * 128 + hl * 8), up);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = silu_bf16(gt[i]) * up[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(a[i]));
+    amax = half_warp_max(amax);
+    const float scale = act_scale_from_amax(amax);
+    if (valid) {
+      *reinterpret_cast<uint2*>(q + static_cast<int64_t>(row) * W + g * 128 + hl * 8) =
+          quant8(a, scale);
+      if (hl == 0) scales[static_cast<int64_t>(row) * G + g] = scale;
+    }
+  }
+}
+
+__device__ __forceinline__ float sigmoid_gate_bf16(const __nv_bfloat16* gate) {
+  const float g = __bfloat162float(*gate);
+  return bf16_round(1.0f / (1.0f + expf(-g)));
+}
+
+__global__ void combine_experts_kernel(const __nv_bfloat16* __restrict__ routed,
+                                       const __nv_bfloat16* __restrict__ shared,
+                                       const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
+                                       int T, int H, __nv_bfloat16* __restrict__ out) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = H / 8;
+  if (idx >= static_cast<int64_t>(T) * per_row) return;
+  const int t = static_cast<int>(idx / per_row), c = static_cast<int>(idx % per_row) * 8;
+  const float g = sigmoid_gate_bf16(gate + t * gate_stride);
+  float r[8], s[8];
+  const int64_t off = static_cast<int64_t>(t) * H + c;
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(routed + off), r);
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(shared + off), s);
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 p = __floats2bfloat162_rn(r[2 * i] + bf16_round(s[2 * i] * g),
+                                             r[2 * i + 1] + bf16_round(s[2 * i + 1] * g));
+    o[i] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  *reinterpret_cast<uint4*>(out + off) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One thread per 4 output columns of one token. Expert rows are read in rank
+// order r = 0..k-1 and summed in fp32 with the bf16 routing weight.
+__global__ void combine_rows_kernel(const float* __restrict__ d, int H,
+                                    const int32_t* __restrict__ inv_rows,
+                                    const __nv_bfloat16* __restrict__ weights, int T, int k,
+                                    int with_shared, const __nv_bfloat16* __restrict__ gate,
+                                    int64_t gate_stride, __nv_bfloat16* __restrict__ routed_out,
+                                    __nv_bfloat16* __restrict__ shared_out,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = H / 4;
+  if (idx >= static_cast<int64_t>(T) * per_row) return;
+  const int t = static_cast<int>(idx / per_row), c = static_cast<int>(idx % per_row) * 4;
+  const int P = T * k;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int r = 0; r < k; ++r) {
+    const int row = inv_rows[t * k + r];
+    if (row < 0) continue;  // pair whose expert id was out of range: not routed
+    const float w = __bfloat162float(weights[t * k + r]);
+    const float4 v = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(row) * H + c);
+    acc[0] += v.x * w;
+    acc[1] += v.y * w;
+    acc[2] += v.z * w;
+    acc[3] += v.w * w;
+  }
+  float routed[4], shared[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) routed[i] = bf16_round(acc[i]);
+  if (with_shared) {
+    const float4 v = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + t) * H + c);
+    shared[0] = bf16_round(v.x);
+    shared[1] = bf16_round(v.y);
+    shared[2] = bf16_round(v.z);
+    shared[3] = bf16_round(v.w);
+  }
+  const int64_t off = static_cast<int64_t>(t) * H + c;
+  auto store4 = [&](__nv_bfloat16* dst, const float (&v)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 u = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    *reinterpret_cast<uint2*>(dst + off) = u;
+  };
+  if (routed_out) store4(routed_out, routed);
+  if (shared_out && with_shared) store4(shared_out, shared);
+  if (out) {
+    float o[4];
+    if (with_shared && gate) {
+      const float g = sigmoid_gate_bf16(gate + t * gate_stride);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = routed[i] + bf16_round(shared[i] * g);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = routed[i] + shared[i];
+    }
+    store4(out, o);
+  }
+}
+
+// One CTA per 128x128 weight block; 256 threads x 64 elements.
+__global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, int K,
+                                    uint8_t* __restrict__ q, float* __restrict__ scales) {
+  const int nb = blockIdx.x, kb = blockIdx.y, KB = K / 128;
+  __shared__ float red[8];
+  const int tid = threadIdx.x;
+  // thread -> row tid/2, columns (tid%2)*64 .. +63
+  const int row = nb * 128 + tid / 2, col = kb * 128 + (tid & 1) * 64;
+  float f[64];
+  const bool valid = row < N;
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    float t[8];
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (valid) u = *reinterpret_cast<const uint4*>(w + static_cast<int64_t>(row) * K + col + v * 8);
+    unpack_bf16x8(u, t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[v * 8 + i] = t[i];
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(f[i]));
+  amax = warp_max(amax);
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 448.0f);
+  uint8_t* qrow = q + static_cast<int64_t>(row) * K + col;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    uint32_t word[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t b = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        b |= static_cast<uint32_t>(f32_to_e4m3(__fdiv_rn(f[v * 16 + j * 4 + i], scale))) << (8 * i);
+      word[j] = b;
+    }
+    *reinterpret_cast<uint4*>(qrow + v * 16) = make_uint4(word[0], word[1], word[2], word[3]);
+  }
+  if (tid == 0) scales[nb * KB + kb] = scale;
+}
+
+inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps); }
+
+}  // namespace
+
+void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
+                         const int32_t* sorted_pairs, int P, int with_shared, uint8_t* xq,
+                         float* sx, cudaStream_t s) {
+  const int rows = P + (with_shared ? T : 0);
+  if (rows <= 0) return;
+  quant_gather_kernel<<<row_blocks(rows), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                       x_stride, T, H, k, sorted_pairs, P, rows,
+                                                       xq, sx);
+}
+
+void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
+                           cudaStream_t s) {
+  if (T <= 0) return;
+  dense_act_prep_kernel<<<row_blocks(T), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                      x_stride, T, K, xh, inv);
+}
+
+void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,
+                         int T, int k, int with_shared, const void* gate, int64_t gate_stride,
+                         void* routed_out, void* shared_out, void* out, cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(T) * (H / 4);
+  if (n <= 0) return;
+  combine_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+      d, H, inv_rows, static_cast<const __nv_bfloat16*>(weights), T, k, with_shared,
+      static_cast<const __nv_bfloat16*>(gate), gate_stride,
+      static_cast<__nv_bfloat16*>(routed_out), static_cast<__nv_bfloat16*>(shared_out),
+      static_cast<__nv_bfloat16*>(out));
+}
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" int d3_quant_act_fp8(const void* x, int64_t x_stride, int T, int H, uint8_t* q,
+                                float* scales, int scales_transposed, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && H > 0 && H % 128 == 0, "quant_act_fp8: H=%d must be a positive multiple of 128", H);
+  D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "quant_act_fp8: x row stride %lld must be >= H and a multiple of 8", (long long)x_stride);
+  D3_REQUIRE(aligned(x, 16) && aligned(q, 16) && aligned(scales, 4), "quant_act_fp8: misaligned pointer");
+  if (T == 0) return D3_OK;
+  quant_act_kernel<<<row_blocks(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_stride, T, H, q, scales, scales_transposed);
+  return check_launch("quant_act_fp8");
+}
+
+extern "C" int d3_prepare_moe_input(const void* x, int64_t x_stride, const void* router,
+                                    int64_t router_stride, int T, int H, int E,
+                                    const void* row_slots, int row_slots_int64,
+                                    int64_t padding_start, uint8_t* q, float* scales_t,
+                                    float* logits, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && H > 0 && H % 128 == 0 && E > 0, "prepare_moe_input: bad shape T=%d H=%d E=%d", T, H, E);
+  D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "prepare_moe_input: x row stride must be >= H and a multiple of 8");
+  D3_REQUIRE(router_stride >= E, "prepare_moe_input: router row stride must be >= E");
+  D3_REQUIRE((row_slots == nullptr) == (padding_start <= 0), "prepare_moe_input: reserved padding routing needs both row_slots and padding_start > 0");
+  D3_REQUIRE(aligned(x, 16) && aligned(q, 16), "prepare_moe_input: misaligned pointer");
+  if (T == 0) return D3_OK;
+  prepare_kernel<<<row_blocks(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(router),
+      router_stride, T, H, E, row_slots, row_slots_int64, padding_start, q, scales_t, logits);
+  return check_launch("prepare_moe_input");
+}
+
+extern "C" int d3_silu_mul(const void* in, int64_t in_stride, int rows, int W, void* out,
+                           d3_stream_t stream) {
+  D3_REQUIRE(rows >= 0 && W > 0 && W % 8 == 0, "silu_mul: width %d must be a positive multiple of 8", W);
+  D3_REQUIRE(in_stride >= 2 * W && in_stride % 8 == 0, "silu_mul: input row stride must be >= 2W and a multiple of 8");
+  D3_REQUIRE(aligned(in, 16) && aligned(out, 16), "silu_mul: misaligned pointer");
+  const int64_t n = static_cast<int64_t>(rows) * (W / 8);
+  if (n == 0) return D3_OK;
+  silu_mul_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                    reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(in), in_stride, rows, W, static_cast<__nv_bfloat16*>(out));
+  return check_launch("silu_mul");
+}
+
+extern "C" int d3_silu_mul_quant(const void* in, int64_t in_stride, int rows, int W, uint8_t* q,
+                                 float* scales, d3_stream_t stream) {
+  D3_REQUIRE(rows >= 0 && W > 0 && W % 128 == 0, "silu_mul_quant: width %d must be a positive multiple of 128", W);
+  D3_REQUIRE(in_stride >= 2 * W && in_stride % 8 == 0, "silu_mul_quant: input row stride must be >= 2W and a multiple of 8");
+  D3_REQUIRE(aligned(in, 16) && aligned(q, 16), "silu_mul_quant: misaligned pointer");
+  if (rows == 0) return D3_OK;
+  silu_mul_quant_kernel<<<row_blocks(rows), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(in), in_stride, rows, W, q, scales);
+  return check_launch("silu_mul_quant");
+}
+
+extern "C" int d3_combine_experts(const void* routed, const void* shared, const void* gate,
+                                  int64_t gate_stride, int T, int H, void* out,
+                                  d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "combine_experts: H=%d must be a positive multiple of 8", H);
+  D3_REQUIRE(aligned(routed, 16) && aligned(shared, 16) && aligned(out, 16), "combine_experts: misaligned pointer");
+  const int64_t n = static_cast<int64_t>(T) * (H / 8);
+  if (n == 0) return D3_OK;
+  combine_experts_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                           reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(routed), static_cast<const __nv_bfloat16*>(shared),
+      static_cast<const __nv_bfloat16*>(gate), gate_stride, T, H,
+      static_cast<__nv_bfloat16*>(out));
+  return check_launch("combine_experts");
+}
+
+extern "C" int d3_fp8_quantize_weight(const void* w, int N, int K, uint8_t* q, float* scales,
+                                      d3_stream_t stream) {
+  D3_REQUIRE(N > 0 && K > 0 && K % 128 == 0, "fp8_quantize_weight: K=%d must be a positive multiple of 128", K);
+  D3_REQUIRE(aligned(w, 16) && aligned(q, 16), "fp8_quantize_weight: misaligned pointer");
+  dim3 grid((N + 127) / 128, K / 128);
+  weight_quant_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(w), N, K, q, scales);
+  return check_launch("fp8_quantize_weight");
+}

@@ -1,0 +1,363 @@
+// C ABI of the expert pipeline: d3_moe_experts, d3_moe_layer, d3_fp8_gemv.
+//
+// Pipeline for T tokens, top-k, E experts (P = T*k pairs, R = P + T rows when
+// a shared expert runs):
+//   1. permute      ids -> counts, starts, sorted pairs, inverse rows, active list
+//   2. quant_gather x -> e4m3 rows in expert order (+ T shared rows), scales
+//   3. gate_up      engine EPI_GATE_UP: a e4m3 [R, I], sa [R, I/128]
+//   4. down         engine EPI_DOWN:    d f32 [R, H]
+//   5. combine      routed/shared/out bf16 [T, H] in fixed rank order
+// All buffers live in the caller's workspace; nothing is allocated here.
+#include "d3_host.h"
+#include "d3_internal.h"
+#include "expert_gemv.cuh"
+
+namespace d3 {
+
+namespace {
+
+thread_local void* const* g_stage_events = nullptr;
+
+inline void stage_mark(int i, cudaStream_t s) {
+  if (g_stage_events) cudaEventRecord(static_cast<cudaEvent_t>(g_stage_events[i]), s);
+}
+
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  template <typename T>
+  T* take(size_t count) {
+    off = align_up(off, 256);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+struct MoeBuffers {
+  int32_t* status;
+  int32_t* counts;
+  int32_t* starts;
+  int32_t* total;
+  int32_t* active;
+  int32_t* n_active;
+  int32_t* sorted;
+  int32_t* tile_experts;
+  int32_t* inv;
+  uint8_t* xq;
+  float* sx;
+  uint8_t* a;
+  float* sa;
+  float* d;
+  __nv_bfloat16* logits;  // layer only: [T, E+1]
+  int64_t* ids;           // layer only
+  __nv_bfloat16* weights; // layer only
+  size_t bytes;
+};
+
+MoeBuffers carve_moe(void* ws, int T, int k, int E, int I, int H, int has_shared, int layer) {
+  Carve c{static_cast<uint8_t*>(ws)};
+  const int64_t P = static_cast<int64_t>(T) * k;
+  const int64_t R = P + (has_shared ? T : 0);
+  MoeBuffers b;
+  b.status = c.take<int32_t>(4);
+  b.counts = c.take<int32_t>(E);
+  b.starts = c.take<int32_t>(E);
+  b.total = c.take<int32_t>(1);
+  b.active = c.take<int32_t>(E);
+  b.n_active = c.take<int32_t>(1);
+  b.sorted = c.take<int32_t>(P > 0 ? P : 1);
+  b.tile_experts = c.take<int32_t>(P > 0 ? P : 1);
+  b.inv = c.take<int32_t>(P > 0 ? P : 1);
+  b.xq = c.take<uint8_t>(R * H);
+  b.sx = c.take<float>(R * (H / 128));
+  b.a = c.take<uint8_t>(R * I);
+  b.sa = c.take<float>(R * (I / 128));
+  b.d = c.take<float>(R * H);
+  if (layer) {
+    b.logits = c.take<__nv_bfloat16>(static_cast<size_t>(T) * (E + 1));
+    b.ids = c.take<int64_t>(P);
+    b.weights = c.take<__nv_bfloat16>(P);
+  } else {
+    b.logits = nullptr;
+    b.ids = nullptr;
+    b.weights = nullptr;
+  }
+  b.bytes = c.off + 256;
+  return b;
+}
+
+int nch_for(int max_tokens) {
+  const int m = max_tokens < kTokensPerGroup ? max_tokens : kTokensPerGroup;
+  if (m <= 8) return 1;
+  if (m <= 16) return 2;
+  if (m <= 32) return 4;
+  return 8;
+}
+
+template <int EPI, bool ACT_F16, int NCH, int STAGES>
+int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& ta,
+                       const EngineArgs& args, int grid, cudaStream_t s) {
+  auto kern = expert_gemv_kernel<EPI, ACT_F16, NCH, STAGES>;
+  const size_t smem = EngineSmem<EPI, ACT_F16, STAGES>::bytes(args.KB);
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || configured[dev] < static_cast<int>(smem)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return set_error(D3_ECUDA, "engine: cannot reserve %zu bytes of shared memory", smem);
+    if (dev >= 0 && dev < 64) configured[dev] = static_cast<int>(smem);
+  }
+  kern<<<grid, kEngineThreads, smem, s>>>(tw, twsh, ta, args);
+  return check_launch("expert engine");
+}
+
+template <int EPI, bool ACT_F16, int STAGES>
+int launch_engine(int nch, const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& ta,
+                  const EngineArgs& args, int grid, cudaStream_t s) {
+  switch (nch) {
+    case 1: return launch_engine_inst<EPI, ACT_F16, 1, STAGES>(tw, twsh, ta, args, grid, s);
+    case 2: return launch_engine_inst<EPI, ACT_F16, 2, STAGES>(tw, twsh, ta, args, grid, s);
+    case 4: return launch_engine_inst<EPI, ACT_F16, 4, STAGES>(tw, twsh, ta, args, grid, s);
+    default: return launch_engine_inst<EPI, ACT_F16, 8, STAGES>(tw, twsh, ta, args, grid, s);
+  }
+}
+
+constexpr int kStagesGateUp = 4;
+constexpr int kStagesDown = 6;
+constexpr int kStagesDense = 5;
+
+int check_experts(const d3_experts_t* e, const char* what) {
+  D3_REQUIRE(e != nullptr, "%s: expert weights missing", what);
+  D3_REQUIRE(e->w13 && e->s13 && e->w2 && e->s2, "%s: null weight pointer", what);
+  D3_REQUIRE(e->E > 0 && e->I > 0 && e->H > 0, "%s: bad expert shape", what);
+  D3_REQUIRE(e->I % 128 == 0 && e->H % 128 == 0, "%s: H=%d and I=%d must be multiples of 128", what, e->H, e->I);
+  D3_REQUIRE(aligned(e->w13, 16) && aligned(e->w2, 16), "%s: weights must be 16-byte aligned", what);
+  return D3_OK;
+}
+
+// Steps 1-5 on an already carved workspace. ids/weights are device tensors
+// [T,k]; gate (nullable) feeds the shared-expert combine.
+int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
+                int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
+                int64_t gate_stride, void* routed_out, void* shared_out, void* out,
+                const MoeBuffers& b, int32_t* status, cudaStream_t s) {
+  const int E = ex->E, I = ex->I, H = ex->H;
+  const int P = T * k;
+  const int has_shared = sh ? 1 : 0;
+  const int R = P + (has_shared ? T : 0);
+  int rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, b.sorted, b.tile_experts,
+                          P, b.inv, b.active, b.n_active, s);
+  if (rc) return rc;
+  launch_quant_gather(x, x_stride, T, H, k, b.sorted, P, has_shared, b.xq, b.sx, s);
+  if ((rc = check_launch("quant_gather"))) return rc;
+
+  const int sms = sm_count();
+  stage_mark(1, s);
+  // ---- gate_up
+  {
+    CUtensorMap tw, twsh, ta;
+    if ((rc = encode_tmap_2d(&tw, ex->w13, 1, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128))) return rc;
+    if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w13 : ex->w13, 1, H,
+                             static_cast<uint64_t>(2) * I, H, 128, 128))) return rc;
+    if ((rc = encode_tmap_2d(&ta, b.xq, 1, H, R, H, 128, 16))) return rc;
+    EngineArgs a{};
+    a.counts = b.counts;
+    a.starts = b.starts;
+    a.active = b.active;
+    a.n_active = b.n_active;
+    a.has_shared = has_shared;
+    a.shared_row0 = P;
+    a.shared_count = T;
+    a.tiles = I / 128;
+    a.KB = H / 128;
+    a.rows_per_expert = 2 * I;
+    a.up_offset = I;
+    a.wscale = ex->s13;
+    a.wscale_sh = has_shared ? sh->s13 : ex->s13;
+    a.act_scale = b.sx;
+    a.out_q = b.a;
+    a.out_qs = b.sa;
+    a.out_cols = I;
+    a.status = status;
+    const int max_items = (E + has_shared) * (I / 128);
+    const int grid = max_items < sms ? max_items : sms;
+    rc = launch_engine<EPI_GATE_UP, false, kStagesGateUp>(nch_for(T), tw, twsh, ta, a, grid, s);
+    if (rc) return rc;
+  }
+  stage_mark(2, s);
+  // ---- down
+  {
+    CUtensorMap tw, twsh, ta;
+    if ((rc = encode_tmap_2d(&tw, ex->w2, 1, I, static_cast<uint64_t>(E) * H, I, 128, 128))) return rc;
+    if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w2 : ex->w2, 1, I, H, I, 128, 128))) return rc;
+    if ((rc = encode_tmap_2d(&ta, b.a, 1, I, R, I, 128, 16))) return rc;
+    EngineArgs a{};
+    a.counts = b.counts;
+    a.starts = b.starts;
+    a.active = b.active;
+    a.n_active = b.n_active;
+    a.has_shared = has_shared;
+    a.shared_row0 = P;
+    a.shared_count = T;
+    a.tiles = H / 128;
+    a.KB = I / 128;
+    a.rows_per_expert = H;
+    a.up_offset = 0;
+    a.wscale = ex->s2;
+    a.wscale_sh = has_shared ? sh->s2 : ex->s2;
+    a.act_scale = b.sa;
+    a.out_rows = b.d;
+    a.out_ld = H;
+    a.status = status;
+    const int max_items = (E + has_shared) * (H / 128);
+    const int grid = max_items < sms ? max_items : sms;
+    rc = launch_engine<EPI_DOWN, false, kStagesDown>(nch_for(T), tw, twsh, ta, a, grid, s);
+    if (rc) return rc;
+  }
+  stage_mark(3, s);
+  launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
+                      shared_out, out, s);
+  rc = check_launch("combine_rows");
+  stage_mark(4, s);
+  return rc;
+}
+
+}  // namespace
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" int d3_set_stage_events(void* const* events, int n) {
+  D3_REQUIRE(events == nullptr || n >= 5, "set_stage_events: need at least 5 events");
+  g_stage_events = events;
+  return D3_OK;
+}
+
+extern "C" int d3_moe_workspace_size(int T, int k, int E, int I, int H, int has_shared,
+                                     size_t* bytes) {
+  D3_REQUIRE(bytes != nullptr, "moe_workspace_size: null output");
+  D3_REQUIRE(T >= 0 && k > 0 && E > 0 && I > 0 && H > 0, "moe_workspace_size: bad shape");
+  *bytes = carve_moe(nullptr, T, k, E, I, H, has_shared, 1).bytes;
+  return D3_OK;
+}
+
+static int check_common(const void* x, int64_t x_stride, int T, int k, const d3_experts_t* ex,
+                        const d3_experts_t* sh, void* ws, size_t ws_bytes, const char* what) {
+  int rc = check_experts(ex, what);
+  if (rc) return rc;
+  if (sh) {
+    if ((rc = check_experts(sh, what))) return rc;
+    D3_REQUIRE(sh->E == 1 && sh->I == ex->I && sh->H == ex->H,
+               "%s: the shared expert must have E=1 and the routed I/H", what);
+  }
+  D3_REQUIRE(T >= 0 && k > 0 && k <= 32 && k <= ex->E, "%s: bad top-k %d", what, k);
+  D3_REQUIRE(ex->E <= 1024, "%s: E=%d above 1024", what, ex->E);
+  D3_REQUIRE(static_cast<int64_t>(T) * k < (1 << 24), "%s: too many pairs", what);
+  D3_REQUIRE(x_stride >= ex->H && x_stride % 8 == 0, "%s: x row stride must be >= H and a multiple of 8", what);
+  D3_REQUIRE(aligned(x, 16), "%s: x must be 16-byte aligned", what);
+  D3_REQUIRE(ws != nullptr && aligned(ws, 256), "%s: workspace must be 256-byte aligned", what);
+  size_t need = carve_moe(nullptr, T, k, ex->E, ex->I, ex->H, sh != nullptr, 1).bytes;
+  if (ws_bytes < need)
+    return set_error(D3_EWORKSPACE, "%s: workspace %zu bytes < %zu", what, ws_bytes, need);
+  return D3_OK;
+}
+
+extern "C" int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* ids,
+                              const void* weights, int T, int k, const d3_experts_t* experts,
+                              const d3_experts_t* shared, void* routed_out, void* shared_out,
+                              void* workspace, size_t workspace_bytes, int32_t* status,
+                              d3_stream_t stream) {
+  int rc = check_common(x, x_stride, T, k, experts, shared, workspace, workspace_bytes,
+                        "moe_experts");
+  if (rc) return rc;
+  D3_REQUIRE(ids && weights && routed_out, "moe_experts: null ids, weights or output");
+  D3_REQUIRE(aligned(routed_out, 16) && (!shared_out || aligned(shared_out, 16)), "moe_experts: outputs must be 16-byte aligned");
+  if (T == 0) return D3_OK;
+  auto b = carve_moe(workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr, 1);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  stage_mark(0, s);
+  return run_experts(x, x_stride, ids, weights, T, k, experts, shared, nullptr, 0, routed_out,
+                     shared_out, nullptr, b, status ? status : b.status, s);
+}
+
+extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w,
+                            const float* router_bias, int T, int k, const d3_experts_t* experts,
+                            const d3_experts_t* shared, void* out, int64_t* ids_out,
+                            void* weights_out, void* workspace, size_t workspace_bytes,
+                            int32_t* status, d3_stream_t stream) {
+  int rc = check_common(x, x_stride, T, k, experts, shared, workspace, workspace_bytes,
+                        "moe_layer");
+  if (rc) return rc;
+  D3_REQUIRE(shared != nullptr, "moe_layer: the layer needs its shared expert");
+  D3_REQUIRE(router_w && out && aligned(router_w, 16) && aligned(out, 16), "moe_layer: null or misaligned router weight / output");
+  D3_REQUIRE(experts->H <= 3072, "moe_layer: H=%d above the 3072 the router kernel stages", experts->H);
+  if (T == 0) return D3_OK;
+  const int E = experts->E, H = experts->H;
+  auto b = carve_moe(workspace, T, k, E, experts->I, H, 1, 1);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int64_t* ids = ids_out ? ids_out : b.ids;
+  void* wts = weights_out ? weights_out : static_cast<void*>(b.weights);
+  stage_mark(0, s);
+  launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s);
+  if ((rc = check_launch("router_logits"))) return rc;
+  launch_route_topk(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts, D3_DTYPE_BF16, s);
+  if ((rc = check_launch("route_topk"))) return rc;
+  return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
+                     nullptr, out, b, status ? status : b.status, s);
+}
+
+extern "C" int d3_fp8_gemv_workspace_size(int T, int K, size_t* bytes) {
+  D3_REQUIRE(bytes != nullptr && T >= 0 && K > 0 && K % 128 == 0, "fp8_gemv_workspace_size: bad arguments");
+  Carve c{nullptr};
+  c.take<int32_t>(4);
+  c.take<__half>(static_cast<size_t>(T) * K);
+  c.take<float>(static_cast<size_t>(T) * (K / 128));
+  *bytes = c.off + 256;
+  return D3_OK;
+}
+
+extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const float* s,
+                           int T, int N, int K, void* y, int64_t y_stride, void* workspace,
+                           size_t workspace_bytes, int32_t* status, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && N > 0 && K > 0 && K % 128 == 0, "fp8_gemv: bad shape T=%d N=%d K=%d", T, N, K);
+  D3_REQUIRE(x_stride >= K && x_stride % 8 == 0, "fp8_gemv: x row stride must be >= K and a multiple of 8");
+  D3_REQUIRE(y_stride >= N, "fp8_gemv: y row stride must be >= N");
+  D3_REQUIRE(x && wq && s && y && aligned(x, 16) && aligned(wq, 16), "fp8_gemv: null or misaligned pointer");
+  D3_REQUIRE(workspace && aligned(workspace, 256), "fp8_gemv: workspace must be 256-byte aligned");
+  size_t need = 0;
+  d3_fp8_gemv_workspace_size(T, K, &need);
+  if (workspace_bytes < need)
+    return set_error(D3_EWORKSPACE, "fp8_gemv: workspace %zu bytes < %zu", workspace_bytes, need);
+  if (T == 0) return D3_OK;
+  Carve c{static_cast<uint8_t*>(workspace)};
+  int32_t* own_status = c.take<int32_t>(4);
+  __half* xh = c.take<__half>(static_cast<size_t>(T) * K);
+  float* inv = c.take<float>(static_cast<size_t>(T) * (K / 128));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  launch_dense_act_prep(x, x_stride, T, K, xh, inv, st);
+  int rc = check_launch("dense_act_prep");
+  if (rc) return rc;
+  CUtensorMap tw, ta;
+  if ((rc = encode_tmap_2d(&tw, wq, 1, K, N, K, 128, 128))) return rc;
+  if ((rc = encode_tmap_2d(&ta, xh, 2, K, T, static_cast<uint64_t>(K) * 2, 64, 16))) return rc;
+  EngineArgs a{};
+  a.num_groups = 1;
+  a.dense_count = T;
+  a.tiles = (N + 127) / 128;
+  a.KB = K / 128;
+  a.rows_per_expert = 0;
+  a.wscale = s;
+  a.wscale_sh = s;
+  a.act_scale = inv;
+  a.out_bf16 = static_cast<__nv_bfloat16*>(y);
+  a.out_ld = static_cast<int>(y_stride);
+  a.out_cols = N;
+  a.status = status ? status : own_status;
+  const int tiles = a.tiles;
+  const int sms = sm_count();
+  const int grid = tiles < sms ? tiles : sms;
+  return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
+}

@@ -1,0 +1,369 @@
+// Routing kernels: the bf16 router projection, softmax/top-k/renormalise and
+// the token->expert bucketing (stable counting sort).
+#include "d3_common.cuh"
+#include "d3_host.h"
+#include "d3_internal.h"
+
+namespace d3 {
+
+namespace {
+
+// ------------------------------------------------------- router projection --
+// logits[t, r] = bf16( sum_k x[t,k] * w[r,k] (+ bias[r]) ).
+// Summation order (fixed, restated by the CPU oracle): lane l of a warp owns
+// k = 256*i + 8*l + j (i ascending, then j = 0..7) and accumulates sequentially
+// in fp32; the 32 lane partials are combined by an xor-butterfly with offsets
+// 16, 8, 4, 2, 1. bf16*bf16 products are exact in fp32, so FMA and
+// multiply-then-add give the same result and the order alone defines the sum.
+// CTA: 8 warps = 8 router rows (one per warp) x 8 tokens staged in smem.
+constexpr int kRouterRows = 8, kRouterTokens = 8;
+
+__global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                                     const __nv_bfloat16* __restrict__ w,
+                                     const float* __restrict__ bias, int nbias, int R, int H, int T,
+                                     __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
+  const int t0 = blockIdx.y * kRouterTokens;
+  const int nt = min(kRouterTokens, T - t0);
+  const int chunks = H / 8;  // 16-byte chunks per row
+  for (int i = threadIdx.x; i < nt * chunks; i += blockDim.x) {
+    const int t = i / chunks, c = i % chunks;
+    reinterpret_cast<uint4*>(xs + t * H)[c] =
+        *reinterpret_cast<const uint4*>(x + (t0 + t) * x_stride + c * 8);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kRouterRows + warp;
+  if (r >= R) return;
+  const __nv_bfloat16* wr = w + static_cast<int64_t>(r) * H;
+  const int iters = (H + 255) / 256;
+  const float b = (bias && r < nbias) ? bias[r] : 0.f;
+  for (int t = 0; t < nt; ++t) {
+    float acc = 0.f;
+    for (int i = 0; i < iters; ++i) {
+      const int k0 = 256 * i + 8 * lane;
+      if (k0 < H) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wr + k0);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + k0);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc = fmaf(__uint_as_float(ww[j] << 16), __uint_as_float(xx[j] << 16), acc);
+          acc = fmaf(__uint_as_float(ww[j] & 0xffff0000u), __uint_as_float(xx[j] & 0xffff0000u),
+                     acc);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[(t0 + t) * out_stride + r] = __float2bfloat16_rn(acc + b);
+  }
+}
+
+// ------------------------------------------------------------------ route --
+// One warp per token. Keys order logits like the reference's packed keys
+// (src/drama3/kernels.py:365-369): the sign-flipped fp32 bit pattern in the
+// high word (larger logit first) and the inverted column in the low word
+// (lower expert id first on ties). For bf16 logits this is the same order as
+// the reference's 32-bit key; for fp32 logits it keeps the full precision.
+constexpr int kMaxPerLane = 32;  // E <= 1024
+
+__device__ __forceinline__ uint64_t route_key(float v, int col) {
+  const uint32_t bits = __float_as_uint(v);
+  const uint32_t ordered = bits ^ ((bits & 0x80000000u) ? 0xffffffffu : 0x80000000u);
+  return (static_cast<uint64_t>(ordered) << 32) | static_cast<uint32_t>(0xffffffffu - col);
+}
+
+template <int PER_LANE>
+__global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T,
+                             int E, int k, const float* __restrict__ bias,
+                             int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  float v[PER_LANE];
+  uint64_t key[PER_LANE];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int c = lane + 32 * i;
+    if (c < E) {
+      float l = f32_in ? static_cast<const float*>(logits)[t * stride + c]
+                       : __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[t * stride + c]);
+      if (bias) l += bias[c];
+      v[i] = l;
+      key[i] = route_key(l, c);
+      mx = fmaxf(mx, l);
+    } else {
+      v[i] = -INFINITY;
+      key[i] = 0;
+    }
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i)
+    if (lane + 32 * i < E) sum += expf(v[i] - mx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+
+  int sel_col = 0;
+  float sel_val = 0.f;  // lane j (< k) keeps pick j
+  for (int j = 0; j < k; ++j) {
+    uint64_t best = 0;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) best = key[i] > best ? key[i] : best;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    const int col = static_cast<int>(0xffffffffu - static_cast<uint32_t>(best & 0xffffffffu));
+    float val = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      if (key[i] == best) {
+        val = v[i];
+        key[i] = 0;
+      }
+    }
+    // owner lane of col holds the value; broadcast it
+    val = __shfl_sync(0xffffffffu, val, col & 31);
+    if (lane == j) {
+      sel_col = col;
+      sel_val = val;
+    }
+  }
+  const float p = (lane < k) ? expf(sel_val - mx) / sum : 0.f;
+  // renormalise over the k picks in pick order
+  float psum = 0.f;
+  for (int j = 0; j < k; ++j) psum += __shfl_sync(0xffffffffu, p, j);
+  if (lane < k) {
+    ids[static_cast<int64_t>(t) * k + lane] = sel_col;
+    const float wgt = p / psum;
+    if (f32_out)
+      static_cast<float*>(weights)[static_cast<int64_t>(t) * k + lane] = wgt;
+    else
+      static_cast<__nv_bfloat16*>(weights)[static_cast<int64_t>(t) * k + lane] =
+          __float2bfloat16_rn(wgt);
+  }
+}
+
+// ---------------------------------------------------------------- permute --
+// Single CTA of 1024 threads. Histogram with shared atomics (order-free), a
+// block scan of padded counts, then pairs are placed chunk by chunk (1024 pairs
+// per chunk, ascending) with ranks from __match_any_sync inside a warp plus the
+// counts of lower warps, so each expert's list is in ascending pair order
+// (a stable counting sort, like src/drama3/kernels.py:674-699).
+constexpr int kPermuteThreads = 1024;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int wv = warp_tot[lane];
+    int wi = wv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    warp_tot[lane] = wi - wv;  // exclusive prefix of warps
+    if (lane == 31) warp_tot[32] = wi;
+  }
+  __syncthreads();
+  const int excl = warp_tot[warp] + incl - v;
+  total = warp_tot[32];
+  __syncthreads();
+  return excl;
+}
+
+__global__ void __launch_bounds__(kPermuteThreads)
+    permute_kernel(const int64_t* __restrict__ ids, int P, int E, int bm,
+                   int32_t* __restrict__ counts, int32_t* __restrict__ starts,
+                   int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
+                   int32_t* __restrict__ expert_ids, int64_t max_rows,
+                   int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
+                   int32_t* __restrict__ n_active) {
+  extern __shared__ int sm[];
+  int* cnt = sm;              // [E]
+  int* start = cnt + E;       // [E]
+  int* cursor = start + E;    // [E]
+  int* wcnt = cursor + E;     // [32][E]
+  __shared__ int warp_tot[33];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += kPermuteThreads) cnt[e] = cursor[e] = 0;
+  for (int i = tid; i < 32 * E; i += kPermuteThreads) wcnt[i] = 0;
+  __syncthreads();
+  for (int p = tid; p < P; p += kPermuteThreads) {
+    const int64_t e = ids[p];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  int total = 0;
+  {
+    const int e = tid;
+    const int c = e < E ? cnt[e] : 0;
+    const int padded = (c + bm - 1) / bm * bm;
+    const int excl = block_exclusive_scan(e < E ? padded : 0, warp_tot, total);
+    if (e < E) start[e] = excl;
+  }
+  __syncthreads();
+  for (int base = 0; base < P; base += kPermuteThreads) {
+    const int p = base + tid;
+    int e = -1;
+    if (p < P) {
+      const int64_t v = ids[p];
+      e = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const bool leader = rank == 0;
+    if (e >= 0 && leader) wcnt[warp * E + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int pre = 0;
+      for (int w2 = 0; w2 < warp; ++w2) pre += wcnt[w2 * E + e];
+      const int pos = start[e] + cursor[e] + pre + rank;
+      sorted_ids[pos] = p;
+      if (inv_rows) inv_rows[p] = pos;
+    } else if (p < P && inv_rows) {
+      inv_rows[p] = -1;
+    }
+    __syncthreads();
+    if (e >= 0 && leader) {
+      atomicAdd(&cursor[e], __popc(peers));
+      wcnt[warp * E + e] = 0;
+    }
+    __syncthreads();
+  }
+  // padding slots of each expert, per-tile expert ids
+  for (int e = warp; e < E; e += kPermuteThreads / 32) {
+    const int c = cnt[e], s = start[e];
+    const int padded = (c + bm - 1) / bm * bm;
+    for (int i = c + lane; i < padded; i += 32) sorted_ids[s + i] = P;
+    for (int b = lane; b * bm < padded; b += 32) expert_ids[s / bm + b] = e;
+    if (lane == 0) {
+      counts[e] = c;
+      starts[e] = s;
+    }
+  }
+  for (int64_t r = total + tid; r < max_rows; r += kPermuteThreads) sorted_ids[r] = P;
+  for (int64_t b = total / bm + tid; b < max_rows / bm; b += kPermuteThreads) expert_ids[b] = -1;
+  if (tid == 0) total_out[0] = total;
+  if (active) {
+    int n = 0;
+    const int e = tid;
+    const int flag = (e < E && cnt[e] > 0) ? 1 : 0;
+    const int pos = block_exclusive_scan(flag, warp_tot, n);
+    if (flag) active[pos] = e;
+    if (tid == 0 && n_active) n_active[0] = n;
+  }
+}
+
+}  // namespace
+
+void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
+                          int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
+                          cudaStream_t s) {
+  if (T <= 0 || R <= 0) return;
+  dim3 grid((R + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
+  const size_t smem = static_cast<size_t>(kRouterTokens) * H * 2;
+  router_logits_kernel<<<grid, 256, smem, s>>>(
+      static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
+      nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
+}
+
+void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
+                       const float* bias, int64_t* ids, void* weights, int weights_dtype,
+                       cudaStream_t s) {
+  if (T <= 0) return;
+  const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  const int f32_in = logits_dtype == D3_DTYPE_F32, f32_out = weights_dtype == D3_DTYPE_F32;
+  const int per_lane = (E + 31) / 32;
+  if (per_lane <= 4)
+    route_kernel<4><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+  else if (per_lane <= 8)
+    route_kernel<8><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+  else
+    route_kernel<kMaxPerLane><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+}
+
+int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
+                   int32_t* starts, int32_t* total, int32_t* sorted_ids, int32_t* expert_ids,
+                   int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,
+                   cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(E) * 35 * sizeof(int);
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             35 * 1024 * 4) != cudaSuccess)
+      return set_error(D3_ECUDA, "permute: cannot raise the shared-memory limit");
+    configured[dev] = true;
+  }
+  permute_kernel<<<1, kPermuteThreads, smem, s>>>(ids, T * k, E, block_m, counts, starts, total,
+                                                   sorted_ids, expert_ids, max_rows, inv_rows,
+                                                   active, n_active);
+  return check_launch("moe_permute");
+}
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H,
+                                int T, void* logits, int64_t logits_stride, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && R > 0 && H > 0 && H % 128 == 0, "router_logits: bad shape R=%d H=%d", R, H);
+  D3_REQUIRE(H <= 16384, "router_logits: H=%d above the 16384 this kernel stages in shared memory", H);
+  D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "router_logits: x row stride must be >= H and a multiple of 8");
+  D3_REQUIRE(logits_stride >= R, "router_logits: logits row stride must be >= R");
+  D3_REQUIRE(aligned(x, 16) && aligned(w, 16), "router_logits: misaligned pointer");
+  if (H * 16 > 48 * 1024) {
+    if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             H * 16) != cudaSuccess)
+      return set_error(D3_ECUDA, "router_logits: cannot raise the shared-memory limit");
+  }
+  launch_router_logits(x, x_stride, w, nullptr, 0, R, H, T, logits, logits_stride,
+                       reinterpret_cast<cudaStream_t>(stream));
+  return check_launch("router_logits");
+}
+
+extern "C" int d3_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E,
+                             int k, const float* bias, int64_t* ids, void* weights,
+                             int weights_dtype, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && E > 0 && E <= 1024, "route_topk: E=%d must be in [1, 1024]", E);
+  D3_REQUIRE(k > 0 && k <= 32 && k <= E, "route_topk: k=%d must be in [1, min(32, E)]", k);
+  D3_REQUIRE(stride >= E, "route_topk: logits row stride must be >= E");
+  D3_REQUIRE(logits_dtype == D3_DTYPE_BF16 || logits_dtype == D3_DTYPE_F32, "route_topk: logits must be bf16 or f32");
+  D3_REQUIRE(weights_dtype == D3_DTYPE_BF16 || weights_dtype == D3_DTYPE_F32, "route_topk: weights must be bf16 or f32");
+  launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype,
+                    reinterpret_cast<cudaStream_t>(stream));
+  return check_launch("route_topk");
+}
+
+extern "C" int d3_moe_permute(const int64_t* ids, int T, int k, int E, int block_m,
+                              int32_t* counts, int32_t* starts, int32_t* total,
+                              int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
+                              int32_t* inv_rows, int32_t* active, int32_t* n_active,
+                              d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && E > 0 && E <= 1024, "moe_permute: E=%d must be in [1, 1024]", E);
+  D3_REQUIRE(block_m > 0, "moe_permute: block_m must be positive");
+  const int64_t P = static_cast<int64_t>(T) * k;
+  D3_REQUIRE(P < (1ll << 30), "moe_permute: too many pairs");
+  const int64_t need = (P + (P < E ? P : E) * (block_m - 1) + block_m - 1) / block_m * block_m;
+  D3_REQUIRE(max_rows >= need, "moe_permute: max_rows %lld < required %lld", (long long)max_rows, (long long)need);
+  D3_REQUIRE(max_rows % block_m == 0, "moe_permute: max_rows must be a multiple of block_m");
+  return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
+                        max_rows, inv_rows, active, n_active, reinterpret_cast<cudaStream_t>(stream));
+}

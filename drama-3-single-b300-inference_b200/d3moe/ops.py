@@ -1,0 +1,274 @@
+"""Tensor-level wrappers over the C ABI (include/d3moe.h).
+
+Each wrapper validates dtypes/devices the way the reference's operators do,
+allocates its outputs (and workspace) with torch.empty on the input's device
+-- the graph pool during CUDA-graph capture -- and enqueues the kernels on the
+current torch stream. Nothing here synchronises, so every call can be
+captured in a CUDA graph like the reference's decode step
+(src/drama3/engine.py:84-92).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import D3Experts, call
+
+FP8 = torch.float8_e4m3fn
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("d3moe operators take CUDA tensors; there is no CPU path")
+
+
+def _row_stride(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("Channel strides must be contiguous")
+    return t.stride(0)
+
+
+class ExpertView:
+    """Read-only view of an expert container as a d3_experts_t.
+
+    `experts` is any object exposing w13_weight [E,2I,H] e4m3, w13_scale_inv
+    [E,2I/128,H/128] f32, w2_weight [E,H,I] e4m3 and w2_scale_inv
+    [E,H/128,I/128] f32 (the reference's container, src/drama3/kernels.py:
+    336-350)."""
+
+    def __init__(self, experts):
+        w13, s13 = experts.w13_weight, experts.w13_scale_inv
+        w2, s2 = experts.w2_weight, experts.w2_scale_inv
+        if w13.dim() == 2:  # a single (shared) expert stored without the E axis
+            w13, s13, w2, s2 = w13[None], s13[None], w2[None], s2[None]
+        E, I2, H = w13.shape
+        I = I2 // 2
+        if w13.dtype != FP8 or w2.dtype != FP8:
+            raise ValueError("expert weights must be float8_e4m3fn")
+        if s13.dtype != torch.float32 or s2.dtype != torch.float32:
+            raise ValueError("expert scales must be float32")
+        if tuple(w2.shape) != (E, H, I):
+            raise ValueError(f"w2_weight shape {tuple(w2.shape)} != {(E, H, I)}")
+        if tuple(s13.shape) != (E, I2 // 128, H // 128) or tuple(s2.shape) != (E, H // 128, I // 128):
+            raise ValueError("scale shapes must be [E, rows/128, cols/128]")
+        for t in (w13, s13, w2, s2):
+            if not t.is_contiguous():
+                raise ValueError("expert tensors must be contiguous")
+        _require_cuda(w13, s13, w2, s2)
+        self.tensors = (w13, s13, w2, s2)
+        self.E, self.I, self.H = E, I, H
+        self.struct = D3Experts(w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(), E, I, H)
+
+
+def quant_act_fp8(x: torch.Tensor, transposed: bool = False):
+    """x bf16 [T,H] -> (q e4m3 [T,H], scales f32 [T,H/128] or [H/128,T])."""
+    _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("x must be bfloat16")
+    T, H = x.shape
+    q = torch.empty((T, H), dtype=FP8, device=x.device)
+    s = torch.empty((H // 128, T) if transposed else (T, H // 128), dtype=torch.float32, device=x.device)
+    call("d3_quant_act_fp8", x.data_ptr(), _row_stride(x), T, H, q.data_ptr(), s.data_ptr(),
+         int(transposed), _stream(x.device))
+    return q, s
+
+
+def router_logits(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """bf16 logits [T,R] = x . weight^T with the fixed summation order."""
+    _require_cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("router projection takes bf16 x and weight")
+    T, H = x.shape
+    R = weight.shape[0]
+    if weight.shape[1] != H or not weight.is_contiguous():
+        raise ValueError("router weight must be contiguous [R, H]")
+    out = torch.empty((T, R), dtype=torch.bfloat16, device=x.device)
+    call("d3_router_logits", x.data_ptr(), _row_stride(x), weight.data_ptr(), R, H, T,
+         out.data_ptr(), out.stride(0), _stream(x.device))
+    return out
+
+
+def route_topk(logits: torch.Tensor, k: int = 8, bias: torch.Tensor | None = None,
+               weights_dtype: torch.dtype | None = None):
+    """Returns (weights [T,k], ids int64 [T,k]) like src/drama3/kernels.py:379-383."""
+    _require_cuda(logits, bias)
+    if logits.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("router logits must be bfloat16 or float32")
+    T, E = logits.shape
+    wdt = weights_dtype or logits.dtype
+    ids = torch.empty((T, k), dtype=torch.int64, device=logits.device)
+    w = torch.empty((T, k), dtype=wdt, device=logits.device)
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+    call("d3_route_topk", logits.data_ptr(),
+         _lib.D3_DTYPE_F32 if logits.dtype == torch.float32 else _lib.D3_DTYPE_BF16,
+         _row_stride(logits), T, E, k, _ptr(bias), ids.data_ptr(), w.data_ptr(),
+         _lib.D3_DTYPE_F32 if wdt == torch.float32 else _lib.D3_DTYPE_BF16, _stream(logits.device))
+    return w, ids
+
+
+def moe_permute(topk_ids: torch.Tensor, num_experts: int, block_m: int = 16):
+    """Reference bucketing buffers (src/drama3/kernels.py:711-731):
+    (counts, starts, total, sorted_ids, expert_ids, inverse_rows, active, n_active)."""
+    _require_cuda(topk_ids)
+    if topk_ids.dtype != torch.int64 or not topk_ids.is_contiguous():
+        raise ValueError("topk_ids must be contiguous int64")
+    T, k = topk_ids.shape
+    P = T * k
+    max_rows = -(-(P + min(P, num_experts) * (block_m - 1)) // block_m) * block_m
+    max_rows = max(max_rows, block_m)
+    dev = topk_ids.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    counts = torch.empty(num_experts, **i32)
+    starts = torch.empty(num_experts, **i32)
+    total = torch.empty(1, **i32)
+    sorted_ids = torch.empty(max_rows, **i32)
+    expert_ids = torch.empty(max_rows // block_m, **i32)
+    inv = torch.empty(max(P, 1), **i32)
+    active = torch.empty(num_experts, **i32)
+    n_active = torch.empty(1, **i32)
+    call("d3_moe_permute", topk_ids.data_ptr(), T, k, num_experts, block_m, counts.data_ptr(),
+         starts.data_ptr(), total.data_ptr(), sorted_ids.data_ptr(), expert_ids.data_ptr(),
+         max_rows, inv.data_ptr(), active.data_ptr(), n_active.data_ptr(), _stream(dev))
+    return counts, starts, total, sorted_ids, expert_ids, inv[:P], active, n_active
+
+
+def silu_mul(projected: torch.Tensor) -> torch.Tensor:
+    _require_cuda(projected)
+    rows, w2 = projected.shape
+    W = w2 // 2
+    out = torch.empty((rows, W), dtype=projected.dtype, device=projected.device)
+    call("d3_silu_mul", projected.data_ptr(), _row_stride(projected), rows, W, out.data_ptr(),
+         _stream(projected.device))
+    return out
+
+
+def silu_mul_quant(projected: torch.Tensor):
+    _require_cuda(projected)
+    rows, w2 = projected.shape
+    W = w2 // 2
+    q = torch.empty((rows, W), dtype=FP8, device=projected.device)
+    s = torch.empty((rows, W // 128), dtype=torch.float32, device=projected.device)
+    call("d3_silu_mul_quant", projected.data_ptr(), _row_stride(projected), rows, W, q.data_ptr(),
+         s.data_ptr(), _stream(projected.device))
+    return q, s
+
+
+def combine_experts(routed: torch.Tensor, shared: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    _require_cuda(routed, shared, gate)
+    T, H = routed.shape
+    if not routed.is_contiguous() or not shared.is_contiguous():
+        raise ValueError("routed and shared outputs must be contiguous")
+    out = torch.empty_like(routed)
+    call("d3_combine_experts", routed.data_ptr(), shared.data_ptr(), gate.data_ptr(), gate.stride(0),
+         T, H, out.data_ptr(), _stream(routed.device))
+    return out
+
+
+def fp8_quantize_weight(weight: torch.Tensor):
+    """bf16 [N,K] -> (e4m3 [Npad,K], f32 [Npad/128, K/128])."""
+    _require_cuda(weight)
+    if weight.dtype != torch.bfloat16 or not weight.is_contiguous():
+        raise ValueError("weight must be contiguous bfloat16")
+    N, K = weight.shape
+    if K % 128:
+        raise ValueError("Experimental dense FP8 needs a 128-aligned reduction width")
+    npad = -(-N // 128) * 128
+    q = torch.empty((npad, K), dtype=FP8, device=weight.device)
+    s = torch.empty((npad // 128, K // 128), dtype=torch.float32, device=weight.device)
+    call("d3_fp8_quantize_weight", weight.data_ptr(), N, K, q.data_ptr(), s.data_ptr(),
+         _stream(weight.device))
+    return q, s
+
+
+def fp8_gemv(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, n: int | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """y bf16 [T,N] = x bf16 [T,K] . dequant(wq, scales)^T (weight-only FP8)."""
+    _require_cuda(x, wq, scales)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("x must be bfloat16")
+    T, K = x.shape
+    N = wq.shape[0] if n is None else n
+    if wq.shape[1] != K or not wq.is_contiguous() or wq.dtype != FP8:
+        raise ValueError("wq must be contiguous float8_e4m3fn [>=N, K]")
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
+    nbytes = ctypes.c_size_t()
+    call("d3_fp8_gemv_workspace_size", T, K, ctypes.byref(nbytes))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+    call("d3_fp8_gemv", x.data_ptr(), _row_stride(x), wq.data_ptr(), scales.data_ptr(), T, N, K,
+         out.data_ptr(), out.stride(0), ws.data_ptr(), nbytes.value, None, _stream(x.device))
+    return out
+
+
+def moe_workspace(T: int, k: int, E: int, I: int, H: int, has_shared: bool, device) -> torch.Tensor:
+    nbytes = ctypes.c_size_t()
+    call("d3_moe_workspace_size", T, k, E, I, H, int(has_shared), ctypes.byref(nbytes))
+    return torch.empty(nbytes.value, dtype=torch.uint8, device=device)
+
+
+def moe_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, experts,
+                shared=None, workspace: torch.Tensor | None = None, status: torch.Tensor | None = None):
+    """Routed (+ shared) expert outputs for given routing: (routed, shared|None)."""
+    _require_cuda(x, topk_ids, topk_weights)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("x must be bfloat16")
+    ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
+    sv = None if shared is None else (shared if isinstance(shared, ExpertView) else ExpertView(shared))
+    T, H = x.shape
+    if H != ev.H:
+        raise ValueError(f"hidden size {H} != expert H {ev.H}")
+    k = topk_ids.shape[1]
+    if topk_ids.dtype != torch.int64 or not topk_ids.is_contiguous():
+        raise ValueError("topk_ids must be contiguous int64")
+    if topk_weights.dtype != torch.bfloat16:
+        topk_weights = topk_weights.to(torch.bfloat16)
+    topk_weights = topk_weights.contiguous()
+    routed = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    shared_out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device) if sv is not None else None
+    if workspace is None:
+        workspace = moe_workspace(T, k, ev.E, ev.I, ev.H, sv is not None, x.device)
+    call("d3_moe_experts", x.data_ptr(), _row_stride(x), topk_ids.data_ptr(), topk_weights.data_ptr(),
+         T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct) if sv is not None else None,
+         routed.data_ptr(), _ptr(shared_out), workspace.data_ptr(), workspace.numel(),
+         _ptr(status), _stream(x.device))
+    return routed, shared_out
+
+
+def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, experts, shared, k: int = 8,
+              router_bias: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, return_routing: bool = False,
+              status: torch.Tensor | None = None):
+    """Whole MoE layer: out = routed + bf16(shared * bf16(sigmoid(gate)))."""
+    _require_cuda(x, router_weight, router_bias)
+    ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
+    sv = shared if isinstance(shared, ExpertView) else ExpertView(shared)
+    T, H = x.shape
+    if router_weight.shape != (ev.E + 1, H) or router_weight.dtype != torch.bfloat16:
+        raise ValueError("router_weight must be bf16 [E+1, H] (router rows + shared-gate row)")
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = moe_workspace(T, k, ev.E, ev.I, ev.H, True, x.device)
+    ids = torch.empty((T, k), dtype=torch.int64, device=x.device) if return_routing else None
+    wts = torch.empty((T, k), dtype=torch.bfloat16, device=x.device) if return_routing else None
+    if router_bias is not None:
+        router_bias = router_bias.to(torch.float32).contiguous()
+    call("d3_moe_layer", x.data_ptr(), _row_stride(x), router_weight.data_ptr(), _ptr(router_bias),
+         T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct), out.data_ptr(), _ptr(ids), _ptr(wts),
+         workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(x.device))
+    if return_routing:
+        return out, ids, wts
+    return out

@@ -1,0 +1,209 @@
+/*
+ * d3moe.h — C ABI of the B200 (sm_100a) FP8 mixture-of-experts hot path.
+ *
+ * Every entry point is stream-ordered (it only enqueues work on `stream`),
+ * performs no device or pinned allocation, never synchronises the device and
+ * keeps no global mutable state apart from a per-thread error string. That
+ * makes every call capturable into a CUDA graph, the way the reference runtime
+ * captures its decode step (reference: src/drama3/engine.py:84-92).
+ *
+ * Return value: D3_OK (0) or a negative D3_E* code. Argument errors are found
+ * on the host before anything is launched; d3_last_error_string() explains the
+ * last failure of the calling thread.
+ *
+ * Tensors are raw device pointers, row-major, with explicit row strides in
+ * elements where the reference accepts strided inputs. Number formats:
+ *   bf16 — IEEE bfloat16 (uint16 storage)
+ *   e4m3 — OCP FP8 E4M3 "fn" (uint8 storage, max 448, no infinities)
+ *   f32  — IEEE binary32
+ * Expert weights keep the reference checkpoint layout (src/drama3/kernels.py:
+ * 298-299, 313-318; src/drama3/model.py:195-198):
+ *   w13 e4m3 [E, 2I, H], rows [gate(0:I) | up(I:2I)];  s13 f32 [E, 2I/128, H/128]
+ *   w2  e4m3 [E, H, I];                                  s2  f32 [E, H/128, I/128]
+ * H and I must be multiples of 128.
+ */
+#ifndef D3MOE_H_
+#define D3MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* d3_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define D3_API __attribute__((visibility("default")))
+#else
+#define D3_API
+#endif
+
+#define D3_OK 0
+#define D3_EINVAL (-1)       /* bad shape, stride, alignment or pointer */
+#define D3_ECUDA (-2)        /* a CUDA runtime / driver call failed */
+#define D3_EWORKSPACE (-3)   /* workspace smaller than the *_workspace_size answer */
+#define D3_EUNSUPPORTED (-4) /* a size beyond what this build supports */
+
+/* dtype tags used where the reference accepts more than one */
+#define D3_DTYPE_BF16 0
+#define D3_DTYPE_F32 1
+
+/* Device status word values written by kernels that wait on barriers. */
+#define D3_STATUS_OK 0
+#define D3_STATUS_WAIT_TIMEOUT 1
+
+D3_API int d3_version(void);
+D3_API const char* d3_last_error_string(void);
+
+/* ------------------------------------------------------------- (a3) quant --
+ * Activation FP8 quantisation per 1x128 group: scale = max(amax,1e-10)/448,
+ * q = e4m3(clamp(x/scale, -448, 448)) with IEEE division and round-to-nearest-
+ * even. x bf16 [T,H] (row stride x_stride >= H, multiple of 8).
+ * scales_transposed = 0: scales f32 [T, H/128] (Fish quantize_groups layout,
+ *   used by src/drama3/kernels.py:297 and model.py:554);
+ * scales_transposed = 1: scales f32 [H/128, T] (FlashInfer layout written by
+ *   src/drama3/moe_input.py:28-30).
+ * Replaces Fish `quantize_groups(quant_kernel, x, H)` (kernels.py:332). */
+D3_API int d3_quant_act_fp8(const void* x, int64_t x_stride, int T, int H, uint8_t* q, float* scales,
+                     int scales_transposed, d3_stream_t stream);
+
+/* Fused activation quant + router-logit conversion.
+ * Replaces prepare_moe_input (src/drama3/moe_input.py:40-79; kernel :8-37).
+ * q e4m3 [T,H]; scales_t f32 [H/128, T]; logits f32 [T,E] from router bf16
+ * [T,E] (stride router_stride). row_slots (int32 or int64 [T], may be NULL)
+ * with padding_start > 0: rows whose slot >= padding_start take row 0's
+ * logits (moe_input.py:32-36). */
+D3_API int d3_prepare_moe_input(const void* x, int64_t x_stride, const void* router,
+                         int64_t router_stride, int T, int H, int E, const void* row_slots,
+                         int row_slots_int64, int64_t padding_start, uint8_t* q, float* scales_t,
+                         float* logits, d3_stream_t stream);
+
+/* --------------------------------------------------- (a1) router projection --
+ * logits bf16 [T, R] = x bf16 [T,H] . W bf16 [R,H]^T with a fixed fp32
+ * summation order (see oracle.moe_oracle.router_logits), rounded to bf16.
+ * Replaces linear(x, layer.gate.weight) / the packed router slice
+ * (src/drama3/model.py:496-504, kernels.py:274-287). R = E (+1 for the
+ * shared-expert gate row). */
+D3_API int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H, int T,
+                     void* logits, int64_t logits_stride, d3_stream_t stream);
+
+/* ------------------------------------------------------------ (a2) route --
+ * fp32 softmax over E logits, top-k by (logit, lower index first), weights
+ * renormalised over the k picks. logits bf16 or f32 [T,E] with row stride;
+ * bias f32 [E] (may be NULL) is added to the fp32 logits first.
+ * ids int64 [T,k] (descending probability); weights [T,k] in weights_dtype.
+ * Replaces route / route_kernel (src/drama3/kernels.py:360-383) and the torch
+ * prefill routing (src/drama3/model.py:526-528). E <= 1024, k <= 32. */
+D3_API int d3_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
+                  const float* bias, int64_t* ids, void* weights, int weights_dtype,
+                  d3_stream_t stream);
+
+/* ---------------------------------------------------------- (a4) permute --
+ * Token->expert bucketing with the reference's device layout
+ * (src/drama3/kernels.py:658-699, buffers :711-731). Pairs p = t*k + r.
+ * counts[E]; starts[E] (each expert's segment padded to block_m); total[1];
+ * sorted_ids[max_rows]: pair ids ascending within each expert, padding slots
+ * hold the sentinel P = T*k, slots at and after `total` are also set to P;
+ * expert_ids[max_rows/block_m]: owning expert per block_m tile, -1 after total.
+ * Optional outputs (NULL to skip): inv_rows[P] = slot of each pair;
+ * active[E] = experts with count > 0 in ascending order, n_active[1].
+ * max_rows must be >= cdiv(P + min(P,E)*(block_m-1), block_m)*block_m. */
+D3_API int d3_moe_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
+                   int32_t* starts, int32_t* total, int32_t* sorted_ids, int32_t* expert_ids,
+                   int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,
+                   d3_stream_t stream);
+
+/* ----------------------------------------------------- (a6) SiLU * mul --
+ * out bf16 [rows, W] = bf16(bf16(silu(gate)) * up), gate = in[:, :W],
+ * up = in[:, W:2W]. Replaces silu_mul (src/drama3/kernels.py:386-402). */
+D3_API int d3_silu_mul(const void* in, int64_t in_stride, int rows, int W, void* out,
+                d3_stream_t stream);
+
+/* SiLU*mul fused with FP8 requantisation per 1x128 group:
+ * a = bf16(silu(gate)) * up (fp32), q e4m3 [rows,W], scales f32 [rows,W/128].
+ * Replaces Fish quantize_groups(silu_mul_quant_kernel, gate_up, W)
+ * (src/drama3/kernels.py:344, :748). */
+D3_API int d3_silu_mul_quant(const void* in, int64_t in_stride, int rows, int W, uint8_t* q,
+                      float* scales, d3_stream_t stream);
+
+/* -------------------------------------------------------- (a9) combine --
+ * out bf16 [T,H] = routed + bf16(shared * bf16(sigmoid(gate))), gate bf16
+ * [T,1] with row stride gate_stride. Replaces combine_experts
+ * (src/drama3/kernels.py:427-445). */
+D3_API int d3_combine_experts(const void* routed, const void* shared, const void* gate,
+                       int64_t gate_stride, int T, int H, void* out, d3_stream_t stream);
+
+/* ------------------------------------------------ (a10) dense FP8 GEMV --
+ * 128x128 block weight quantisation: scale = max(amax,1e-8)/448 per block,
+ * q = e4m3(w/scale). w bf16 [N,K] (K multiple of 128); q e4m3 [Npad,K],
+ * scales f32 [Npad/128, K/128], Npad = cdiv(N,128)*128 (padding rows are 0).
+ * Replaces experimental_fp8._quantize / register (experimental_fp8.py:10-53). */
+D3_API int d3_fp8_quantize_weight(const void* w, int N, int K, uint8_t* q, float* scales,
+                           d3_stream_t stream);
+
+/* y bf16 [T,N] = x bf16 [T,K] . dequant(Wq,S)^T with fp32 accumulation and
+ * bf16 activations (weight-only FP8, the arithmetic of experimental_fp8._gemv,
+ * experimental_fp8.py:21-29, for every T). Wq e4m3 [>=N, K], S f32
+ * [cdiv(N,128), K/128]. Needs workspace of d3_fp8_gemv_workspace_size bytes.
+ * status (device int32, may be NULL) receives D3_STATUS_*. */
+D3_API int d3_fp8_gemv_workspace_size(int T, int K, size_t* bytes);
+D3_API int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const float* s, int T, int N,
+                int K, void* y, int64_t y_stride, void* workspace, size_t workspace_bytes,
+                int32_t* status, d3_stream_t stream);
+
+/* --------------------------------------------- (a5-a8) routed experts --
+ * Expert weights of one MoE layer (reference container: experts.w13_weight,
+ * w13_scale_inv, w2_weight, w2_scale_inv; src/drama3/kernels.py:336-350).
+ * A shared expert is described with E = 1. */
+typedef struct d3_experts {
+  const uint8_t* w13;
+  const float* s13;
+  const uint8_t* w2;
+  const float* s2;
+  int E;
+  int I;
+  int H;
+} d3_experts_t;
+
+/* Workspace for d3_moe_experts / d3_moe_layer at T tokens, top-k. */
+D3_API int d3_moe_workspace_size(int T, int k, int E, int I, int H, int has_shared, size_t* bytes);
+
+/* Routed (and optionally shared) expert computation for given routing:
+ *   routed[t] = bf16( sum_r w[t,r] * down_e(silu_mul_quant(gate_up_e(q(x_t)))) )
+ * in fixed rank order r = 0..k-1 with fp32 accumulation.
+ * ids int64 [T,k], weights bf16 [T,k]. routed_out bf16 [T,H].
+ * If `shared` is not NULL the shared expert runs in the same launches and
+ * shared_out bf16 [T,H] receives bf16(down_shared(...)).
+ * Replaces small_batch_moe (src/drama3/kernels.py:325-357), native_moe
+ * (kernels.py:702-779) and the routed/shared parts of moe_parts
+ * (src/drama3/model.py:490-541). */
+D3_API int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights,
+                   int T, int k, const d3_experts_t* experts, const d3_experts_t* shared,
+                   void* routed_out, void* shared_out, void* workspace, size_t workspace_bytes,
+                   int32_t* status, d3_stream_t stream);
+
+/* One whole MoE layer: router projection over [E+1, H] bf16 (rows 0..E-1 the
+ * router, row E the shared-expert gate; src/drama3/model.py:236-245), top-k
+ * routing with optional per-expert bias, routed + shared experts, and
+ *   out = routed + bf16(shared * bf16(sigmoid(gate)))
+ * Replaces DramaModel.moe (src/drama3/model.py:485-488). Optional debug
+ * outputs (NULL to skip): ids int64 [T,k], weights bf16 [T,k]. */
+D3_API int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w, const float* router_bias,
+                 int T, int k, const d3_experts_t* experts, const d3_experts_t* shared, void* out,
+                 int64_t* ids_out, void* weights_out, void* workspace, size_t workspace_bytes,
+                 int32_t* status, d3_stream_t stream);
+
+/* Benchmark hook: while set, d3_moe_experts / d3_moe_layer calls made by the
+ * calling thread record events[i] (cudaEvent_t handles, n >= 5) on their
+ * stream at stage boundaries: 0 call start, 1 before the gate_up engine,
+ * 2 after gate_up, 3 after the down engine, 4 call end. NULL clears it.
+ * No counterpart in the reference (its scripts time whole calls). */
+D3_API int d3_set_stage_events(void* const* events, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* D3MOE_H_ */
