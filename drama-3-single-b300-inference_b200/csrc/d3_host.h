@@ -8,7 +8,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
-#include "../../include/d3moe.h"
+#include "d3moe.h"  // include/ of the repository root (passed with -I)
 
 namespace d3 {
 

@@ -9,10 +9,12 @@
 //     the checkpoint layout, 128B-swizzled) and the matching activation rows by
 //     TMA into a STAGES-deep mbarrier ring that runs across item boundaries;
 //   * eight consumer warps each own 16 weight rows and run mma.sync
-//     m16n8k32 e4m3 (weights as A, up to 64 tokens as B in chunks of 8) per
-//     128-wide K block, then fold that block's partial sums into fp32 registers
-//     with weight_scale[n/128][k/128] * act_scale[token][k/128] (the 128x128
-//     block-scale promotion, done in registers at no memory cost);
+//     m16n8k32 e4m3 (weights as A, tokens as B in chunks of 8) per 128-wide K
+//     block, then fold that block's partial sums into fp32 registers with
+//     weight_scale[n/128][k/128] * act_scale[token][k/128] (the 128x128
+//     block-scale promotion, done in registers at no memory cost). The inner
+//     loop is instantiated per token-chunk count (1, 2, 4, 8) and chosen per
+//     item, so a stage costs work proportional to the expert's real tokens;
 //   * epilogues: gate_up -> bf16(gate), bf16(up), a = bf16(silu(gate))*up,
 //     FP8 requant per 128-group across the 8 warps (EPI_GATE_UP);
 //     down -> fp32 rows for the fixed-order combine (EPI_DOWN);
@@ -35,7 +37,8 @@ namespace d3 {
 enum EpilogueKind { EPI_GATE_UP = 0, EPI_DOWN = 1, EPI_DENSE = 2 };
 
 constexpr int kEngineConsumerWarps = 8;
-constexpr int kEngineThreads = (kEngineConsumerWarps + 1) * 32;
+constexpr int kEngineConsumerThreads = kEngineConsumerWarps * 32;
+constexpr int kEngineThreads = kEngineConsumerThreads + 32;
 constexpr int kTokensPerGroup = 64;
 
 struct EngineArgs {
@@ -46,7 +49,8 @@ struct EngineArgs {
   const int32_t* active;    // [E] active expert ids, ascending
   const int32_t* n_active;  // [1]
   int num_groups;           // routed groups when active == nullptr
-  int has_shared;           // 1: shared expert present
+  int shared_groups;        // work groups of the shared expert (0: none)
+  int shared_chunk;         // tokens per shared-expert work group
   int shared_row0;          // first activation row of the shared expert
   int shared_count;         // its token count
   int dense_count;          // token count in dense mode
@@ -68,12 +72,12 @@ struct EngineArgs {
 };
 
 struct WorkItem {
-  int wrow;        // first weight row of the tile (gate half for EPI_GATE_UP)
-  int wrow_up;     // first up-half weight row (EPI_GATE_UP)
-  int tile;        // tile index within the group
-  int row0;        // first activation row
-  int m;           // tokens
-  int shared;      // uses the shared-expert tensor map / scales
+  int wrow;     // first weight row of the tile (gate half for EPI_GATE_UP)
+  int wrow_up;  // first up-half weight row (EPI_GATE_UP)
+  int tile;     // tile index within the group
+  int row0;     // first activation row
+  int m;        // tokens
+  int shared;   // uses the shared-expert tensor map / scales
 };
 
 __device__ __forceinline__ WorkItem engine_item(const EngineArgs& a, int i) {
@@ -81,14 +85,15 @@ __device__ __forceinline__ WorkItem engine_item(const EngineArgs& a, int i) {
   const int gi = i / a.tiles;
   w.tile = i - gi * a.tiles;
   int e;
-  if (a.has_shared && gi == 0) {
+  if (gi < a.shared_groups) {
+    // the shared expert's tokens are split into groups spread over CTAs
     w.shared = 1;
     e = 0;
-    w.row0 = a.shared_row0;
-    w.m = a.shared_count;
+    w.row0 = a.shared_row0 + gi * a.shared_chunk;
+    w.m = min(a.shared_chunk, a.shared_count - gi * a.shared_chunk);
   } else {
     w.shared = 0;
-    const int ri = gi - a.has_shared;
+    const int ri = gi - a.shared_groups;
     e = a.active ? a.active[ri] : ri;
     w.row0 = a.starts ? a.starts[e] : 0;
     w.m = a.counts ? a.counts[e] : a.dense_count;
@@ -104,13 +109,15 @@ struct EngineSmem {
   static constexpr int kActBytes = (ACT_F16 ? 2 : 1) * kTokensPerGroup * 128;
   static constexpr int kStageBytes = kWBytes + kActBytes;
   static constexpr int kRingBytes = STAGES * kStageBytes;
-  // after the ring: full[STAGES], empty[STAGES], abort flag, amax[8][64], slab[64][KB]
+  // after the ring: full[STAGES], empty[STAGES], abort flag, amax[8][64],
+  // weight-scale slab [2][KB], activation-scale slab [64][KB]
   static constexpr int kBarOffset = kRingBytes;
   static constexpr int kAbortOffset = kBarOffset + 2 * STAGES * 8;
   static constexpr int kAmaxOffset = kAbortOffset + 16;
-  static constexpr int kSlabOffset = kAmaxOffset + kEngineConsumerWarps * kTokensPerGroup * 4;
+  static constexpr int kWsOffset = kAmaxOffset + kEngineConsumerWarps * kTokensPerGroup * 4;
+  __host__ __device__ static int slab_offset(int KB) { return kWsOffset + 2 * KB * 4; }
   static size_t bytes(int KB) {
-    return 1024 + static_cast<size_t>(kSlabOffset) + static_cast<size_t>(kTokensPerGroup) * KB * 4;
+    return 1024 + static_cast<size_t>(slab_offset(KB)) + static_cast<size_t>(kTokensPerGroup) * KB * 4;
   }
 };
 
@@ -124,7 +131,197 @@ __device__ __forceinline__ bool ring_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
-template <int EPI, bool ACT_F16, int NCH, int STAGES>
+struct ConsumerCtx {
+  uint8_t* smem;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* abort_flag;
+  float* amax_sm;  // [8][64]
+  float* wsl;      // [2][KB] weight scales of the current item (gate, up)
+  float* slab;     // [64][KB] activation scales of the current group
+  int warp, lane;
+};
+
+// All K blocks of one token group (mg <= 8*NC tokens) of one work item, then
+// its epilogue. `it` is the ring position, shared with the producer's order.
+template <int EPI, bool ACT_F16, int STAGES, int NC>
+__device__ __forceinline__ void consume_group(const EngineArgs& args, const ConsumerCtx& cx,
+                                              const WorkItem& w, int g0, int mg, uint32_t& it) {
+  using L = EngineSmem<EPI, ACT_F16, STAGES>;
+  constexpr int NACC = (EPI == EPI_GATE_UP) ? 2 : 1;
+  const int warp = cx.warp, lane = cx.lane;
+  const int g = lane >> 2, tq = lane & 3;
+  const int KB = args.KB;
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+
+  float acc[NACC][NC][4];
+#pragma unroll
+  for (int h = 0; h < NACC; ++h)
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[h][c][j] = 0.f;
+
+  // per-lane smem offsets that do not change across stages
+  const uint32_t ar = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
+  const uint32_t a_hi = lane >> 4;
+  const uint32_t br = lane & 7, b_hi = (lane >> 3) & 1;
+
+  for (int kb = 0; kb < KB; ++kb, ++it) {
+    const int s = it % STAGES;
+    const uint32_t ph = (it / STAGES) & 1;
+    ring_wait(&cx.full[s], ph, cx.abort_flag, args.status);
+    const uint32_t wsm = smem_u32(cx.smem + s * L::kStageBytes);
+    const uint32_t asm_ = wsm + L::kWBytes;
+    float tmp[NACC][NC][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t a[NACC][4];
+#pragma unroll
+      for (int h = 0; h < NACC; ++h)
+        ldmatrix_x4(wsm + h * 16384 + swz128(ar, 2 * ks + a_hi), a[h][0], a[h][1], a[h][2], a[h][3]);
+      if constexpr (!ACT_F16) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          uint32_t b0, b1;
+          ldmatrix_x2(asm_ + swz128(c * 8 + br, 2 * ks + b_hi), b0, b1);
+#pragma unroll
+          for (int h = 0; h < NACC; ++h) {
+            if (ks == 0)
+              mma_e4m3_16832(tmp[h][c], a[h], b0, b1, zero4);
+            else
+              mma_e4m3_16832(tmp[h][c], a[h], b0, b1, tmp[h][c]);
+          }
+        }
+      } else {
+        // widen the fp8 A fragment to two f16 k16 fragments
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          lo[j] = e4m3x2_to_f16x2(static_cast<uint16_t>(a[0][j] & 0xffffu));
+          hi[j] = e4m3x2_to_f16x2(static_cast<uint16_t>(a[0][j] >> 16));
+        }
+        const uint32_t half_base = asm_ + (ks >> 1) * 8192;
+        const uint32_t ch = 4 * (ks & 1) + (tq >> 1);
+        const uint32_t off = (tq & 1) * 8;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const uint32_t row = c * 8 + g;
+          uint32_t b0, b1, b2, b3;
+          asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
+                       : "=r"(b0), "=r"(b1)
+                       : "r"(half_base + swz128(row, ch) + off));
+          asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
+                       : "=r"(b2), "=r"(b3)
+                       : "r"(half_base + swz128(row, ch + 2) + off));
+          if (ks == 0)
+            mma_f16_16816(tmp[0][c], lo[0], lo[1], hi[0], hi[1], b0, b1, zero4);
+          else
+            mma_f16_16816(tmp[0][c], lo[0], lo[1], hi[0], hi[1], b0, b1, tmp[0][c]);
+          mma_f16_16816(tmp[0][c], lo[2], lo[3], hi[2], hi[3], b2, b3, tmp[0][c]);
+        }
+      }
+    }
+    // release the stage as soon as its shared memory has been read
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&cx.empty[s]);
+    // block-scale promotion
+    const float ws_g = cx.wsl[kb];
+    const float ws_u = (EPI == EPI_GATE_UP) ? cx.wsl[KB + kb] : 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int t0 = c * 8 + 2 * tq;
+      const float f0 = cx.slab[t0 * KB + kb], f1 = cx.slab[(t0 + 1) * KB + kb];
+#pragma unroll
+      for (int h = 0; h < NACC; ++h) {
+        const float ws = h ? ws_u : ws_g;
+        const float p0 = ws * f0, p1 = ws * f1;
+        acc[h][c][0] = fmaf(tmp[h][c][0], p0, acc[h][c][0]);
+        acc[h][c][1] = fmaf(tmp[h][c][1], p1, acc[h][c][1]);
+        acc[h][c][2] = fmaf(tmp[h][c][2], p0, acc[h][c][2]);
+        acc[h][c][3] = fmaf(tmp[h][c][3], p1, acc[h][c][3]);
+      }
+    }
+  }
+
+  // -------------------------------------------------------------- epilogue --
+  const int out_row0 = w.row0 + g0;
+  const int col0 = w.tile * 128 + 16 * warp + g;  // rows g and g+8 of this warp
+  if constexpr (EPI == EPI_GATE_UP) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float gv = bf16_round(acc[0][c][j]);
+        const float uv = bf16_round(acc[1][c][j]);
+        const float sg = bf16_round(gv * (1.0f / (1.0f + expf(-gv))));
+        acc[0][c][j] = sg * uv;
+      }
+      float m0 = fmaxf(fabsf(acc[0][c][0]), fabsf(acc[0][c][2]));
+      float m1 = fmaxf(fabsf(acc[0][c][1]), fabsf(acc[0][c][3]));
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+      }
+      if (g == 0) {
+        cx.amax_sm[warp * kTokensPerGroup + c * 8 + 2 * tq] = m0;
+        cx.amax_sm[warp * kTokensPerGroup + c * 8 + 2 * tq + 1] = m1;
+      }
+    }
+    named_bar_sync(1, kEngineConsumerThreads);
+    const int I = args.out_cols;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = c * 8 + 2 * tq + u;
+        if (t < mg) {
+          float am = 0.f;
+#pragma unroll
+          for (int w2 = 0; w2 < kEngineConsumerWarps; ++w2)
+            am = fmaxf(am, cx.amax_sm[w2 * kTokensPerGroup + t]);
+          const float sc = act_scale_from_amax(am);
+          uint8_t* qrow = args.out_q + static_cast<int64_t>(out_row0 + t) * I;
+          qrow[col0] = act_quant(acc[0][c][u], sc);
+          qrow[col0 + 8] = act_quant(acc[0][c][u + 2], sc);
+          if (warp == 0 && g == 0)
+            args.out_qs[static_cast<int64_t>(out_row0 + t) * (I / 128) + w.tile] = sc;
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_DOWN) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = c * 8 + 2 * tq + u;
+        if (t < mg) {
+          float* orow = args.out_rows + static_cast<int64_t>(out_row0 + t) * args.out_ld;
+          orow[col0] = acc[0][c][u];
+          orow[col0 + 8] = acc[0][c][u + 2];
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = c * 8 + 2 * tq + u;
+        if (t < mg) {
+          __nv_bfloat16* orow = args.out_bf16 + static_cast<int64_t>(out_row0 + t) * args.out_ld;
+          if (col0 < args.out_cols) orow[col0] = __float2bfloat16_rn(acc[0][c][u]);
+          if (col0 + 8 < args.out_cols) orow[col0 + 8] = __float2bfloat16_rn(acc[0][c][u + 2]);
+        }
+      }
+    }
+  }
+}
+
+// MAXNC: largest token-chunk count (8 tokens each) any item of this launch can
+// need, i.e. ceil(min(max tokens per expert, 64) / 8) rounded up to 1, 2, 4, 8.
+template <int EPI, bool ACT_F16, int STAGES, int MAXNC>
 __global__ void __launch_bounds__(kEngineThreads, 1)
     expert_gemv_kernel(const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_w_sh,
@@ -136,13 +333,12 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty = full + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbortOffset);
-  float* amax_sm = reinterpret_cast<float*>(smem + L::kAmaxOffset);
-  float* slab = reinterpret_cast<float*>(smem + L::kSlabOffset);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = args.KB;
-  const int n_groups = (args.active ? *args.n_active : args.num_groups) + args.has_shared;
+  const int n_groups = (args.active ? *args.n_active : args.num_groups) + args.shared_groups;
   const int n_items = n_groups * args.tiles;
+  constexpr int kGroup = MAXNC * 8 < kTokensPerGroup ? MAXNC * 8 : kTokensPerGroup;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -159,7 +355,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
     if (lane == 0) {
       prefetch_tensormap(&tm_w);
       prefetch_tensormap(&tm_act);
-      if (args.has_shared) prefetch_tensormap(&tm_w_sh);
+      if (args.shared_groups) prefetch_tensormap(&tm_w_sh);
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_a = l2_policy_evict_last();
       uint32_t it = 0;
@@ -169,9 +365,8 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
       for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
         const WorkItem w = engine_item(args, i);
         const CUtensorMap* wmap = w.shared ? &tm_w_sh : &tm_w;
-        const int wrow = w.shared ? w.wrow - 0 : w.wrow;
-        for (int g0 = 0; g0 < w.m; g0 += kTokensPerGroup) {
-          const int mg = min(kTokensPerGroup, w.m - g0);
+        for (int g0 = 0; g0 < w.m; g0 += kGroup) {
+          const int mg = min(kGroup, w.m - g0);
           const int nbox = (mg + 15) / 16;
           const uint32_t bytes = L::kWBytes + nbox * (ACT_F16 ? 4096 : 2048);
           for (int kb = 0; kb < KB; ++kb, ++it) {
@@ -181,19 +376,16 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             uint8_t* st = smem + s * L::kStageBytes;
             mbar_arrive_expect_tx(&full[s], bytes);
             last_parity[s] = static_cast<int>(ph);
-            tma_load_2d_hint(st, wmap, kb * 128, wrow, &full[s], pol_w);
+            tma_load_2d_hint(st, wmap, kb * 128, w.wrow, &full[s], pol_w);
             if (EPI == EPI_GATE_UP)
               tma_load_2d_hint(st + 128 * 128, wmap, kb * 128, w.wrow_up, &full[s], pol_w);
             uint8_t* act = st + L::kWBytes;
             for (int b = 0; b < nbox; ++b) {
               const int row = w.row0 + g0 + 16 * b;
-              if (ACT_F16) {
-                tma_load_2d_hint(act + b * 2048, &tm_act, kb * 128, row, &full[s], pol_a);
+              tma_load_2d_hint(act + b * 2048, &tm_act, kb * 128, row, &full[s], pol_a);
+              if (ACT_F16)
                 tma_load_2d_hint(act + 8192 + b * 2048, &tm_act, kb * 128 + 64, row, &full[s],
                                  pol_a);
-              } else {
-                tma_load_2d_hint(act + b * 2048, &tm_act, kb * 128, row, &full[s], pol_a);
-              }
             }
           }
         }
@@ -207,206 +399,44 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
   }
 
   // -------------------------------------------------------------- consumers --
-  const int g = lane >> 2, tq = lane & 3;
+  ConsumerCtx cx;
+  cx.smem = smem;
+  cx.full = full;
+  cx.empty = empty;
+  cx.abort_flag = abort_flag;
+  cx.amax_sm = reinterpret_cast<float*>(smem + L::kAmaxOffset);
+  cx.wsl = reinterpret_cast<float*>(smem + L::kWsOffset);
+  cx.slab = reinterpret_cast<float*>(smem + L::slab_offset(KB));
+  cx.warp = warp;
+  cx.lane = lane;
   const int ctid = threadIdx.x;  // 0..255
   uint32_t it = 0;
-  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-  constexpr int NACC = (EPI == EPI_GATE_UP) ? 2 : 1;
 
   for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
     const WorkItem w = engine_item(args, i);
     const float* wscale = w.shared ? args.wscale_sh : args.wscale;
-    const int sb_g = (w.shared ? w.wrow : w.wrow) / 128;  // scale row block of the tile
-    const int sb_u = w.wrow_up / 128;
-    for (int g0 = 0; g0 < w.m; g0 += kTokensPerGroup) {
-      const int mg = min(kTokensPerGroup, w.m - g0);
-      // stage this group's activation scales [mg][KB] into shared memory
-      named_bar_sync(1, kEngineConsumerWarps * 32);
+    for (int g0 = 0; g0 < w.m; g0 += kGroup) {
+      const int mg = min(kGroup, w.m - g0);
+      // stage this group's scales in shared memory: weights [2][KB], acts [mg][KB]
+      named_bar_sync(1, kEngineConsumerThreads);
       {
         const float* src = args.act_scale + static_cast<int64_t>(w.row0 + g0) * KB;
-        for (int idx = ctid; idx < mg * KB; idx += kEngineConsumerWarps * 32) slab[idx] = src[idx];
-      }
-      named_bar_sync(1, kEngineConsumerWarps * 32);
-
-      float acc[NACC][NCH][4];
-#pragma unroll
-      for (int h = 0; h < NACC; ++h)
-#pragma unroll
-        for (int c = 0; c < NCH; ++c)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[h][c][j] = 0.f;
-
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        ring_wait(&full[s], ph, abort_flag, args.status);
-        const uint32_t wsm = smem_u32(smem + s * L::kStageBytes);
-        const uint32_t asm_ = wsm + L::kWBytes;
-        float tmp[NACC][NCH][4];
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint32_t ar = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const uint32_t ach = 2 * ks + (lane >> 4);
-          uint32_t a[NACC][4];
-#pragma unroll
-          for (int h = 0; h < NACC; ++h)
-            ldmatrix_x4(wsm + h * 16384 + swz128(ar, ach), a[h][0], a[h][1], a[h][2], a[h][3]);
-          if constexpr (!ACT_F16) {
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              if (c * 8 < mg) {
-                const uint32_t br = c * 8 + (lane & 7);
-                const uint32_t bch = 2 * ks + ((lane >> 3) & 1);
-                uint32_t b0, b1;
-                ldmatrix_x2(asm_ + swz128(br, bch), b0, b1);
-#pragma unroll
-                for (int h = 0; h < NACC; ++h) {
-                  if (ks == 0)
-                    mma_e4m3_16832(tmp[h][c], a[h], b0, b1, zero4);
-                  else
-                    mma_e4m3_16832(tmp[h][c], a[h], b0, b1, tmp[h][c]);
-                }
-              }
-            }
-          } else {
-            // widen the fp8 A fragment to two f16 k16 fragments
-            uint32_t lo[4], hi[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              lo[j] = e4m3x2_to_f16x2(static_cast<uint16_t>(a[0][j] & 0xffffu));
-              hi[j] = e4m3x2_to_f16x2(static_cast<uint16_t>(a[0][j] >> 16));
-            }
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              if (c * 8 < mg) {
-                const uint32_t br = c * 8 + g;
-                const uint32_t half_base = asm_ + (ks >> 1) * 8192;
-                const uint32_t ch = 4 * (ks & 1) + (tq >> 1);
-                const uint32_t off = (tq & 1) * 8;
-                uint32_t b0, b1, b2, b3;
-                asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
-                             : "=r"(b0), "=r"(b1)
-                             : "r"(half_base + swz128(br, ch) + off));
-                asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
-                             : "=r"(b2), "=r"(b3)
-                             : "r"(half_base + swz128(br, ch + 2) + off));
-                if (ks == 0)
-                  mma_f16_16816(tmp[0][c], lo[0], lo[1], hi[0], hi[1], b0, b1, zero4);
-                else
-                  mma_f16_16816(tmp[0][c], lo[0], lo[1], hi[0], hi[1], b0, b1, tmp[0][c]);
-                mma_f16_16816(tmp[0][c], lo[2], lo[3], hi[2], hi[3], b2, b3, tmp[0][c]);
-              }
-            }
-          }
-        }
-        // release the stage as soon as its shared memory has been read
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        // block-scale promotion
-        const float ws_g = wscale[sb_g * KB + kb];
-        const float ws_u = (EPI == EPI_GATE_UP) ? wscale[sb_u * KB + kb] : 0.f;
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          if (c * 8 < mg) {
-            const int t0 = c * 8 + 2 * tq;
-            const float f0 = slab[t0 * KB + kb], f1 = slab[(t0 + 1) * KB + kb];
-#pragma unroll
-            for (int h = 0; h < NACC; ++h) {
-              const float ws = h ? ws_u : ws_g;
-              const float p0 = ws * f0, p1 = ws * f1;
-              acc[h][c][0] = fmaf(tmp[h][c][0], p0, acc[h][c][0]);
-              acc[h][c][1] = fmaf(tmp[h][c][1], p1, acc[h][c][1]);
-              acc[h][c][2] = fmaf(tmp[h][c][2], p0, acc[h][c][2]);
-              acc[h][c][3] = fmaf(tmp[h][c][3], p1, acc[h][c][3]);
-            }
-          }
+        for (int idx = ctid; idx < mg * KB; idx += kEngineConsumerThreads) cx.slab[idx] = src[idx];
+        for (int idx = ctid; idx < KB; idx += kEngineConsumerThreads) {
+          cx.wsl[idx] = wscale[(w.wrow / 128) * KB + idx];
+          if (EPI == EPI_GATE_UP) cx.wsl[KB + idx] = wscale[(w.wrow_up / 128) * KB + idx];
         }
       }
-
-      // ------------------------------------------------------------ epilogue --
-      const int out_row0 = w.row0 + g0;
-      const int col0 = w.tile * 128 + 16 * warp + g;  // rows g and g+8 of this warp
-      if constexpr (EPI == EPI_GATE_UP) {
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          if (c * 8 < mg) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float gv = bf16_round(acc[0][c][j]);
-              const float uv = bf16_round(acc[1][c][j]);
-              const float sg = bf16_round(gv * (1.0f / (1.0f + expf(-gv))));
-              acc[0][c][j] = sg * uv;
-            }
-            float m0 = fmaxf(fabsf(acc[0][c][0]), fabsf(acc[0][c][2]));
-            float m1 = fmaxf(fabsf(acc[0][c][1]), fabsf(acc[0][c][3]));
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-              m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-              m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
-            }
-            if (g == 0) {
-              amax_sm[warp * kTokensPerGroup + c * 8 + 2 * tq] = m0;
-              amax_sm[warp * kTokensPerGroup + c * 8 + 2 * tq + 1] = m1;
-            }
-          }
-        }
-        named_bar_sync(1, kEngineConsumerWarps * 32);
-        const int I = args.out_cols;
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          if (c * 8 < mg) {
-            const int t0 = c * 8 + 2 * tq;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int t = t0 + u;
-              if (t < mg) {
-                float am = 0.f;
-#pragma unroll
-                for (int w2 = 0; w2 < kEngineConsumerWarps; ++w2)
-                  am = fmaxf(am, amax_sm[w2 * kTokensPerGroup + t]);
-                const float sc = act_scale_from_amax(am);
-                uint8_t* qrow = args.out_q + static_cast<int64_t>(out_row0 + t) * I;
-                qrow[col0] = act_quant(acc[0][c][u], sc);
-                qrow[col0 + 8] = act_quant(acc[0][c][u + 2], sc);
-                if (warp == 0 && g == 0)
-                  args.out_qs[static_cast<int64_t>(out_row0 + t) * (I / 128) + w.tile] = sc;
-              }
-            }
-          }
-        }
-      } else if constexpr (EPI == EPI_DOWN) {
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          if (c * 8 < mg) {
-            const int t0 = c * 8 + 2 * tq;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int t = t0 + u;
-              if (t < mg) {
-                float* orow = args.out_rows + static_cast<int64_t>(out_row0 + t) * args.out_ld;
-                orow[col0] = acc[0][c][u];
-                orow[col0 + 8] = acc[0][c][u + 2];
-              }
-            }
-          }
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          if (c * 8 < mg) {
-            const int t0 = c * 8 + 2 * tq;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int t = t0 + u;
-              if (t < mg) {
-                __nv_bfloat16* orow = args.out_bf16 + static_cast<int64_t>(out_row0 + t) * args.out_ld;
-                if (col0 < args.out_cols) orow[col0] = __float2bfloat16_rn(acc[0][c][u]);
-                if (col0 + 8 < args.out_cols) orow[col0 + 8] = __float2bfloat16_rn(acc[0][c][u + 2]);
-              }
-            }
-          }
-        }
-      }
+      named_bar_sync(1, kEngineConsumerThreads);
+      const int nc = (mg + 7) / 8;
+      if (MAXNC == 1 || nc <= 1)
+        consume_group<EPI, ACT_F16, STAGES, 1>(args, cx, w, g0, mg, it);
+      else if (MAXNC == 2 || nc <= 2)
+        consume_group<EPI, ACT_F16, STAGES, (MAXNC >= 2 ? 2 : 1)>(args, cx, w, g0, mg, it);
+      else if (MAXNC == 4 || nc <= 4)
+        consume_group<EPI, ACT_F16, STAGES, (MAXNC >= 4 ? 4 : 1)>(args, cx, w, g0, mg, it);
+      else
+        consume_group<EPI, ACT_F16, STAGES, (MAXNC >= 8 ? 8 : 1)>(args, cx, w, g0, mg, it);
     }
   }
 }

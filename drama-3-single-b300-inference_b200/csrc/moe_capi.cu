@@ -98,7 +98,7 @@ int nch_for(int max_tokens) {
 template <int EPI, bool ACT_F16, int NCH, int STAGES>
 int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& ta,
                        const EngineArgs& args, int grid, cudaStream_t s) {
-  auto kern = expert_gemv_kernel<EPI, ACT_F16, NCH, STAGES>;
+  auto kern = expert_gemv_kernel<EPI, ACT_F16, STAGES, NCH>;
   const size_t smem = EngineSmem<EPI, ACT_F16, STAGES>::bytes(args.KB);
   static int configured[64] = {0};
   int dev = 0;
@@ -116,11 +116,12 @@ int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUt
 template <int EPI, bool ACT_F16, int STAGES>
 int launch_engine(int nch, const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& ta,
                   const EngineArgs& args, int grid, cudaStream_t s) {
+  constexpr int kMax = (EPI == EPI_GATE_UP) ? 4 : 8;  // gate_up holds two accumulator sets
   switch (nch) {
     case 1: return launch_engine_inst<EPI, ACT_F16, 1, STAGES>(tw, twsh, ta, args, grid, s);
     case 2: return launch_engine_inst<EPI, ACT_F16, 2, STAGES>(tw, twsh, ta, args, grid, s);
     case 4: return launch_engine_inst<EPI, ACT_F16, 4, STAGES>(tw, twsh, ta, args, grid, s);
-    default: return launch_engine_inst<EPI, ACT_F16, 8, STAGES>(tw, twsh, ta, args, grid, s);
+    default: return launch_engine_inst<EPI, ACT_F16, kMax, STAGES>(tw, twsh, ta, args, grid, s);
   }
 }
 
@@ -167,7 +168,11 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.starts = b.starts;
     a.active = b.active;
     a.n_active = b.n_active;
-    a.has_shared = has_shared;
+    // gate_up keeps two accumulator sets (gate, up): at most 4 token chunks
+    // (32 tokens) per group fit the 168 registers a 9-warp CTA gets
+    const int nch = nch_for(T) < 4 ? nch_for(T) : 4;
+    a.shared_chunk = nch * 8;
+    a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
     a.shared_row0 = P;
     a.shared_count = T;
     a.tiles = I / 128;
@@ -181,9 +186,9 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.out_qs = b.sa;
     a.out_cols = I;
     a.status = status;
-    const int max_items = (E + has_shared) * (I / 128);
+    const int max_items = (E + a.shared_groups) * (I / 128);
     const int grid = max_items < sms ? max_items : sms;
-    rc = launch_engine<EPI_GATE_UP, false, kStagesGateUp>(nch_for(T), tw, twsh, ta, a, grid, s);
+    rc = launch_engine<EPI_GATE_UP, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s);
     if (rc) return rc;
   }
   stage_mark(2, s);
@@ -198,7 +203,9 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.starts = b.starts;
     a.active = b.active;
     a.n_active = b.n_active;
-    a.has_shared = has_shared;
+    const int nch = nch_for(T);
+    a.shared_chunk = nch * 8;
+    a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
     a.shared_row0 = P;
     a.shared_count = T;
     a.tiles = H / 128;
@@ -211,9 +218,9 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.out_rows = b.d;
     a.out_ld = H;
     a.status = status;
-    const int max_items = (E + has_shared) * (H / 128);
+    const int max_items = (E + a.shared_groups) * (H / 128);
     const int grid = max_items < sms ? max_items : sms;
-    rc = launch_engine<EPI_DOWN, false, kStagesDown>(nch_for(T), tw, twsh, ta, a, grid, s);
+    rc = launch_engine<EPI_DOWN, false, kStagesDown>(nch, tw, twsh, ta, a, grid, s);
     if (rc) return rc;
   }
   stage_mark(3, s);

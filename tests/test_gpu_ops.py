@@ -186,9 +186,17 @@ def test_dense_fp8_gemv_matches_oracle(d3, T, N, K):
     x = O.bf16_round(rng.standard_normal((T, K)).astype(np.float32))
     y = d3["ops"].fp8_gemv(to_bf16(x), to_fp8(q), torch.from_numpy(s).cuda(), n=N)
     ref = O.fp8_gemv(x, q, s, n=N)
-    d = ulps_bf16(from_bf16(y), ref)
-    assert d.max() <= 2 and (d > 0).mean() < 0.02
-    assert_close(from_bf16(y), ref, what="dense gemv")
+    got = from_bf16(y)
+    # Exact value of the same dequantise-then-matmul in float64: the kernel must
+    # return it correctly rounded to bf16, up to fp32 summation-order noise
+    # (half a bf16 ulp + 2^-16 of the output rms).
+    exact = x.astype(np.float64) @ O.dequant_blocks(q, s)[:N].astype(np.float64).T
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exact), 1e-30))) - 7)
+    bound = 0.5 * ulp + np.sqrt((exact ** 2).mean()) * 2.0 ** -16
+    excess = np.abs(got - exact) - bound
+    assert (excess <= 0).all(), float(excess.max())
+    assert (ulps_bf16(got, ref) > 1).sum() == 0
+    assert_close(got, ref, what="dense gemv")
 
 
 # ---------------------------------------------------------------- (a5-a7) --
