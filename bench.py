@@ -249,7 +249,7 @@ def main() -> None:
     views = [(ops.ExpertView(l.experts), ops.ExpertView(l.shared)) for l in layers]
     ws_moe = ops.moe_workspace(T, TOPK, E, I, H, True, dev)
     nb = ctypes.c_size_t()
-    lib.d3_fp8_gemv_workspace_size(T, H, ctypes.byref(nb))
+    lib.d3_fp8_gemv_workspace_size(T, N_QKV, H, ctypes.byref(nb))
     ws_dense = torch.empty(nb.value, dtype=torch.uint8, device=dev)
     nsteps_total = args.warmup + args.steps
     gin = torch.Generator(device=dev)

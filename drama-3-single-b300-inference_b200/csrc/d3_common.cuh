@@ -121,6 +121,22 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// 4-byte asynchronous global->shared copy (LDGSTS), completion tracked by an
+// mbarrier through cp_async_arrive_noinc.
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async issued so far by this thread has landed.
+// The arrival is not added to the pending count (.noinc): the barrier's
+// expected count must include it.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // Byte offset of 16-byte chunk `chunk` of row `row` in a tile written by TMA
 // with CU_TENSOR_MAP_SWIZZLE_128B (rows of 128 bytes, 1024-byte aligned base).
 __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {

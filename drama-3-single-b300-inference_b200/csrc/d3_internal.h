@@ -35,6 +35,13 @@ void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int
                        const float* bias, int64_t* ids, void* weights, int weights_dtype,
                        cudaStream_t s);
 
+// route_topk + permute; one fused single-CTA kernel when T*k <= 4096.
+int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, int T, int E,
+                         int k, const float* bias, int64_t* ids, void* weights, int weights_dtype,
+                         int block_m, int32_t* counts, int32_t* starts, int32_t* total,
+                         int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
+                         int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s);
+
 int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
                    int32_t* starts, int32_t* total, int32_t* sorted_ids, int32_t* expert_ids,
                    int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,

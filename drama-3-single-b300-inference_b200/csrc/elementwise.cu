@@ -3,9 +3,10 @@
 // SiLU*mul (+ requant), routed/shared combine, 128x128 weight quantisation and
 // the f16 activation prep of the weight-only dense GEMV.
 //
-// Layout rule for all of them: one warp owns one row; a half-warp owns one
-// 128-element quantisation group, each lane 8 consecutive elements (16-byte
-// loads), so the group amax is a 4-step shuffle inside the half-warp.
+// Layout rule for the quantisers: one warp owns two 128-element groups of one
+// row (warps = rows x ceil(groups/2), so every load is issued at once); a
+// half-warp owns one group, each lane 8 consecutive elements (16-byte loads),
+// so the group amax is a 4-step shuffle inside the half-warp.
 #include "d3_common.cuh"
 #include "d3_host.h"
 #include "d3_internal.h"
@@ -40,38 +41,47 @@ __device__ __forceinline__ float half_warp_max(float v) {
   return v;
 }
 
-// Quantise one bf16 row of G groups (warp-cooperative). scale for group g goes
-// to s[g * s_step].
-__device__ __forceinline__ void quant_row(const __nv_bfloat16* x, int G, uint8_t* q, float* s,
-                                          int64_t s_step) {
+// Quantise groups 2*gp and 2*gp+1 of one bf16 row (warp-cooperative). The
+// scale of group g goes to s[g * s_step].
+__device__ __forceinline__ void quant_pair(const __nv_bfloat16* x, int G, int gp, uint8_t* q,
+                                           float* s, int64_t s_step) {
   const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-  for (int g0 = 0; g0 < G; g0 += 2) {
-    const int g = g0 + half;
-    const bool valid = g < G;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (valid) v = *reinterpret_cast<const uint4*>(x + g * 128 + hl * 8);
-    float f[8];
-    unpack_bf16x8(v, f);
-    float amax = 0.f;
+  const int g = 2 * gp + half;
+  const bool valid = g < G;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + g * 128 + hl * 8));
+  float f[8];
+  unpack_bf16x8(v, f);
+  float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
-    amax = half_warp_max(amax);
-    const float scale = act_scale_from_amax(amax);
-    if (valid) {
-      *reinterpret_cast<uint2*>(q + g * 128 + hl * 8) = quant8(f, scale);
-      if (hl == 0) s[g * s_step] = scale;
-    }
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+  amax = half_warp_max(amax);
+  const float scale = act_scale_from_amax(amax);
+  if (valid) {
+    *reinterpret_cast<uint2*>(q + g * 128 + hl * 8) = quant8(f, scale);
+    if (hl == 0) s[g * s_step] = scale;
   }
+}
+
+// Global warp index -> (row, group pair).
+struct RowPair {
+  int row, gp;
+};
+__device__ __forceinline__ RowPair row_pair(int G) {
+  const int gw = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int GP = (G + 1) / 2;
+  return {gw / GP, gw % GP};
 }
 
 __global__ void quant_act_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                  int H, uint8_t* __restrict__ q, float* __restrict__ scales,
                                  int transposed) {
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  if (row >= T) return;
   const int G = H / 128;
-  float* s = transposed ? scales + row : scales + static_cast<int64_t>(row) * G;
-  quant_row(x + row * x_stride, G, q + static_cast<int64_t>(row) * H, s, transposed ? T : 1);
+  const RowPair rp = row_pair(G);
+  if (rp.row >= T) return;
+  float* s = transposed ? scales + rp.row : scales + static_cast<int64_t>(rp.row) * G;
+  quant_pair(x + rp.row * x_stride, G, rp.gp, q + static_cast<int64_t>(rp.row) * H, s,
+             transposed ? T : 1);
 }
 
 __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
@@ -79,10 +89,12 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
                                int T, int H, int E, const void* row_slots, int slots64,
                                int64_t padding_start, uint8_t* __restrict__ q,
                                float* __restrict__ scales_t, float* __restrict__ logits) {
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  if (row >= T) return;
   const int G = H / 128;
-  quant_row(x + row * x_stride, G, q + static_cast<int64_t>(row) * H, scales_t + row, T);
+  const RowPair rp = row_pair(G);
+  const int row = rp.row;
+  if (row >= T) return;
+  quant_pair(x + row * x_stride, G, rp.gp, q + static_cast<int64_t>(row) * H, scales_t + row, T);
+  if (rp.gp != 0) return;
   int router_row = row;
   if (padding_start > 0 && row_slots) {
     const int64_t slot = slots64 ? static_cast<const int64_t*>(row_slots)[row]
@@ -97,9 +109,10 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
 __global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                     int H, int k, const int32_t* __restrict__ sorted_pairs, int P,
                                     int rows, uint8_t* __restrict__ xq, float* __restrict__ sx) {
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const int G = H / 128;
+  const RowPair rp = row_pair(G);
+  const int row = rp.row;
+  if (row >= rows) return;
   int token;
   if (row < P) {
     const int p = sorted_pairs[row];
@@ -110,50 +123,57 @@ __global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   uint8_t* qrow = xq + static_cast<int64_t>(row) * H;
   float* srow = sx + static_cast<int64_t>(row) * G;
   if (token < 0 || token >= T) {
-    const int lane = threadIdx.x & 31;
-    for (int i = lane; i < H / 16; i += 32) reinterpret_cast<uint4*>(qrow)[i] = make_uint4(0, 0, 0, 0);
-    for (int g = lane; g < G; g += 32) srow[g] = 0.f;
+    const int lane = threadIdx.x & 31, g = 2 * rp.gp + (lane >> 4);
+    if (g < G) {
+      reinterpret_cast<uint2*>(qrow + g * 128)[lane & 15] = make_uint2(0, 0);
+      if ((lane & 15) == 0) srow[g] = 0.f;
+    }
     return;
   }
-  quant_row(x + token * x_stride, G, qrow, srow, 1);
+  quant_pair(x + token * x_stride, G, rp.gp, qrow, srow, 1);
 }
 
 // Exact bf16 -> f16 transfer: each 128-group is multiplied by 2^s with s chosen
 // so that the group amax lands in [2^14, 2^15); the GEMV multiplies by 2^-s.
+// Within each 128-element block, element k is stored at dense_act_position(k)
+// (expert_gemv.cuh).
 __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                       int K, __half* __restrict__ xh, float* __restrict__ inv) {
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  if (row >= T) return;
   const int G = K / 128;
+  const RowPair rp = row_pair(G);
+  const int row = rp.row;
+  if (row >= T) return;
   const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-  for (int g0 = 0; g0 < G; g0 += 2) {
-    const int g = g0 + half;
-    const bool valid = g < G;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (valid) v = *reinterpret_cast<const uint4*>(x + row * x_stride + g * 128 + hl * 8);
-    float f[8];
-    unpack_bf16x8(v, f);
-    float amax = 0.f;
+  const int g = 2 * rp.gp + half;
+  const bool valid = g < G;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + row * x_stride + g * 128 + hl * 8));
+  float f[8];
+  unpack_bf16x8(v, f);
+  float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
-    amax = half_warp_max(amax);
-    int e = 0;
-    if (amax > 0.f && isfinite(amax)) {
-      frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
-      e = 15 - e;        // scaled amax in [2^14, 2^15)
-    }
-    const float mul = ldexpf(1.0f, e);
-    if (valid) {
-      uint32_t h[4];
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+  amax = half_warp_max(amax);
+  int e = 0;
+  if (amax > 0.f && isfinite(amax)) {
+    frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+    e = 15 - e;        // scaled amax in [2^14, 2^15)
+  }
+  const float mul = ldexpf(1.0f, e);
+  if (valid) {
+    uint32_t h[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        __half2 p = __floats2half2_rn(f[2 * i] * mul, f[2 * i + 1] * mul);
-        h[i] = *reinterpret_cast<uint32_t*>(&p);
-      }
-      *reinterpret_cast<uint4*>(xh + static_cast<int64_t>(row) * K + g * 128 + hl * 8) =
-          make_uint4(h[0], h[1], h[2], h[3]);
-      if (hl == 0) inv[static_cast<int64_t>(row) * G + g] = ldexpf(1.0f, -e);
+    for (int i = 0; i < 4; ++i) {
+      __half2 p = __floats2half2_rn(f[2 * i] * mul, f[2 * i + 1] * mul);
+      h[i] = *reinterpret_cast<uint32_t*>(&p);
     }
+    // stored in the bank-conflict-free k order of the GEMV's B fragments
+    // (dense_act_position): this lane's 8 elements stay contiguous
+    const int c = hl >> 1;
+    const int pos = 8 * (8 * (c >> 2) + (c & 3) + 4 * (hl & 1));
+    *reinterpret_cast<uint4*>(xh + static_cast<int64_t>(row) * K + g * 128 + pos) =
+        make_uint4(h[0], h[1], h[2], h[3]);
+    if (hl == 0) inv[static_cast<int64_t>(row) * G + g] = ldexpf(1.0f, -e);
   }
 }
 
@@ -352,6 +372,12 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, 
 
 inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps); }
 
+// CTAs for one warp per (row, group pair).
+inline unsigned pair_blocks(int rows, int cols) {
+  const int64_t warps = static_cast<int64_t>(rows) * ((cols / 128 + 1) / 2);
+  return static_cast<unsigned>((warps + kRowWarps - 1) / kRowWarps);
+}
+
 }  // namespace
 
 void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
@@ -359,7 +385,7 @@ void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
                          float* sx, cudaStream_t s) {
   const int rows = P + (with_shared ? T : 0);
   if (rows <= 0) return;
-  quant_gather_kernel<<<row_blocks(rows), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+  quant_gather_kernel<<<pair_blocks(rows, H), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                        x_stride, T, H, k, sorted_pairs, P, rows,
                                                        xq, sx);
 }
@@ -367,7 +393,7 @@ void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
                            cudaStream_t s) {
   if (T <= 0) return;
-  dense_act_prep_kernel<<<row_blocks(T), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+  dense_act_prep_kernel<<<pair_blocks(T, K), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                       x_stride, T, K, xh, inv);
 }
 
@@ -393,7 +419,7 @@ extern "C" int d3_quant_act_fp8(const void* x, int64_t x_stride, int T, int H, u
   D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "quant_act_fp8: x row stride %lld must be >= H and a multiple of 8", (long long)x_stride);
   D3_REQUIRE(aligned(x, 16) && aligned(q, 16) && aligned(scales, 4), "quant_act_fp8: misaligned pointer");
   if (T == 0) return D3_OK;
-  quant_act_kernel<<<row_blocks(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  quant_act_kernel<<<pair_blocks(T, H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), x_stride, T, H, q, scales, scales_transposed);
   return check_launch("quant_act_fp8");
 }
@@ -409,7 +435,7 @@ extern "C" int d3_prepare_moe_input(const void* x, int64_t x_stride, const void*
   D3_REQUIRE((row_slots == nullptr) == (padding_start <= 0), "prepare_moe_input: reserved padding routing needs both row_slots and padding_start > 0");
   D3_REQUIRE(aligned(x, 16) && aligned(q, 16), "prepare_moe_input: misaligned pointer");
   if (T == 0) return D3_OK;
-  prepare_kernel<<<row_blocks(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  prepare_kernel<<<pair_blocks(T, H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(router),
       router_stride, T, H, E, row_slots, row_slots_int64, padding_start, q, scales_t, logits);
   return check_launch("prepare_moe_input");

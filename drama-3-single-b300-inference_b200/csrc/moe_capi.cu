@@ -99,7 +99,9 @@ template <int EPI, bool ACT_F16, int NCH, int STAGES>
 int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& ta,
                        const EngineArgs& args, int grid, cudaStream_t s) {
   auto kern = expert_gemv_kernel<EPI, ACT_F16, STAGES, NCH>;
-  const size_t smem = EngineSmem<EPI, ACT_F16, STAGES>::bytes(args.KB);
+  constexpr int kGroup = NCH * 8 < kTokensPerGroup ? NCH * 8 : kTokensPerGroup;
+  constexpr int kActRows = kGroup < 16 ? 16 : kGroup;
+  const size_t smem = EngineSmem<EPI, ACT_F16, STAGES, kActRows>::bytes(args.KB, args.num_experts);
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -125,9 +127,11 @@ int launch_engine(int nch, const CUtensorMap& tw, const CUtensorMap& twsh, const
   }
 }
 
-constexpr int kStagesGateUp = 4;
-constexpr int kStagesDown = 6;
-constexpr int kStagesDense = 5;
+// Ring depths: the deepest ring that fits 227 KB of shared memory with E <= 1024
+// experts of routing metadata (gate_up: 36 KB stages, down: 24 KB, dense: 32 KB).
+constexpr int kStagesGateUp = 5;
+constexpr int kStagesDown = 8;
+constexpr int kStagesDense = 6;
 
 int check_experts(const d3_experts_t* e, const char* what) {
   D3_REQUIRE(e != nullptr, "%s: expert weights missing", what);
@@ -143,14 +147,17 @@ int check_experts(const d3_experts_t* e, const char* what) {
 int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
                 int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
                 int64_t gate_stride, void* routed_out, void* shared_out, void* out,
-                const MoeBuffers& b, int32_t* status, cudaStream_t s) {
+                const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted) {
   const int E = ex->E, I = ex->I, H = ex->H;
   const int P = T * k;
   const int has_shared = sh ? 1 : 0;
   const int R = P + (has_shared ? T : 0);
-  int rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, b.sorted, b.tile_experts,
-                          P, b.inv, b.active, b.n_active, s);
-  if (rc) return rc;
+  int rc = D3_OK;
+  if (!permuted) {
+    rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, b.sorted, b.tile_experts, P,
+                        b.inv, b.active, b.n_active, s);
+    if (rc) return rc;
+  }
   launch_quant_gather(x, x_stride, T, H, k, b.sorted, P, has_shared, b.xq, b.sx, s);
   if ((rc = check_launch("quant_gather"))) return rc;
 
@@ -168,6 +175,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.starts = b.starts;
     a.active = b.active;
     a.n_active = b.n_active;
+    a.num_experts = E;
     // gate_up keeps two accumulator sets (gate, up): at most 4 token chunks
     // (32 tokens) per group fit the 168 registers a 9-warp CTA gets
     const int nch = nch_for(T) < 4 ? nch_for(T) : 4;
@@ -177,6 +185,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.shared_count = T;
     a.tiles = I / 128;
     a.KB = H / 128;
+    a.ksplit = 1;
+    a.kb_per_split = a.KB;
     a.rows_per_expert = 2 * I;
     a.up_offset = I;
     a.wscale = ex->s13;
@@ -203,6 +213,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.starts = b.starts;
     a.active = b.active;
     a.n_active = b.n_active;
+    a.num_experts = E;
     const int nch = nch_for(T);
     a.shared_chunk = nch * 8;
     a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
@@ -210,6 +221,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.shared_count = T;
     a.tiles = H / 128;
     a.KB = I / 128;
+    a.ksplit = 1;
+    a.kb_per_split = a.KB;
     a.rows_per_expert = H;
     a.up_offset = 0;
     a.wscale = ex->s2;
@@ -287,7 +300,7 @@ extern "C" int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* id
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   stage_mark(0, s);
   return run_experts(x, x_stride, ids, weights, T, k, experts, shared, nullptr, 0, routed_out,
-                     shared_out, nullptr, b, status ? status : b.status, s);
+                     shared_out, nullptr, b, status ? status : b.status, s, false);
 }
 
 extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w,
@@ -310,19 +323,46 @@ extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_
   stage_mark(0, s);
   launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s);
   if ((rc = check_launch("router_logits"))) return rc;
-  launch_route_topk(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts, D3_DTYPE_BF16, s);
-  if ((rc = check_launch("route_topk"))) return rc;
+  const int P = T * k;
+  rc = launch_route_permute(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts,
+                            D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, b.sorted,
+                            b.tile_experts, P, b.inv, b.active, b.n_active, s);
+  if (rc) return rc;
   return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
-                     nullptr, out, b, status ? status : b.status, s);
+                     nullptr, out, b, status ? status : b.status, s, true);
 }
 
-extern "C" int d3_fp8_gemv_workspace_size(int T, int K, size_t* bytes) {
-  D3_REQUIRE(bytes != nullptr && T >= 0 && K > 0 && K % 128 == 0, "fp8_gemv_workspace_size: bad arguments");
-  Carve c{nullptr};
-  c.take<int32_t>(4);
-  c.take<__half>(static_cast<size_t>(T) * K);
-  c.take<float>(static_cast<size_t>(T) * (K / 128));
-  *bytes = c.off + 256;
+namespace {
+constexpr int kMaxDenseSplit = 8;
+
+struct DenseBuffers {
+  int32_t* status;
+  __half* xh;
+  float* inv;
+  float* partials;
+  int32_t* counters;
+  size_t bytes;
+};
+
+DenseBuffers carve_dense(void* ws, int T, int N, int K) {
+  Carve c{static_cast<uint8_t*>(ws)};
+  const int tiles = (N + 127) / 128;
+  const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
+  DenseBuffers b;
+  b.status = c.take<int32_t>(4);
+  b.xh = c.take<__half>(static_cast<size_t>(T) * K);
+  b.inv = c.take<float>(static_cast<size_t>(T) * (K / 128));
+  b.partials = c.take<float>(static_cast<size_t>(kMaxDenseSplit) * T * tiles * 128);
+  b.counters = c.take<int32_t>(static_cast<size_t>(tiles) * (groups > 0 ? groups : 1));
+  b.bytes = c.off + 256;
+  return b;
+}
+}  // namespace
+
+extern "C" int d3_fp8_gemv_workspace_size(int T, int N, int K, size_t* bytes) {
+  D3_REQUIRE(bytes != nullptr && T >= 0 && N > 0 && K > 0 && K % 128 == 0,
+             "fp8_gemv_workspace_size: bad arguments T=%d N=%d K=%d", T, N, K);
+  *bytes = carve_dense(nullptr, T, N, K).bytes;
   return D3_OK;
 }
 
@@ -334,37 +374,49 @@ extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, c
   D3_REQUIRE(y_stride >= N, "fp8_gemv: y row stride must be >= N");
   D3_REQUIRE(x && wq && s && y && aligned(x, 16) && aligned(wq, 16), "fp8_gemv: null or misaligned pointer");
   D3_REQUIRE(workspace && aligned(workspace, 256), "fp8_gemv: workspace must be 256-byte aligned");
-  size_t need = 0;
-  d3_fp8_gemv_workspace_size(T, K, &need);
-  if (workspace_bytes < need)
-    return set_error(D3_EWORKSPACE, "fp8_gemv: workspace %zu bytes < %zu", workspace_bytes, need);
+  const DenseBuffers need = carve_dense(nullptr, T, N, K);
+  if (workspace_bytes < need.bytes)
+    return set_error(D3_EWORKSPACE, "fp8_gemv: workspace %zu bytes < %zu", workspace_bytes, need.bytes);
   if (T == 0) return D3_OK;
-  Carve c{static_cast<uint8_t*>(workspace)};
-  int32_t* own_status = c.take<int32_t>(4);
-  __half* xh = c.take<__half>(static_cast<size_t>(T) * K);
-  float* inv = c.take<float>(static_cast<size_t>(T) * (K / 128));
+  const DenseBuffers b = carve_dense(workspace, T, N, K);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  launch_dense_act_prep(x, x_stride, T, K, xh, inv, st);
+  const int tiles = (N + 127) / 128, KB = K / 128;
+  const int sms = sm_count();
+  // K splits so that tiles * splits fills about one wave of SMs
+  int split = sms / tiles;
+  split = split < 1 ? 1 : (split > kMaxDenseSplit ? kMaxDenseSplit : split);
+  split = split > KB ? KB : split;
+  const int kbps = (KB + split - 1) / split;
+  split = (KB + kbps - 1) / kbps;
+  if (split > 1) {
+    const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
+    if (cudaMemsetAsync(b.counters, 0, sizeof(int32_t) * tiles * groups, st) != cudaSuccess)
+      return set_error(D3_ECUDA, "fp8_gemv: counter reset failed");
+  }
+  launch_dense_act_prep(x, x_stride, T, K, b.xh, b.inv, st);
   int rc = check_launch("dense_act_prep");
   if (rc) return rc;
   CUtensorMap tw, ta;
   if ((rc = encode_tmap_2d(&tw, wq, 1, K, N, K, 128, 128))) return rc;
-  if ((rc = encode_tmap_2d(&ta, xh, 2, K, T, static_cast<uint64_t>(K) * 2, 64, 16))) return rc;
+  if ((rc = encode_tmap_2d(&ta, b.xh, 2, K, T, static_cast<uint64_t>(K) * 2, 64, 16))) return rc;
   EngineArgs a{};
   a.num_groups = 1;
   a.dense_count = T;
-  a.tiles = (N + 127) / 128;
-  a.KB = K / 128;
+  a.tiles = tiles;
+  a.KB = KB;
+  a.ksplit = split;
+  a.kb_per_split = kbps;
+  a.partials = b.partials;
+  a.tile_counters = b.counters;
   a.rows_per_expert = 0;
   a.wscale = s;
   a.wscale_sh = s;
-  a.act_scale = inv;
+  a.act_scale = b.inv;
   a.out_bf16 = static_cast<__nv_bfloat16*>(y);
   a.out_ld = static_cast<int>(y_stride);
   a.out_cols = N;
-  a.status = status ? status : own_status;
-  const int tiles = a.tiles;
-  const int sms = sm_count();
-  const int grid = tiles < sms ? tiles : sms;
+  a.status = status ? status : b.status;
+  const int items = tiles * split;
+  const int grid = items < sms ? items : sms;
   return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
 }

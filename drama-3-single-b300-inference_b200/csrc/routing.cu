@@ -15,50 +15,77 @@ namespace {
 // in fp32; the 32 lane partials are combined by an xor-butterfly with offsets
 // 16, 8, 4, 2, 1. bf16*bf16 products are exact in fp32, so FMA and
 // multiply-then-add give the same result and the order alone defines the sum.
-// CTA: 8 warps = 8 router rows (one per warp) x 8 tokens staged in smem.
-constexpr int kRouterRows = 8, kRouterTokens = 8;
+// CTA: 8 warps = 8 router rows, each warp holding its weight row in registers
+// and running 4 tokens at a time as independent chains (the order inside each
+// chain is unchanged); x is read through the read-only cache.
+constexpr int kRouterRows = 8, kRouterTokens = 8, kRouterMaxIters = 12;  // H <= 3072
 
-__global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
-                                     const __nv_bfloat16* __restrict__ w,
-                                     const float* __restrict__ bias, int nbias, int R, int H, int T,
-                                     __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+__global__ void __launch_bounds__(256)
+    router_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                         const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
+                         int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
+                         int64_t out_stride) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
-  const int t0 = blockIdx.y * kRouterTokens;
-  const int nt = min(kRouterTokens, T - t0);
-  const int chunks = H / 8;  // 16-byte chunks per row
-  for (int i = threadIdx.x; i < nt * chunks; i += blockDim.x) {
-    const int t = i / chunks, c = i % chunks;
-    reinterpret_cast<uint4*>(xs + t * H)[c] =
-        *reinterpret_cast<const uint4*>(x + (t0 + t) * x_stride + c * 8);
-  }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kRouterRows + warp;
-  if (r >= R) return;
-  const __nv_bfloat16* wr = w + static_cast<int64_t>(r) * H;
+  const int t0 = blockIdx.y * kRouterTokens;
+  const int nt = min(kRouterTokens, T - t0);
   const int iters = (H + 255) / 256;
-  const float b = (bias && r < nbias) ? bias[r] : 0.f;
-  for (int t = 0; t < nt; ++t) {
-    float acc = 0.f;
-    for (int i = 0; i < iters; ++i) {
-      const int k0 = 256 * i + 8 * lane;
-      if (k0 < H) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wr + k0);
-        const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + k0);
-        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+  // weight row into registers first: all of its loads are in flight together
+  uint4 wv[kRouterMaxIters];
+  const __nv_bfloat16* wr = w + static_cast<int64_t>(r < R ? r : 0) * H;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc = fmaf(__uint_as_float(ww[j] << 16), __uint_as_float(xx[j] << 16), acc);
-          acc = fmaf(__uint_as_float(ww[j] & 0xffff0000u), __uint_as_float(xx[j] & 0xffff0000u),
-                     acc);
+  for (int i = 0; i < kRouterMaxIters; ++i) {
+    const int k0 = 256 * i + 8 * lane;
+    wv[i] = (i < iters && k0 < H) ? __ldg(reinterpret_cast<const uint4*>(wr + k0))
+                                  : make_uint4(0, 0, 0, 0);
+  }
+  // the CTA's tokens into shared memory (every thread issues its loads at once)
+  const int chunks = H / 8;
+  for (int idx = threadIdx.x; idx < nt * chunks; idx += blockDim.x) {
+    const int t = idx / chunks, c = idx - t * chunks;
+    reinterpret_cast<uint4*>(xs + t * H)[c] =
+        __ldg(reinterpret_cast<const uint4*>(x + (t0 + t) * x_stride) + c);
+  }
+  __syncthreads();
+  if (r >= R) return;
+  const float b = (bias && r < nbias) ? bias[r] : 0.f;
+  for (int tb = 0; tb < nt; tb += 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kRouterMaxIters; ++i) {
+      const int k0 = 256 * i + 8 * lane;
+      if (i < iters && k0 < H) {
+        uint4 xv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          xv[u] = reinterpret_cast<const uint4*>(xs + (tb + u < nt ? tb + u : 0) * H + k0)[0];
+        const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t xx[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc[u] = fmaf(__uint_as_float(ww[j] << 16), __uint_as_float(xx[j] << 16), acc[u]);
+            acc[u] = fmaf(__uint_as_float(ww[j] & 0xffff0000u),
+                          __uint_as_float(xx[j] & 0xffff0000u), acc[u]);
+          }
         }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) out[(t0 + t) * out_stride + r] = __float2bfloat16_rn(acc + b);
+    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+    }
+    if (lane < 4 && tb + lane < nt) {
+      float v = acc[0];
+#pragma unroll
+      for (int u = 1; u < 4; ++u)
+        if (lane == u) v = acc[u];
+      out[(t0 + tb + lane) * out_stride + r] = __float2bfloat16_rn(v + b);
+    }
   }
 }
 
@@ -76,12 +103,15 @@ __device__ __forceinline__ uint64_t route_key(float v, int col) {
   return (static_cast<uint64_t>(ordered) << 32) | static_cast<uint32_t>(0xffffffffu - col);
 }
 
+// Routes token t with the calling warp. Lane j < k ends with pick j; the ids
+// (int64), weights and, when ids_smem != nullptr, an int32 copy of the ids are
+// written out.
 template <int PER_LANE>
-__global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T,
-                             int E, int k, const float* __restrict__ bias,
-                             int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (t >= T) return;
+__device__ __forceinline__ void route_token(const void* __restrict__ logits, int f32_in,
+                                            int64_t stride, int t, int E, int k,
+                                            const float* __restrict__ bias,
+                                            int64_t* __restrict__ ids, void* __restrict__ weights,
+                                            int f32_out, int* ids_smem) {
   const int lane = threadIdx.x & 31;
   float v[PER_LANE];
   uint64_t key[PER_LANE];
@@ -142,6 +172,7 @@ __global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_
   for (int j = 0; j < k; ++j) psum += __shfl_sync(0xffffffffu, p, j);
   if (lane < k) {
     ids[static_cast<int64_t>(t) * k + lane] = sel_col;
+    if (ids_smem) ids_smem[t * k + lane] = sel_col;
     const float wgt = p / psum;
     if (f32_out)
       static_cast<float*>(weights)[static_cast<int64_t>(t) * k + lane] = wgt;
@@ -149,6 +180,15 @@ __global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_
       static_cast<__nv_bfloat16*>(weights)[static_cast<int64_t>(t) * k + lane] =
           __float2bfloat16_rn(wgt);
   }
+}
+
+template <int PER_LANE>
+__global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T,
+                             int E, int k, const float* __restrict__ bias,
+                             int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  route_token<PER_LANE>(logits, f32_in, stride, t, E, k, bias, ids, weights, f32_out, nullptr);
 }
 
 // ---------------------------------------------------------------- permute --
@@ -187,14 +227,17 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int& t
   return excl;
 }
 
-__global__ void __launch_bounds__(kPermuteThreads)
-    permute_kernel(const int64_t* __restrict__ ids, int P, int E, int bm,
-                   int32_t* __restrict__ counts, int32_t* __restrict__ starts,
-                   int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
-                   int32_t* __restrict__ expert_ids, int64_t max_rows,
-                   int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
-                   int32_t* __restrict__ n_active) {
-  extern __shared__ int sm[];
+// id_at(p) returns the expert of pair p, or -1 for an id outside [0, E).
+template <typename IdAt>
+__device__ __forceinline__ void permute_body(IdAt id_at, int P, int E, int bm, int* sm,
+                                             int32_t* __restrict__ counts,
+                                             int32_t* __restrict__ starts,
+                                             int32_t* __restrict__ total_out,
+                                             int32_t* __restrict__ sorted_ids,
+                                             int32_t* __restrict__ expert_ids, int64_t max_rows,
+                                             int32_t* __restrict__ inv_rows,
+                                             int32_t* __restrict__ active,
+                                             int32_t* __restrict__ n_active) {
   int* cnt = sm;              // [E]
   int* start = cnt + E;       // [E]
   int* cursor = start + E;    // [E]
@@ -205,8 +248,8 @@ __global__ void __launch_bounds__(kPermuteThreads)
   for (int i = tid; i < 32 * E; i += kPermuteThreads) wcnt[i] = 0;
   __syncthreads();
   for (int p = tid; p < P; p += kPermuteThreads) {
-    const int64_t e = ids[p];
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    const int e = id_at(p);
+    if (e >= 0) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
   int total = 0;
@@ -220,11 +263,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
   __syncthreads();
   for (int base = 0; base < P; base += kPermuteThreads) {
     const int p = base + tid;
-    int e = -1;
-    if (p < P) {
-      const int64_t v = ids[p];
-      e = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
-    }
+    const int e = p < P ? id_at(p) : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank = __popc(peers & ((1u << lane) - 1u));
     const bool leader = rank == 0;
@@ -270,6 +309,47 @@ __global__ void __launch_bounds__(kPermuteThreads)
   }
 }
 
+__global__ void __launch_bounds__(kPermuteThreads)
+    permute_kernel(const int64_t* __restrict__ ids, int P, int E, int bm,
+                   int32_t* __restrict__ counts, int32_t* __restrict__ starts,
+                   int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
+                   int32_t* __restrict__ expert_ids, int64_t max_rows,
+                   int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
+                   int32_t* __restrict__ n_active) {
+  extern __shared__ int sm[];
+  auto id_at = [&](int p) -> int {
+    const int64_t v = ids[p];
+    return (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+  };
+  permute_body(id_at, P, E, bm, sm, counts, starts, total_out, sorted_ids, expert_ids, max_rows,
+               inv_rows, active, n_active);
+}
+
+// Decode-size fusion of route_topk and permute in one CTA: the ids never leave
+// shared memory between the two. T*k <= kFusedMaxPairs.
+constexpr int kFusedMaxPairs = 4096;
+
+template <int PER_LANE>
+__global__ void __launch_bounds__(kPermuteThreads)
+    route_permute_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T, int E,
+                         int k, const float* __restrict__ bias, int64_t* __restrict__ ids,
+                         void* __restrict__ weights, int f32_out, int bm,
+                         int32_t* __restrict__ counts, int32_t* __restrict__ starts,
+                         int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
+                         int32_t* __restrict__ expert_ids, int64_t max_rows,
+                         int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
+                         int32_t* __restrict__ n_active) {
+  extern __shared__ int sm[];
+  int* ids_s = sm;                     // [kFusedMaxPairs]
+  int* work = sm + kFusedMaxPairs;     // permute scratch
+  for (int t = threadIdx.x >> 5; t < T; t += kPermuteThreads / 32)
+    route_token<PER_LANE>(logits, f32_in, stride, t, E, k, bias, ids, weights, f32_out, ids_s);
+  __syncthreads();
+  auto id_at = [&](int p) -> int { return ids_s[p]; };
+  permute_body(id_at, T * k, E, bm, work, counts, starts, total_out, sorted_ids, expert_ids,
+               max_rows, inv_rows, active, n_active);
+}
+
 }  // namespace
 
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
@@ -277,7 +357,7 @@ void launch_router_logits(const void* x, int64_t x_stride, const void* w, const 
                           cudaStream_t s) {
   if (T <= 0 || R <= 0) return;
   dim3 grid((R + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
-  const size_t smem = static_cast<size_t>(kRouterTokens) * H * 2;
+  const size_t smem = static_cast<size_t>(kRouterTokens) * H * 2;  // <= 48 KB for H <= 3072
   router_logits_kernel<<<grid, 256, smem, s>>>(
       static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
       nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
@@ -296,6 +376,42 @@ void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int
     route_kernel<8><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
   else
     route_kernel<kMaxPerLane><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+}
+
+int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, int T, int E,
+                         int k, const float* bias, int64_t* ids, void* weights, int weights_dtype,
+                         int block_m, int32_t* counts, int32_t* starts, int32_t* total,
+                         int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
+                         int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s) {
+  if (T <= 0) return D3_OK;
+  if (static_cast<int64_t>(T) * k > kFusedMaxPairs) {
+    launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype, s);
+    int rc = check_launch("route_topk");
+    if (rc) return rc;
+    return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
+                          max_rows, inv_rows, active, n_active, s);
+  }
+  const size_t smem = (static_cast<size_t>(kFusedMaxPairs) + static_cast<size_t>(E) * 35) * sizeof(int);
+  const int f32_in = logits_dtype == D3_DTYPE_F32, f32_out = weights_dtype == D3_DTYPE_F32;
+  const int per_lane = (E + 31) / 32;
+  auto launch = [&](auto kern) -> int {
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && configured[dev] < static_cast<int>(smem)) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return set_error(D3_ECUDA, "route_permute: cannot raise the shared-memory limit");
+      configured[dev] = static_cast<int>(smem);
+    }
+    kern<<<1, kPermuteThreads, smem, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights,
+                                          f32_out, block_m, counts, starts, total, sorted_ids,
+                                          expert_ids, max_rows, inv_rows, active, n_active);
+    return check_launch("route_permute");
+  };
+  if (per_lane <= 4) return launch(route_permute_kernel<4>);
+  if (per_lane <= 8) return launch(route_permute_kernel<8>);
+  return launch(route_permute_kernel<kMaxPerLane>);
 }
 
 int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
@@ -325,15 +441,10 @@ using namespace d3;
 extern "C" int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H,
                                 int T, void* logits, int64_t logits_stride, d3_stream_t stream) {
   D3_REQUIRE(T >= 0 && R > 0 && H > 0 && H % 128 == 0, "router_logits: bad shape R=%d H=%d", R, H);
-  D3_REQUIRE(H <= 16384, "router_logits: H=%d above the 16384 this kernel stages in shared memory", H);
+  D3_REQUIRE(H <= 256 * kRouterMaxIters, "router_logits: H=%d above the %d this kernel holds in registers", H, 256 * kRouterMaxIters);
   D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "router_logits: x row stride must be >= H and a multiple of 8");
   D3_REQUIRE(logits_stride >= R, "router_logits: logits row stride must be >= R");
   D3_REQUIRE(aligned(x, 16) && aligned(w, 16), "router_logits: misaligned pointer");
-  if (H * 16 > 48 * 1024) {
-    if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             H * 16) != cudaSuccess)
-      return set_error(D3_ECUDA, "router_logits: cannot raise the shared-memory limit");
-  }
   launch_router_logits(x, x_stride, w, nullptr, 0, R, H, T, logits, logits_stride,
                        reinterpret_cast<cudaStream_t>(stream));
   return check_launch("router_logits");

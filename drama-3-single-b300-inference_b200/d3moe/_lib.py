@@ -67,7 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "d3_silu_mul_quant": (_i32, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_combine_experts": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p]),
     "d3_fp8_quantize_weight": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
-    "d3_fp8_gemv_workspace_size": (_i32, [_i32, _i32, ctypes.POINTER(_size_t)]),
+    "d3_fp8_gemv_workspace_size": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_size_t)]),
     "d3_fp8_gemv": (
         _i32,
         [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _i64,

@@ -206,7 +206,7 @@ def fp8_gemv(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, n: int | N
     if out is None:
         out = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
     nbytes = ctypes.c_size_t()
-    call("d3_fp8_gemv_workspace_size", T, K, ctypes.byref(nbytes))
+    call("d3_fp8_gemv_workspace_size", T, N, K, ctypes.byref(nbytes))
     ws = torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
     call("d3_fp8_gemv", x.data_ptr(), _row_stride(x), wq.data_ptr(), scales.data_ptr(), T, N, K,
          out.data_ptr(), out.stride(0), ws.data_ptr(), nbytes.value, None, _stream(x.device))

@@ -147,8 +147,10 @@ D3_API int d3_fp8_quantize_weight(const void* w, int N, int K, uint8_t* q, float
  * bf16 activations (weight-only FP8, the arithmetic of experimental_fp8._gemv,
  * experimental_fp8.py:21-29, for every T). Wq e4m3 [>=N, K], S f32
  * [cdiv(N,128), K/128]. Needs workspace of d3_fp8_gemv_workspace_size bytes.
+ * Small N is split along K over several CTAs; the fp32 partial sums are added
+ * in a fixed split order, so results are deterministic.
  * status (device int32, may be NULL) receives D3_STATUS_*. */
-D3_API int d3_fp8_gemv_workspace_size(int T, int K, size_t* bytes);
+D3_API int d3_fp8_gemv_workspace_size(int T, int N, int K, size_t* bytes);
 D3_API int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const float* s, int T, int N,
                 int K, void* y, int64_t y_stride, void* workspace, size_t workspace_bytes,
                 int32_t* status, d3_stream_t stream);

@@ -320,12 +320,15 @@ def combine_experts(routed, shared, gate):
 
 
 def fp8_gemv(x, wq, scales, n=None):
-    """src/drama3/experimental_fp8.py:21-29 (_gemv): y = sum_k w*scale*x in
-    fp32 with bf16 activations (no activation quantisation), stored bf16."""
+    """src/drama3/experimental_fp8.py:21-29 (_gemv): y = sum_k w*scale*x with
+    bf16 activations (no activation quantisation), stored bf16. The sum is
+    taken in float64 so the oracle returns the correctly rounded value that
+    any fp32 summation order approximates."""
     wd = dequant_blocks(np.asarray(wq), np.asarray(scales))
     if n is not None:
         wd = wd[:n]
-    return bf16_round(np.asarray(x, dtype=np.float32) @ wd.T)
+    y = np.asarray(x, dtype=np.float64) @ wd.T.astype(np.float64)
+    return bf16_round(y.astype(np.float32))
 
 
 # ------------------------------------------------------------ whole layer --

@@ -58,9 +58,9 @@ def test_workspace_sizes_are_host_only(lib):
     assert n.value >= R * 2048 + R * 768 + R * 2048 * 4
     assert lib.d3_moe_workspace_size(0, 8, 128, 768, 2048, 1, ctypes.byref(n)) == 0
     assert lib.d3_moe_workspace_size(-1, 8, 128, 768, 2048, 1, ctypes.byref(n)) == _lib.D3_EINVAL
-    assert lib.d3_fp8_gemv_workspace_size(64, 2048, ctypes.byref(n)) == 0
+    assert lib.d3_fp8_gemv_workspace_size(64, 4096, 2048, ctypes.byref(n)) == 0
     assert n.value >= 64 * 2048 * 2
-    assert lib.d3_fp8_gemv_workspace_size(64, 100, ctypes.byref(n)) == _lib.D3_EINVAL
+    assert lib.d3_fp8_gemv_workspace_size(64, 4096, 100, ctypes.byref(n)) == _lib.D3_EINVAL
 
 
 def test_invalid_arguments_fail_before_launch(lib):
