@@ -269,10 +269,14 @@ def main() -> None:
                   out.data_ptr(), out.stride(0), ws_dense.data_ptr(), ws_dense.numel(),
                   status.data_ptr(), sptr)
 
-    def step(i: int, x: torch.Tensor, ids_buf):
+    def step(i: int, x: torch.Tensor, ids_buf, dense_events=None):
         li = i % args.layers
         wq, sq, wo_, so_ = dense[li]
+        if dense_events:
+            dense_events[0].record(stream)
         gemv(x, x.stride(0), wq, sq, N_QKV, qkv)
+        if dense_events:
+            dense_events[1].record(stream)
         gemv(qkv, qkv.stride(0), wo_, so_, N_O, o)  # first 2048 columns of qkv, row stride 4096
         lw = layers[li]
         ev, sv = views[li]
@@ -281,7 +285,8 @@ def main() -> None:
                   None if ids_buf is None else ids_buf.data_ptr(), wts.data_ptr(),
                   ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), sptr)
 
-    launches_per_step = 2 * 2 + 7  # (act prep + engine) x 2 GEMVs; router, route, permute, gather, gate_up, down, combine
+    # (act prep + engine) x 2 GEMVs; router, route+permute, gather, gate_up, down, combine
+    launches_per_step = 2 * 2 + 6
 
     # per-step stage events (gate_up / down engine launches) inside the timed region
     stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
@@ -289,6 +294,7 @@ def main() -> None:
         for e in evs:
             e.record(stream)  # materialise the cudaEvent_t handles
     stage_arrays = [(ctypes.c_void_p * 5)(*[e._as_parameter_.value for e in evs]) for evs in stage_events]
+    dense_events = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
 
     for i in range(args.warmup):
         step(i, xs[i % len(xs)], None)
@@ -301,7 +307,7 @@ def main() -> None:
         start.record(stream)
         for i in range(args.steps):
             lib.d3_set_stage_events(stage_arrays[i], 5)
-            step(args.warmup + i, xs[(args.warmup + i) % len(xs)], ids_all[i])
+            step(args.warmup + i, xs[(args.warmup + i) % len(xs)], ids_all[i], dense_events[i])
             lib.d3_set_stage_events(None, 0)
         end.record(stream)
         torch.cuda.synchronize(dev)
@@ -311,6 +317,10 @@ def main() -> None:
     gate_ms = [evs[1].elapsed_time(evs[2]) for evs in stage_events]
     down_ms = [evs[2].elapsed_time(evs[3]) for evs in stage_events]
     moe_ms = [evs[0].elapsed_time(evs[4]) for evs in stage_events]
+    qkv_ms = [de[0].elapsed_time(de[1]) for de in dense_events]
+    oproj_ms = [de[1].elapsed_time(se[0]) for de, se in zip(dense_events, stage_events)]
+    pre_ms = [se[0].elapsed_time(se[1]) for se in stage_events]
+    post_ms = [se[3].elapsed_time(se[4]) for se in stage_events]
     ids_host = ids_all.cpu().numpy()
     if int(status.item()) != 0:
         raise RuntimeError(f"device status word {int(status.item())}: a bounded wait timed out")
@@ -387,6 +397,9 @@ def main() -> None:
             "down_kernel": {"achieved": down_bytes / (down_avg * 1e-3) / 1e9, "avg_launch_ms": down_avg,
                             "algorithmic_bytes_per_launch": down_bytes},
             "moe_layer_ms": statistics.mean(moe_ms),
+            "stage_ms": {"qkv_gemv": statistics.mean(qkv_ms), "o_proj_gemv": statistics.mean(oproj_ms),
+                         "router_route_permute_gather": statistics.mean(pre_ms),
+                         "gate_up": gate_avg, "down": down_avg, "combine": statistics.mean(post_ms)},
             "step_bytes": total_bytes,
             "step_achieved_gbs": total_bytes / (ms * 1e-3) / 1e9,
             "mean_active_experts": statistics.mean(p["U"] for p in per_step),
