@@ -8,6 +8,8 @@
 //   4. down         engine EPI_DOWN:    d f32 [R, H]
 //   5. combine      routed/shared/out bf16 [T, H] in fixed rank order
 // All buffers live in the caller's workspace; nothing is allocated here.
+#include <mutex>
+
 #include "d3_host.h"
 #include "d3_internal.h"
 #include "expert_gemv.cuh"
@@ -417,6 +419,120 @@ extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, c
   a.out_cols = N;
   a.status = status ? status : b.status;
   const int items = tiles * split;
+  const int grid = items < sms ? items : sms;
+  return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
+}
+
+// --------------------------------------------------------------------------
+// Weight-only FP8 GEMV for callers that cannot allocate device memory.
+//
+// d3_fp8_gemv needs a caller-provided workspace (the f16 copy of x, its
+// per-group scales and the split-K partial sums). Some callers have no way to
+// provide one: a host runtime that gives a plugin only its input and output
+// buffers and a stream, and does not let it grow device memory while a request
+// is in flight, because an allocation there can synchronise the device or fail
+// under memory pressure. This variant keeps that scratch in a fixed array in
+// the library's own device memory instead. Each GPU that loads the library
+// holds the array (D3_GEMV_NOALLOC_SCRATCH_BYTES) until the process exits.
+// Its address is looked up once per device (cudaGetSymbolAddress, with that
+// device current) on the first call; that first call should therefore come
+// before any stream capture. All calls share the array: the split-K counters
+// are cleared at the start of each call, and two calls whose work overlaps on
+// the GPU (different streams, or different host threads) race on it.
+namespace {
+constexpr int kNoAllocSplit = 4;
+constexpr size_t kNoAllocXhBytes =
+    static_cast<size_t>(D3_GEMV_NOALLOC_MAX_T) * D3_GEMV_NOALLOC_MAX_K * 2;
+constexpr size_t kNoAllocInvBytes =
+    static_cast<size_t>(D3_GEMV_NOALLOC_MAX_T) * (D3_GEMV_NOALLOC_MAX_K / 128) * 4;
+constexpr size_t kNoAllocPartialBytes = static_cast<size_t>(kNoAllocSplit) *
+                                        D3_GEMV_NOALLOC_MAX_T * D3_GEMV_NOALLOC_MAX_N * 4;
+constexpr size_t kNoAllocCounterBytes = (D3_GEMV_NOALLOC_MAX_N / 128) * 4;
+// layout: [status 256][xh][inv][partials][counters], each 256-byte aligned
+constexpr size_t kNoAllocXhOff = 256;
+constexpr size_t kNoAllocInvOff = kNoAllocXhOff + kNoAllocXhBytes;
+constexpr size_t kNoAllocPartOff = kNoAllocInvOff + ((kNoAllocInvBytes + 255) / 256) * 256;
+constexpr size_t kNoAllocCntOff = kNoAllocPartOff + kNoAllocPartialBytes;
+static_assert(kNoAllocCntOff + kNoAllocCounterBytes <= D3_GEMV_NOALLOC_SCRATCH_BYTES,
+              "scratch array too small for the stated limits");
+
+static __device__ __align__(256) uint8_t g_gemv_noalloc_scratch[D3_GEMV_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[64] = {nullptr};
+
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(D3_ECUDA, "fp8_gemv_noalloc: no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(D3_ECUDA, "fp8_gemv_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_addr[dev]);
+  return D3_OK;
+}
+}  // namespace
+
+extern "C" int d3_fp8_gemv_noalloc(const void* x, int64_t x_stride, const uint8_t* wq,
+                                   const float* s, int T, int N, int K, void* y,
+                                   int64_t y_stride, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && N > 0 && K > 0 && K % 128 == 0, "fp8_gemv_noalloc: bad shape T=%d N=%d K=%d", T, N, K);
+  D3_REQUIRE(T <= D3_GEMV_NOALLOC_MAX_T && N <= D3_GEMV_NOALLOC_MAX_N && K <= D3_GEMV_NOALLOC_MAX_K,
+             "fp8_gemv_noalloc: T=%d N=%d K=%d exceeds the fixed scratch limits T<=%d N<=%d K<=%d; "
+             "use d3_fp8_gemv with a workspace", T, N, K, D3_GEMV_NOALLOC_MAX_T,
+             D3_GEMV_NOALLOC_MAX_N, D3_GEMV_NOALLOC_MAX_K);
+  D3_REQUIRE(x_stride >= K && x_stride % 8 == 0, "fp8_gemv_noalloc: x row stride must be >= K and a multiple of 8");
+  D3_REQUIRE(y_stride >= N, "fp8_gemv_noalloc: y row stride must be >= N");
+  D3_REQUIRE(x && wq && s && y && aligned(x, 16) && aligned(wq, 16), "fp8_gemv_noalloc: null or misaligned pointer");
+  uint8_t* base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  if (T == 0) return D3_OK;
+  int32_t* status = reinterpret_cast<int32_t*>(base);
+  __half* xh = reinterpret_cast<__half*>(base + kNoAllocXhOff);
+  float* inv = reinterpret_cast<float*>(base + kNoAllocInvOff);
+  float* partials = reinterpret_cast<float*>(base + kNoAllocPartOff);
+  int32_t* counters = reinterpret_cast<int32_t*>(base + kNoAllocCntOff);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int tiles = (N + 127) / 128, KB = K / 128;
+  int split = sm_count() / tiles;
+  split = split < 1 ? 1 : (split > kNoAllocSplit ? kNoAllocSplit : split);
+  split = split > KB ? KB : split;
+  const int kbps = (KB + split - 1) / split;
+  split = (KB + kbps - 1) / kbps;
+  // the counters and status word left by the previous call are cleared here
+  if (cudaMemsetAsync(counters, 0, kNoAllocCounterBytes, st) != cudaSuccess ||
+      cudaMemsetAsync(status, 0, sizeof(int32_t), st) != cudaSuccess)
+    return set_error(D3_ECUDA, "fp8_gemv_noalloc: clearing the scratch counters failed");
+  launch_dense_act_prep(x, x_stride, T, K, xh, inv, st);
+  if ((rc = check_launch("dense_act_prep"))) return rc;
+  CUtensorMap tw, ta;
+  if ((rc = encode_tmap_2d(&tw, wq, 1, K, N, K, 128, 128))) return rc;
+  if ((rc = encode_tmap_2d(&ta, xh, 2, K, T, static_cast<uint64_t>(K) * 2, 64, 16))) return rc;
+  EngineArgs a{};
+  a.num_groups = 1;
+  a.dense_count = T;
+  a.tiles = tiles;
+  a.KB = KB;
+  a.ksplit = split;
+  a.kb_per_split = kbps;
+  a.partials = partials;
+  a.tile_counters = counters;
+  a.wscale = s;
+  a.wscale_sh = s;
+  a.act_scale = inv;
+  a.out_bf16 = static_cast<__nv_bfloat16*>(y);
+  a.out_ld = static_cast<int>(y_stride);
+  a.out_cols = N;
+  a.status = status;
+  const int items = tiles * split;
+  const int sms = sm_count();
   const int grid = items < sms ? items : sms;
   return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
 }

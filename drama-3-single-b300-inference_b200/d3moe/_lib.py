@@ -73,6 +73,10 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _i64,
          _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
+    "d3_fp8_gemv_noalloc": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _i64, _c_void_p],
+    ),
     "d3_moe_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_size_t)]),
     "d3_moe_experts": (
         _i32,

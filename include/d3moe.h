@@ -155,6 +155,25 @@ D3_API int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const
                 int K, void* y, int64_t y_stride, void* workspace, size_t workspace_bytes,
                 int32_t* status, d3_stream_t stream);
 
+/* The same weight-only FP8 GEMV for callers that cannot allocate device
+ * memory, and so cannot pass a workspace: for example a host runtime that
+ * hands a plugin only its inputs, outputs and a stream and does not let it
+ * allocate while a request runs. No counterpart in the reference.
+ * Scratch lives in a fixed array inside the library (D3_GEMV_NOALLOC_SCRATCH_BYTES
+ * on every GPU that loads it, held until the process exits). Limits: T <= 64,
+ * N <= 4096, K <= 4096; larger sizes return D3_EINVAL. Nothing is allocated.
+ * The first call on a device looks up the array's device address (once per
+ * device), so make that first call before any stream capture. All calls share
+ * the array: calls whose GPU work overlaps (other streams or host threads)
+ * race on it and must be serialised by the caller. */
+#define D3_GEMV_NOALLOC_MAX_T 64
+#define D3_GEMV_NOALLOC_MAX_N 4096
+#define D3_GEMV_NOALLOC_MAX_K 4096
+#define D3_GEMV_NOALLOC_SCRATCH_BYTES (5u << 20) /* 5 MiB */
+D3_API int d3_fp8_gemv_noalloc(const void* x, int64_t x_stride, const uint8_t* wq, const float* s,
+                               int T, int N, int K, void* y, int64_t y_stride,
+                               d3_stream_t stream);
+
 /* --------------------------------------------- (a5-a8) routed experts --
  * Expert weights of one MoE layer (reference container: experts.w13_weight,
  * w13_scale_inv, w2_weight, w2_scale_inv; src/drama3/kernels.py:336-350).

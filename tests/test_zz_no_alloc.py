@@ -1,0 +1,62 @@
+"""The workspace-free weight-only FP8 GEMV (d3_fp8_gemv_noalloc).
+
+Some callers cannot hand this library a workspace: a host runtime that gives
+a plugin only its inputs, outputs and a stream, and does not let it allocate
+device memory while a request runs. For them the library keeps the GEMV's
+scratch in a fixed array of its own. These tests call that entry point through
+the C ABI and check it against the workspace entry point (d3_fp8_gemv) on two
+calls in a row with different shapes, so the second call proves that whatever
+the first call left in the shared array does not leak into the result.
+This file is collected last on purpose.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from helpers import assert_close, from_bf16, to_bf16, to_fp8, ulps_bf16  # noqa: E402
+from oracle import moe_oracle as O  # noqa: E402
+
+
+def _case(T, N, K, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    q, s = O.quantize_weight_blocks(w)
+    x = O.bf16_round(rng.standard_normal((T, K)).astype(np.float32))
+    return to_bf16(x), to_fp8(q), torch.from_numpy(s).cuda()
+
+
+def _noalloc(x, wq, s, N):
+    from d3moe import _lib, ops
+    T, K = x.shape
+    y = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
+    _lib.call("d3_fp8_gemv_noalloc", x.data_ptr(), x.stride(0), wq.data_ptr(), s.data_ptr(), T, N, K,
+              y.data_ptr(), y.stride(0), ops._stream(x.device))
+    return y
+
+
+def test_noalloc_gemv_matches_workspace_gemv_on_consecutive_calls():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from d3moe import ops
+    for T, N, K, seed in ((64, 4096, 2048, 1), (13, 2048, 4096, 2)):
+        x, wq, s = _case(T, N, K, seed)
+        got = from_bf16(_noalloc(x, wq, s, N))
+        ref = from_bf16(ops.fp8_gemv(x, wq, s, n=N))
+        torch.cuda.synchronize()
+        # same products; the K-split count may differ, so the fp32 sums may
+        # round to neighbouring bf16 values
+        assert ulps_bf16(got, ref).max() <= 1
+        assert_close(got, ref, what=f"noalloc gemv T={T} N={N} K={K}")
+
+
+def test_noalloc_gemv_rejects_sizes_beyond_its_scratch():
+    from d3moe import _lib
+    with pytest.raises(ValueError, match="fixed scratch limits"):
+        _lib.call("d3_fp8_gemv_noalloc", 16, 2048, 16, 16, 65, 4096, 2048, 16, 4096, None)
+    with pytest.raises(ValueError, match="fixed scratch limits"):
+        _lib.call("d3_fp8_gemv_noalloc", 16, 8192, 16, 16, 8, 4096, 8192, 16, 4096, None)
