@@ -202,6 +202,181 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_ep(args, world: int, rank: int, local: int, dev) -> None:
+    """N > 1: the expert-parallel layer (d3moe.ep) with 128/N experts per rank
+    and `--tokens` decode tokens per rank (weak scaling), after the replicated
+    dense QKV / o_proj GEMVs. Dispatch and combine are NCCL all_to_all_v over
+    NVLink; the time is the max over ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from d3moe import _lib, ops, synth
+    from d3moe.ep import CudaEPOps, ExpertParallelMoE
+
+    T = args.tokens
+    lib = _lib.load()
+    E_local = E // world
+    stage = {"events": None}
+
+    class TimedOps(CudaEPOps):
+        """Records the stage events around this rank's routed-expert launches."""
+
+        def local_experts_k(self, rows, ids, weights, experts):
+            if stage["events"] is not None:
+                lib.d3_set_stage_events(stage["events"], 5)
+            try:
+                return super().local_experts_k(rows, ids, weights, experts)
+            finally:
+                lib.d3_set_stage_events(None, 0)
+
+    eops = TimedOps()
+    layers, dense = [], []
+    for li in range(args.layers):
+        gen = torch.Generator(device="cpu")
+        gen.manual_seed(li)
+        router = (torch.randn((E + 1, H), generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+        experts = synth.make_experts(E_local, I, H, 1000 * li + 7 + rank, dev)
+        shared = synth.make_experts(1, I, H, 1000 * li + 3, dev)
+        layers.append(ExpertParallelMoE(router, experts, shared, E, TOPK, ops=eops))
+        g = torch.Generator(device=dev)
+        g.manual_seed(li + 77)
+        wq, sq = synth.block_quantize(torch.randn((N_QKV, H), generator=g, device=dev) * 0.02)
+        wo, so = synth.block_quantize(torch.randn((N_O, H), generator=g, device=dev) * 0.02)
+        dense.append((wq, sq, wo, so))
+    nb = ctypes.c_size_t()
+    lib.d3_fp8_gemv_workspace_size(T, N_QKV, H, ctypes.byref(nb))
+    ws_dense = torch.empty(nb.value, dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    gin = torch.Generator(device=dev)
+    gin.manual_seed(4242 + rank)
+    xs = torch.randn((8, T, H), generator=gin, device=dev).to(torch.bfloat16)
+    qkv = torch.empty((T, N_QKV), dtype=torch.bfloat16, device=dev)
+    o = torch.empty((T, N_O), dtype=torch.bfloat16, device=dev)
+
+    def gemv(x, wq, sq, n, out):
+        _lib.call("d3_fp8_gemv", x.data_ptr(), x.stride(0), wq.data_ptr(), sq.data_ptr(), T, n, H,
+                  out.data_ptr(), out.stride(0), ws_dense.data_ptr(), ws_dense.numel(),
+                  status.data_ptr(), sptr)
+
+    ids_seen = []
+
+    def step(i, x, keep_ids=False):
+        li = i % args.layers
+        wq, sq, wo_, so_ = dense[li]
+        gemv(x, wq, sq, N_QKV, qkv)
+        gemv(qkv, wo_, so_, N_O, o)
+        out, ids, _ = layers[li].forward(o, return_routing=True)
+        if keep_ids:
+            ids_seen.append(ids)
+        return out
+
+    for i in range(args.warmup):
+        step(i, xs[i % len(xs)])
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    for evs in stage_events:
+        for e in evs:
+            e.record(stream)
+    stage_arrays = [(ctypes.c_void_p * 5)(*[e._as_parameter_.value for e in evs]) for evs in stage_events]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            stage["events"] = stage_arrays[i]
+            step(args.warmup + i, xs[(args.warmup + i) % len(xs)], keep_ids=True)
+        stage["events"] = None
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    gate_avg = statistics.mean(evs[1].elapsed_time(evs[2]) for evs in stage_events)
+    down_avg = statistics.mean(evs[2].elapsed_time(evs[3]) for evs in stage_events)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # experts this rank streamed per step: distinct global ids it owns, over all ranks' tokens
+    gathered = [torch.empty_like(ids_seen[0]) for _ in range(world)]
+    U_local = []
+    for ids in ids_seen:
+        dist.all_gather(gathered, ids)
+        allids = torch.cat(gathered).cpu().numpy()
+        mine = allids[(allids // E_local) == rank]
+        U_local.append(len(np.unique(mine)))
+    u = statistics.mean(U_local)
+
+    # end to end with host buffers
+    hx = torch.randn((T, H)).to(torch.bfloat16).pin_memory()
+    hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    for i in range(2):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(step(i, dx), non_blocking=True)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(step(i, dx), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([e2e_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+
+    pk = peaks()
+    w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
+    rows = T * world  # token rows received per rank (capacity mode: every token once)
+    gate_bytes = u * w13 + rows * TOPK * (H + I)
+    achieved = gate_bytes / (gate_avg * 1e-3) / 1e9
+    line = {
+        "metric": "fp8_moe_layer_decode_tokens_per_s",
+        "value": T * world / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8_e4m3 x fp8_e4m3 -> f32 (experts); fp8 weights x bf16 (dense)",
+        "data": "synthetic",
+        "config": {
+            "workload": f"decode T={T}/GPU: FP8 QKV + o_proj weight-only GEMV + expert-parallel MoE layer "
+                        f"(H=2048, E=128 sharded {E_local}/GPU, I=768, top-8, shared expert replicated)",
+            "tokens_per_gpu": T, "weight_sets_rotated": args.layers,
+            "l2": "inputs larger than L2: weight sets rotated per step",
+            "parallelism": f"ep{world}",
+            "collective": "NCCL all_to_all_single, fixed capacity (token rows + per-rank routing out, "
+                          "weighted partial rows back; no host synchronisation)",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "expert_gemv_kernel<EPI_GATE_UP> on the rank's received rows (rank 0)",
+            "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+            "peak_source": pk["source"], "traffic": None,
+            "algorithmic_bytes_per_launch": gate_bytes, "avg_launch_ms": gate_avg,
+            "down_avg_launch_ms": down_avg, "mean_local_active_experts": u,
+        },
+        "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
+                "ms_per_step": e2e_ms},
+        # dense 2 x (prep + engine), router, route, dispatch meta, routed experts (permute, gather,
+        # gate_up, down, combine), shared expert (the same five), combine_pairs
+        "gpu_launches": 18 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -212,6 +387,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=4, help="weight sets rotated across steps")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with N > 1: independent full-layer replicas instead of expert parallelism")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -232,6 +409,10 @@ def main() -> None:
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        if not args.replicas:
+            run_ep(args, world, rank, local, dev)
+            dist.destroy_process_group()
+            return
 
     from d3moe import _lib, ops, synth
 

@@ -370,6 +370,82 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, 
   if (tid == 0) scales[nb * KB + kb] = scale;
 }
 
+// dst[j] = src[token(j)] with token(j) = sorted_pairs[j] / k (zero row for a
+// pair id outside [0, T*k)); one warp per row, 16-byte copies.
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t src_stride,
+                                   int T, int H, int k, const int32_t* __restrict__ sorted_pairs,
+                                   int rows, __nv_bfloat16* __restrict__ dst) {
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int p = sorted_pairs[row];
+  const int t = (p >= 0 && p < T * k) ? p / k : -1;
+  uint4* d = reinterpret_cast<uint4*>(dst + static_cast<int64_t>(row) * H);
+  const uint4* sp = t >= 0 ? reinterpret_cast<const uint4*>(src + t * src_stride) : nullptr;
+  for (int c = threadIdx.x & 31; c < H / 8; c += 32) d[c] = sp ? __ldg(sp + c) : make_uint4(0, 0, 0, 0);
+}
+
+// Expert-parallel combine on the token's own rank:
+//   routed[t] = bf16( sum_r w[t,r] * rows[inv[t*k+r]] )   (fp32, r = 0..k-1)
+//   out[t]    = routed + bf16(shared[t] * bf16(sigmoid(gate[t])))
+__global__ void combine_pairs_kernel(const __nv_bfloat16* __restrict__ rows, int H,
+                                     const int32_t* __restrict__ inv_rows,
+                                     const __nv_bfloat16* __restrict__ weights, int T, int k,
+                                     const __nv_bfloat16* __restrict__ shared,
+                                     const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
+                                     __nv_bfloat16* __restrict__ out) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = H / 8;
+  if (idx >= static_cast<int64_t>(T) * per_row) return;
+  const int t = static_cast<int>(idx / per_row), c = static_cast<int>(idx % per_row) * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int r = 0; r < k; ++r) {
+    const int row = inv_rows[t * k + r];
+    if (row < 0) continue;
+    const float w = __bfloat162float(weights[t * k + r]);
+    float v[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(rows + static_cast<int64_t>(row) * H + c), v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += v[i] * w;
+  }
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = bf16_round(acc[i]);
+  if (shared) {
+    float sv[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(shared + static_cast<int64_t>(t) * H + c), sv);
+    const float g = gate ? sigmoid_gate_bf16(gate + t * gate_stride) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] += gate ? bf16_round(sv[i] * g) : sv[i];
+  }
+  uint32_t wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    wv[i] = *reinterpret_cast<uint32_t*>(&p2);
+  }
+  *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * H + c) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+}
+
+// Fixed-capacity EP dispatch metadata: for every destination rank d and
+// token t, the routing of t restricted to the experts d owns:
+//   meta_ids[d][t][j] = ids[t][j] - d*experts_per_rank if d owns ids[t][j], else -1
+//   meta_w[d][t][j]   = w[t][j] if d owns ids[t][j], else 0
+__global__ void ep_dispatch_meta_kernel(const int64_t* __restrict__ ids,
+                                        const __nv_bfloat16* __restrict__ w, int T, int k,
+                                        int experts_per_rank, int ranks,
+                                        int64_t* __restrict__ meta_ids,
+                                        __nv_bfloat16* __restrict__ meta_w) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n = static_cast<int64_t>(ranks) * T * k;
+  if (idx >= n) return;
+  const int d = static_cast<int>(idx / (static_cast<int64_t>(T) * k));
+  const int tj = static_cast<int>(idx % (static_cast<int64_t>(T) * k));
+  const int64_t e = ids[tj];
+  const bool mine = e >= 0 && e / experts_per_rank == d && e < static_cast<int64_t>(experts_per_rank) * ranks;
+  meta_ids[idx] = mine ? e - static_cast<int64_t>(d) * experts_per_rank : -1;
+  meta_w[idx] = mine ? w[tj] : __float2bfloat16_rn(0.f);
+}
+
 inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps); }
 
 // CTAs for one warp per (row, group pair).
@@ -488,4 +564,45 @@ extern "C" int d3_fp8_quantize_weight(const void* w, int N, int K, uint8_t* q, f
   weight_quant_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(w), N, K, q, scales);
   return check_launch("fp8_quantize_weight");
+}
+
+extern "C" int d3_gather_rows(const void* src, int64_t src_stride, int T, int H, int k,
+                              const int32_t* sorted_pairs, int rows, void* dst,
+                              d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && k > 0 && rows >= 0, "gather_rows: bad shape");
+  D3_REQUIRE(src_stride >= H && src_stride % 8 == 0, "gather_rows: src row stride must be >= H and a multiple of 8");
+  D3_REQUIRE(aligned(src, 16) && aligned(dst, 16), "gather_rows: misaligned pointer");
+  if (rows == 0) return D3_OK;
+  gather_rows_kernel<<<row_blocks(rows), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), src_stride, T, H, k, sorted_pairs, rows,
+      static_cast<__nv_bfloat16*>(dst));
+  return check_launch("gather_rows");
+}
+
+extern "C" int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const void* weights,
+                                int T, int k, int H, const void* shared, const void* gate,
+                                int64_t gate_stride, void* out, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && H > 0 && H % 8 == 0, "combine_pairs: bad shape");
+  D3_REQUIRE(aligned(rows, 16) && aligned(out, 16) && (!shared || aligned(shared, 16)), "combine_pairs: misaligned pointer");
+  const int64_t n = static_cast<int64_t>(T) * (H / 8);
+  if (n == 0) return D3_OK;
+  combine_pairs_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                         reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(rows), H, inv_rows, static_cast<const __nv_bfloat16*>(weights),
+      T, k, static_cast<const __nv_bfloat16*>(shared), static_cast<const __nv_bfloat16*>(gate),
+      gate_stride, static_cast<__nv_bfloat16*>(out));
+  return check_launch("combine_pairs");
+}
+
+extern "C" int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, int k,
+                                   int experts_per_rank, int ranks, int64_t* meta_ids,
+                                   void* meta_w, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && experts_per_rank > 0 && ranks > 0, "ep_dispatch_meta: bad arguments");
+  const int64_t n = static_cast<int64_t>(ranks) * T * k;
+  if (n == 0) return D3_OK;
+  ep_dispatch_meta_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __nv_bfloat16*>(weights), T, k, experts_per_rank, ranks, meta_ids,
+      static_cast<__nv_bfloat16*>(meta_w));
+  return check_launch("ep_dispatch_meta");
 }

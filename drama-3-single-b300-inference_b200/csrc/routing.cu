@@ -350,7 +350,43 @@ __global__ void __launch_bounds__(kPermuteThreads)
                max_rows, inv_rows, active, n_active);
 }
 
+// Expert-parallel dispatch plan. Experts are owned contiguously by ranks
+// (rank = id / experts_per_rank). Pairs are bucketed by destination rank with
+// the same stable counting sort as permute (ascending pair order within a
+// rank), and each bucketed slot gets the expert's id local to its rank.
+__global__ void __launch_bounds__(kPermuteThreads)
+    ep_plan_kernel(const int64_t* __restrict__ ids, int P, int experts_per_rank, int ranks,
+                   int32_t* __restrict__ send_counts, int32_t* __restrict__ send_starts,
+                   int32_t* __restrict__ total, int32_t* __restrict__ sorted_pairs,
+                   int32_t* __restrict__ scratch_tiles, int32_t* __restrict__ inv_rows,
+                   int64_t* __restrict__ local_ids) {
+  extern __shared__ int sm[];
+  const int E = experts_per_rank * ranks;
+  auto id_at = [&](int p) -> int {
+    const int64_t v = ids[p];
+    return (v >= 0 && v < E) ? static_cast<int>(v / experts_per_rank) : -1;
+  };
+  permute_body(id_at, P, ranks, 1, sm, send_counts, send_starts, total, sorted_pairs,
+               scratch_tiles, P, inv_rows, nullptr, nullptr);
+  __syncthreads();
+  for (int j = threadIdx.x; j < P; j += kPermuteThreads) {
+    const int p = sorted_pairs[j];
+    local_ids[j] = (p >= 0 && p < P) ? ids[p] % experts_per_rank : -1;
+  }
+}
+
 }  // namespace
+
+int launch_ep_plan(const int64_t* ids, int P, int experts_per_rank, int ranks,
+                   int32_t* send_counts, int32_t* send_starts, int32_t* total,
+                   int32_t* sorted_pairs, int32_t* scratch_tiles, int32_t* inv_rows,
+                   int64_t* local_ids, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(ranks) * 35 * sizeof(int);
+  ep_plan_kernel<<<1, kPermuteThreads, smem, s>>>(ids, P, experts_per_rank, ranks, send_counts,
+                                                  send_starts, total, sorted_pairs, scratch_tiles,
+                                                  inv_rows, local_ids);
+  return check_launch("ep_plan");
+}
 
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
@@ -477,4 +513,19 @@ extern "C" int d3_moe_permute(const int64_t* ids, int T, int k, int E, int block
   D3_REQUIRE(max_rows % block_m == 0, "moe_permute: max_rows must be a multiple of block_m");
   return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
                         max_rows, inv_rows, active, n_active, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int d3_ep_plan(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,
+                          int32_t* send_counts, int32_t* send_starts, int32_t* sorted_pairs,
+                          int32_t* inv_rows, int64_t* local_ids, int32_t* scratch,
+                          d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && experts_per_rank > 0 && ranks > 0 && ranks <= 1024,
+             "ep_plan: bad arguments T=%d k=%d experts_per_rank=%d ranks=%d", T, k,
+             experts_per_rank, ranks);
+  D3_REQUIRE(static_cast<int64_t>(T) * k < (1 << 24), "ep_plan: too many pairs");
+  if (T == 0) return D3_OK;
+  const int P = T * k;
+  return launch_ep_plan(ids, P, experts_per_rank, ranks, send_counts, send_starts, scratch,
+                        sorted_pairs, scratch + 1, inv_rows, local_ids,
+                        reinterpret_cast<cudaStream_t>(stream));
 }

@@ -84,6 +84,17 @@ SIGNATURES: dict[str, tuple] = {
          ctypes.POINTER(D3Experts), _c_void_p, _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
     "d3_set_stage_events": (_i32, [ctypes.POINTER(_c_void_p), _i32]),
+    "d3_ep_plan": (
+        _i32,
+        [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p, _c_void_p],
+    ),
+    "d3_ep_dispatch_meta": (_i32, [_c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
+    "d3_gather_rows": (_i32, [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p]),
+    "d3_combine_pairs": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p],
+    ),
     "d3_moe_layer": (
         _i32,
         [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.POINTER(D3Experts),

@@ -216,6 +216,41 @@ D3_API int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w, c
                  int64_t* ids_out, void* weights_out, void* workspace, size_t workspace_bytes,
                  int32_t* status, d3_stream_t stream);
 
+/* ---------------------------------------------- (e) expert parallelism --
+ * The reference runs on one GPU and has no expert parallelism; these entry
+ * points are the device-side steps of the EP layer in d3moe/ep.py (dispatch
+ * and combine over NCCL all-to-all). Experts are owned contiguously: rank
+ * r holds experts [r*experts_per_rank, (r+1)*experts_per_rank).
+ *
+ * d3_ep_plan: pairs p = t*k + r bucketed by destination rank (stable, like
+ * d3_moe_permute). send_counts/send_starts int32 [ranks]; sorted_pairs,
+ * inv_rows int32 [T*k]; local_ids int64 [T*k] in bucketed order = the expert
+ * id on its owner rank (-1 for an id outside [0, experts_per_rank*ranks));
+ * scratch int32 [T*k + 1]. */
+D3_API int d3_ep_plan(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,
+                      int32_t* send_counts, int32_t* send_starts, int32_t* sorted_pairs,
+                      int32_t* inv_rows, int64_t* local_ids, int32_t* scratch,
+                      d3_stream_t stream);
+
+/* Fixed-capacity dispatch (no host-visible counts): for each rank d and token
+ * t, meta_ids int64 [ranks, T, k] = ids[t][j] - d*experts_per_rank where rank d
+ * owns that expert, else -1; meta_w bf16 [ranks, T, k] = the routing weight
+ * there, else 0. */
+D3_API int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, int k,
+                               int experts_per_rank, int ranks, int64_t* meta_ids, void* meta_w,
+                               d3_stream_t stream);
+
+/* dst bf16 [rows, H] = src rows of token sorted_pairs[j] / k. */
+D3_API int d3_gather_rows(const void* src, int64_t src_stride, int T, int H, int k,
+                          const int32_t* sorted_pairs, int rows, void* dst, d3_stream_t stream);
+
+/* out bf16 [T,H] = bf16(sum_r w[t,r] * rows[inv[t*k+r]]) + bf16(shared * bf16(sigmoid(gate)))
+ * with rows bf16 [T*k, H] (expert outputs returned to the token's rank),
+ * the sum in fp32 in rank order; shared and gate may be NULL. */
+D3_API int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const void* weights,
+                            int T, int k, int H, const void* shared, const void* gate,
+                            int64_t gate_stride, void* out, d3_stream_t stream);
+
 /* Benchmark hook: while set, d3_moe_experts / d3_moe_layer calls made by the
  * calling thread record events[i] (cudaEvent_t handles, n >= 5) on their
  * stream at stage boundaries: 0 call start, 1 before the gate_up engine,
