@@ -8,11 +8,14 @@
 //   4. down         engine EPI_DOWN:    d f32 [R, H]
 //   5. combine      routed/shared/out bf16 [T, H] in fixed rank order
 // All buffers live in the caller's workspace; nothing is allocated here.
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "d3_host.h"
 #include "d3_internal.h"
 #include "expert_gemv.cuh"
+#include "tc_grouped.cuh"
 
 namespace d3 {
 
@@ -135,6 +138,50 @@ constexpr int kStagesGateUp = 5;
 constexpr int kStagesDown = 8;
 constexpr int kStagesDense = 6;
 
+// Token count from which the expert GEMMs run on tcgen05 (128-token tiles)
+// instead of the streaming engine. D3MOE_PREFILL_MIN_T overrides it.
+int default_prefill_min_tokens() {
+  static const int v = [] {
+    const char* e = std::getenv("D3MOE_PREFILL_MIN_T");
+    const int t = e ? std::atoi(e) : 0;
+    return t > 0 ? t : 1024;
+  }();
+  return v;
+}
+
+std::atomic<int> g_prefill_min_tokens{0};
+
+int prefill_min_tokens() {
+  const int t = g_prefill_min_tokens.load(std::memory_order_relaxed);
+  return t > 0 ? t : default_prefill_min_tokens();
+}
+
+template <int KIND>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& twsh,
+              const TcArgs& args, int grid, cudaStream_t s) {
+  auto kern = tc_grouped_kernel<KIND>;
+  const size_t smem = TcSmem::bytes();
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return set_error(D3_ECUDA, "tc grouped GEMM: cannot reserve %zu bytes of shared memory", smem);
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  kern<<<grid, kTcThreads, smem, s>>>(ta, tw, twsh, args);
+  return check_launch("tc grouped GEMM");
+}
+
+// Upper bound of the 128 x 256 tiles of one grouped GEMM (every group's rows
+// rounded up to 128), used to size the grid before the counts are known.
+int tc_grid(int R, int groups, int ntiles, int sms) {
+  const int64_t mt = (static_cast<int64_t>(R) + 127) / 128 + groups;
+  const int64_t tiles = mt * ntiles;
+  return static_cast<int>(tiles < sms ? tiles : sms);
+}
+
 int check_experts(const d3_experts_t* e, const char* what) {
   D3_REQUIRE(e != nullptr, "%s: expert weights missing", what);
   D3_REQUIRE(e->w13 && e->s13 && e->w2 && e->s2, "%s: null weight pointer", what);
@@ -165,6 +212,65 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
 
   const int sms = sm_count();
   stage_mark(1, s);
+  if (T >= prefill_min_tokens() && H % 256 == 0) {
+    // ---- prefill: both expert GEMMs on tcgen05
+    TcArgs a{};
+    a.counts = b.counts;
+    a.starts = b.starts;
+    a.E = E;
+    a.has_shared = has_shared;
+    a.shared_row0 = P;
+    a.shared_count = T;
+    a.act_rows = R;
+    a.I = I;
+    a.status = status;
+    {
+      CUtensorMap tw, twsh, ta;
+      if ((rc = encode_tmap_2d(&tw, ex->w13, 1, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w13 : ex->w13, 1, H,
+                               static_cast<uint64_t>(2) * I, H, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&ta, b.xq, 1, H, R, H, 128, 128))) return rc;
+      a.ntiles = I / 128;
+      a.KB = H / 128;
+      a.rows_per_expert = 2 * I;
+      a.second_box = I;
+      a.nt_stride = 128;
+      a.wscale = ex->s13;
+      a.wscale_sh = has_shared ? sh->s13 : ex->s13;
+      a.act_scale = b.sx;
+      a.out_q = b.a;
+      a.out_qs = b.sa;
+      rc = launch_tc<TC_GATE_UP>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s);
+      if (rc) return rc;
+    }
+    stage_mark(2, s);
+    {
+      CUtensorMap tw, twsh, ta;
+      if ((rc = encode_tmap_2d(&tw, ex->w2, 1, I, static_cast<uint64_t>(E) * H, I, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w2 : ex->w2, 1, I, H, I, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&ta, b.a, 1, I, R, I, 128, 128))) return rc;
+      a.ntiles = H / 256;
+      a.KB = I / 128;
+      a.rows_per_expert = H;
+      a.second_box = 128;
+      a.nt_stride = 256;
+      a.wscale = ex->s2;
+      a.wscale_sh = has_shared ? sh->s2 : ex->s2;
+      a.act_scale = b.sa;
+      a.out_q = nullptr;
+      a.out_qs = nullptr;
+      a.out_rows = b.d;
+      a.out_ld = H;
+      rc = launch_tc<TC_DOWN>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s);
+      if (rc) return rc;
+    }
+    stage_mark(3, s);
+    launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
+                        shared_out, out, s);
+    rc = check_launch("combine_rows");
+    stage_mark(4, s);
+    return rc;
+  }
   // ---- gate_up
   {
     CUtensorMap tw, twsh, ta;
@@ -256,6 +362,12 @@ extern "C" int d3_set_stage_events(void* const* events, int n) {
   D3_REQUIRE(events == nullptr || n >= 5, "set_stage_events: need at least 5 events");
   g_stage_events = events;
   return D3_OK;
+}
+
+extern "C" int d3_set_prefill_min_tokens(int t) {
+  const int prev = prefill_min_tokens();
+  g_prefill_min_tokens.store(t > 0 ? t : 0, std::memory_order_relaxed);
+  return prev;
 }
 
 extern "C" int d3_moe_workspace_size(int T, int k, int E, int I, int H, int has_shared,

@@ -1,0 +1,128 @@
+// tcgen05 (5th-generation tensor core) building blocks for sm_100a, as inline
+// PTX: tensor-memory (TMEM) allocation, shared-memory matrix descriptors,
+// instruction descriptors for kind::f8f6f4, the MMA issue/commit pair and the
+// TMEM -> register loads used by the epilogue warps.
+//
+// Operand layout used throughout: K-major tiles of 128-byte rows written by
+// TMA with CU_TENSOR_MAP_SWIZZLE_128B (8-row x 128-byte swizzle atoms, 1 KiB
+// apart). One 128-wide K block of FP8 is exactly one atom row; an MMA step of
+// K = 32 FP8 elements starts 32 bytes further inside the atom.
+#pragma once
+
+#include "d3_common.cuh"
+
+namespace d3 {
+namespace tc {
+
+// ---------------------------------------------------------------- TMEM --
+// Allocate `ncols` TMEM columns (power of two >= 32) for this CTA; the base
+// address is written to *smem_dst. Executed by one whole warp.
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before_thread_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_after_thread_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// --------------------------------------------------------- descriptors --
+// Shared-memory matrix descriptor (sm100 format): start address >> 4 in bits
+// [0,14), leading byte offset >> 4 in [16,30) (unused for swizzled K-major),
+// stride byte offset >> 4 in [32,46) (distance between 8-row groups), version
+// 1 in [46,48), base offset 0, layout type in [61,64) (2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(0) << 16;                    // LBO (ignored here)
+  d |= static_cast<uint64_t>((1024u >> 4) & 0x3FFFu) << 32;  // SBO = 8 rows x 128 B
+  d |= static_cast<uint64_t>(1) << 46;                    // descriptor version (sm100)
+  d |= static_cast<uint64_t>(2) << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f8f6f4 with E4M3 A and B, both K-major,
+// fp32 accumulation: c_format (F32 = 1) in bits [4,6), a/b format (E4M3 = 0)
+// in [7,10) / [10,13), N >> 3 in [17,23), M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one CTA, FP8 kind. `accumulate` = 0
+// overwrites D. Issued by a single thread.
+__device__ __forceinline__ void mma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once) on `bar` when every MMA this thread issued so far completes.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// -------------------------------------------------------- TMEM -> regs --
+// 32 lanes x 32 columns: lane i of the warp receives row (taddr.lane + i),
+// columns [taddr.col, taddr.col + 32) in r[0..31].
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&r)[32]) {
+  uint32_t u[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
+        "=r"(u[14]), "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]),
+        "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]),
+        "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&r)[16]) {
+  uint32_t u[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
+        "=r"(u[14]), "=r"(u[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = __uint_as_float(u[i]);
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// TMEM address of (lane, column).
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
+  return base + (lane << 16) + col;
+}
+
+}  // namespace tc
+}  // namespace d3

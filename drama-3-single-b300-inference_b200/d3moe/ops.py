@@ -213,6 +213,28 @@ def fp8_gemv(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, n: int | N
     return out
 
 
+def set_prefill_min_tokens(t: int) -> int:
+    """Token count from which the expert GEMMs run on the tcgen05 prefill
+    kernel (t <= 0 restores the default); returns the previous value."""
+    return int(_lib.load().d3_set_prefill_min_tokens(int(t)))
+
+
+class prefill_min_tokens:
+    """Context manager form of set_prefill_min_tokens."""
+
+    def __init__(self, t: int):
+        self.t = t
+        self.prev = None
+
+    def __enter__(self):
+        self.prev = set_prefill_min_tokens(self.t)
+        return self
+
+    def __exit__(self, *exc):
+        set_prefill_min_tokens(self.prev)
+        return False
+
+
 def moe_workspace(T: int, k: int, E: int, I: int, H: int, has_shared: bool, device) -> torch.Tensor:
     nbytes = ctypes.c_size_t()
     call("d3_moe_workspace_size", T, k, E, I, H, int(has_shared), ctypes.byref(nbytes))

@@ -258,6 +258,16 @@ D3_API int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const voi
  * No counterpart in the reference (its scripts time whole calls). */
 D3_API int d3_set_stage_events(void* const* events, int n);
 
+/* Token count T from which d3_moe_experts / d3_moe_layer run both expert GEMMs
+ * on the tcgen05 grouped kernel (128-token x 256-column tiles, TMEM
+ * accumulators) instead of the weight-streaming decode engine; H must be a
+ * multiple of 256 for that path. Default 1024, or D3MOE_PREFILL_MIN_T from the
+ * environment at first use. t <= 0 restores the default. Returns the previous
+ * value. Process-wide. The reference switches kernels by token count the
+ * same way (src/drama3/model.py:522-540: small_batch_moe up to
+ * small_moe_max_batch tokens, native_moe with tuned tiles from 1024). */
+D3_API int d3_set_prefill_min_tokens(int t);
+
 #ifdef __cplusplus
 }
 #endif
