@@ -40,11 +40,16 @@ int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, i
                          int k, const float* bias, int64_t* ids, void* weights, int weights_dtype,
                          int block_m, int32_t* counts, int32_t* starts, int32_t* total,
                          int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
-                         int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s);
+                         int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s,
+                         int32_t* scratch = nullptr);
 
+// Stable token->expert bucketing. With `scratch` (permute_scratch_ints(E)
+// ints) and T*k >= 8192 pairs it runs as three multi-CTA kernels; otherwise as
+// one 1024-thread CTA. Both give identical outputs.
 int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
                    int32_t* starts, int32_t* total, int32_t* sorted_ids, int32_t* expert_ids,
                    int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,
-                   cudaStream_t s);
+                   cudaStream_t s, int32_t* scratch = nullptr);
+size_t permute_scratch_ints(int E);
 
 }  // namespace d3

@@ -106,13 +106,18 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
     logits[static_cast<int64_t>(row) * E + e] = __bfloat162float(r[e]);
 }
 
+// One warp per expert-ordered row: every 16-byte load of the row is issued
+// before any group is reduced (H <= 2*128*kGatherMaxPairs), so a warp keeps a
+// whole row in flight instead of one group pair.
+constexpr int kGatherMaxPairs = 16;  // H <= 4096
+
 __global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                     int H, int k, const int32_t* __restrict__ sorted_pairs, int P,
                                     int rows, uint8_t* __restrict__ xq, float* __restrict__ sx) {
-  const int G = H / 128;
-  const RowPair rp = row_pair(G);
-  const int row = rp.row;
+  const int G = H / 128, GP = (G + 1) / 2;
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
   int token;
   if (row < P) {
     const int p = sorted_pairs[row];
@@ -123,14 +128,36 @@ __global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   uint8_t* qrow = xq + static_cast<int64_t>(row) * H;
   float* srow = sx + static_cast<int64_t>(row) * G;
   if (token < 0 || token >= T) {
-    const int lane = threadIdx.x & 31, g = 2 * rp.gp + (lane >> 4);
-    if (g < G) {
-      reinterpret_cast<uint2*>(qrow + g * 128)[lane & 15] = make_uint2(0, 0);
-      if ((lane & 15) == 0) srow[g] = 0.f;
+    for (int g = half; g < G; g += 2) {
+      reinterpret_cast<uint2*>(qrow + g * 128)[hl] = make_uint2(0, 0);
+      if (hl == 0) srow[g] = 0.f;
     }
     return;
   }
-  quant_pair(x + token * x_stride, G, rp.gp, qrow, srow, 1);
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(token) * x_stride;
+  uint4 v[kGatherMaxPairs];
+#pragma unroll
+  for (int i = 0; i < kGatherMaxPairs; ++i) {
+    const int g = 2 * i + half;
+    v[i] = (i < GP && g < G) ? __ldg(reinterpret_cast<const uint4*>(xr + g * 128 + hl * 8))
+                             : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < kGatherMaxPairs; ++i) {
+    if (i >= GP) break;
+    const int g = 2 * i + half;
+    float f[8];
+    unpack_bf16x8(v[i], f);
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    amax = half_warp_max(amax);
+    const float scale = act_scale_from_amax(amax);
+    if (g < G) {
+      *reinterpret_cast<uint2*>(qrow + g * 128 + hl * 8) = quant8(f, scale);
+      if (hl == 0) srow[g] = scale;
+    }
+  }
 }
 
 // Exact bf16 -> f16 transfer: each 128-group is multiplied by 2^s with s chosen
@@ -461,7 +488,8 @@ void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
                          float* sx, cudaStream_t s) {
   const int rows = P + (with_shared ? T : 0);
   if (rows <= 0) return;
-  quant_gather_kernel<<<pair_blocks(rows, H), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+  const unsigned blocks = static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps);
+  quant_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                        x_stride, T, H, k, sorted_pairs, P, rows,
                                                        xq, sx);
 }

@@ -49,6 +49,7 @@ struct MoeBuffers {
   int32_t* sorted;
   int32_t* tile_experts;
   int32_t* inv;
+  int32_t* permute_scratch;
   uint8_t* xq;
   float* sx;
   uint8_t* a;
@@ -74,6 +75,7 @@ MoeBuffers carve_moe(void* ws, int T, int k, int E, int I, int H, int has_shared
   b.sorted = c.take<int32_t>(P > 0 ? P : 1);
   b.tile_experts = c.take<int32_t>(P > 0 ? P : 1);
   b.inv = c.take<int32_t>(P > 0 ? P : 1);
+  b.permute_scratch = c.take<int32_t>(permute_scratch_ints(E));
   b.xq = c.take<uint8_t>(R * H);
   b.sx = c.take<float>(R * (H / 128));
   b.a = c.take<uint8_t>(R * I);
@@ -160,11 +162,18 @@ template <int KIND>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& twsh,
               const TcArgs& args, int grid, cudaStream_t s) {
   auto kern = tc_grouped_kernel<KIND>;
-  const size_t smem = TcSmem::bytes();
+  const size_t smem = TcSmem<KIND>::bytes();
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
+    // The warpgroup register split (setmaxnreg) is sized for exactly
+    // kTcLaunchRegs registers per thread at launch; any other allocation would
+    // make the increase wait forever, so refuse to launch instead.
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kTcLaunchRegs)
+      return set_error(D3_ECUDA, "tc grouped GEMM: built with %d registers per thread, expected %d",
+                       fa.numRegs, kTcLaunchRegs);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return set_error(D3_ECUDA, "tc grouped GEMM: cannot reserve %zu bytes of shared memory", smem);
@@ -204,7 +213,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
   int rc = D3_OK;
   if (!permuted) {
     rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, b.sorted, b.tile_experts, P,
-                        b.inv, b.active, b.n_active, s);
+                        b.inv, b.active, b.n_active, s, b.permute_scratch);
     if (rc) return rc;
   }
   launch_quant_gather(x, x_stride, T, H, k, b.sorted, P, has_shared, b.xq, b.sx, s);
@@ -389,6 +398,7 @@ static int check_common(const void* x, int64_t x_stride, int T, int k, const d3_
   }
   D3_REQUIRE(T >= 0 && k > 0 && k <= 32 && k <= ex->E, "%s: bad top-k %d", what, k);
   D3_REQUIRE(ex->E <= 1024, "%s: E=%d above 1024", what, ex->E);
+  D3_REQUIRE(ex->H <= 4096, "%s: H=%d above 4096", what, ex->H);
   D3_REQUIRE(static_cast<int64_t>(T) * k < (1 << 24), "%s: too many pairs", what);
   D3_REQUIRE(x_stride >= ex->H && x_stride % 8 == 0, "%s: x row stride must be >= H and a multiple of 8", what);
   D3_REQUIRE(aligned(x, 16), "%s: x must be 16-byte aligned", what);
@@ -440,7 +450,7 @@ extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_
   const int P = T * k;
   rc = launch_route_permute(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts,
                             D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, b.sorted,
-                            b.tile_experts, P, b.inv, b.active, b.n_active, s);
+                            b.tile_experts, P, b.inv, b.active, b.n_active, s, b.permute_scratch);
   if (rc) return rc;
   return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
                      nullptr, out, b, status ? status : b.status, s, true);

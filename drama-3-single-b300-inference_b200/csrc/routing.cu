@@ -89,6 +89,117 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Prefill form of the same projection, in the same summation order. A CTA of
+// 8 warps computes a 32-token x 16-row tile: warp w owns tokens 4w..4w+3 and
+// all 16 rows (64 independent fp32 chains per lane, lane l still owning
+// k = 256*i + 8*l + j). The 256-wide k blocks of the 32 x rows and 16 weight
+// rows stream through a 4-stage cp.async ring in shared memory (24 KB a
+// stage), so weights are read once per 32 tokens instead of once per 8.
+constexpr int kRtTok = 32, kRtRows = 16, kRtStages = 4, kRtThreads = 256;
+constexpr int kRtStageElems = (kRtTok + kRtRows) * 256;
+constexpr size_t kRtSmem = static_cast<size_t>(kRtStages) * kRtStageElems * 2;  // 96 KB
+constexpr int kRouterTiledMinTokens = 256;
+
+__global__ void __launch_bounds__(kRtThreads)
+    router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                               const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
+                               int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
+                               int64_t out_stride) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
+  const int nt = min(kRtTok, T - t0), nr = min(kRtRows, R - r0);
+  const int iters = (H + 255) / 256;
+
+  auto fill = [&](int i) {
+    __nv_bfloat16* st = ring + (i % kRtStages) * kRtStageElems;
+    for (int idx = threadIdx.x; idx < (kRtTok + kRtRows) * 32; idx += kRtThreads) {
+      const int row = idx >> 5, c = idx & 31;
+      const int k0 = 256 * i + 8 * c;
+      if (k0 >= H) continue;  // half-filled last block: those lanes skip it below
+      const __nv_bfloat16* src =
+          row < kRtTok ? x + static_cast<int64_t>(t0 + min(row, nt - 1)) * x_stride + k0
+                       : w + static_cast<int64_t>(r0 + min(row - kRtTok, nr - 1)) * H + k0;
+      cp_async_16(st + row * 256 + 8 * c, src);
+    }
+  };
+
+#pragma unroll
+  for (int i = 0; i < kRtStages - 1; ++i) {
+    if (i < iters) fill(i);
+    cp_async_commit();
+  }
+  float acc[4][kRtRows];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int r = 0; r < kRtRows; ++r) acc[u][r] = 0.f;
+
+  for (int i = 0; i < iters; ++i) {
+    if (i + kRtStages - 1 < iters) fill(i + kRtStages - 1);
+    cp_async_commit();
+    cp_async_wait<kRtStages - 1>();
+    __syncthreads();
+    if (256 * i + 8 * lane < H) {
+      const __nv_bfloat16* st = ring + (i % kRtStages) * kRtStageElems;
+      uint32_t xx[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 v = *reinterpret_cast<const uint4*>(st + (4 * warp + u) * 256 + 8 * lane);
+        xx[u][0] = v.x; xx[u][1] = v.y; xx[u][2] = v.z; xx[u][3] = v.w;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t ww[8][4];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const uint4 v = *reinterpret_cast<const uint4*>(st + (kRtTok + 8 * h + r) * 256 + 8 * lane);
+          ww[r][0] = v.x; ww[r][1] = v.y; ww[r][2] = v.z; ww[r][3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              float& a = acc[u][8 * h + r];
+              a = fmaf(__uint_as_float(ww[r][j] << 16), __uint_as_float(xx[u][j] << 16), a);
+              a = fmaf(__uint_as_float(ww[r][j] & 0xffff0000u),
+                       __uint_as_float(xx[u][j] & 0xffff0000u), a);
+            }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  // xor-butterfly: afterwards every lane holds every sum
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int r = 0; r < kRtRows; ++r)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[u][r] += __shfl_xor_sync(0xffffffffu, acc[u][r], o);
+  // lane = (token u of this warp) * 8 + (row pair): each lane writes rows 2*(lane&7) and +1
+  const int u = lane >> 3, rp = lane & 7;
+  const int t = 4 * warp + u;
+  if (t < nt) {
+    float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+    for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (uu == u && q == rp) {
+          v0 = acc[uu][2 * q];
+          v1 = acc[uu][2 * q + 1];
+        }
+    const int ra = r0 + 2 * rp;
+    __nv_bfloat16* o = out + static_cast<int64_t>(t0 + t) * out_stride;
+    if (ra < R) o[ra] = __float2bfloat16_rn(v0 + ((bias && ra < nbias) ? bias[ra] : 0.f));
+    if (ra + 1 < R) o[ra + 1] = __float2bfloat16_rn(v1 + ((bias && ra + 1 < nbias) ? bias[ra + 1] : 0.f));
+  }
+}
+
 // ------------------------------------------------------------------ route --
 // One warp per token. Keys order logits like the reference's packed keys
 // (src/drama3/kernels.py:365-369): the sign-flipped fp32 bit pattern in the
@@ -325,6 +436,130 @@ __global__ void __launch_bounds__(kPermuteThreads)
                inv_rows, active, n_active);
 }
 
+// Prefill-size permute over many CTAs: the same stable counting sort as
+// permute_body, split into three kernels over chunks of consecutive pairs.
+//   hist:    chunk c counts its pairs per expert        -> cc[c][e]
+//   scan:    one CTA: counts, padded starts, and cc[c][e] rewritten to the
+//            first slot of chunk c's pairs of expert e (start[e] + sum of
+//            cc[c'][e] for c' < c); padding slots, tile experts, active list
+//   scatter: chunk c places its pairs from cc[c][e] on, in ascending pair
+//            order (ranks from __match_any_sync and lower warps' counts)
+// Ascending chunk bases + ascending order inside a chunk give the same
+// sorted_ids as the single-CTA kernel.
+constexpr int kMaxPermuteChunks = 256;
+constexpr int kChunkedPermuteMinPairs = 8192;
+
+inline int permute_chunk_pairs(int P) {
+  const int per = (P + kMaxPermuteChunks - 1) / kMaxPermuteChunks;
+  return ((per + kPermuteThreads - 1) / kPermuteThreads) * kPermuteThreads;
+}
+
+__global__ void __launch_bounds__(kPermuteThreads)
+    permute_hist_kernel(const int64_t* __restrict__ ids, int P, int E, int chunk,
+                        int32_t* __restrict__ cc) {
+  extern __shared__ int cnt[];
+  for (int e = threadIdx.x; e < E; e += kPermuteThreads) cnt[e] = 0;
+  __syncthreads();
+  const int p0 = blockIdx.x * chunk, p1 = min(P, p0 + chunk);
+  for (int p = p0 + threadIdx.x; p < p1; p += kPermuteThreads) {
+    const int64_t v = ids[p];
+    if (v >= 0 && v < E) atomicAdd(&cnt[v], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kPermuteThreads)
+    cc[static_cast<int64_t>(blockIdx.x) * E + e] = cnt[e];
+}
+
+__global__ void __launch_bounds__(kPermuteThreads)
+    permute_scan_kernel(int32_t* __restrict__ cc, int chunks, int P, int E, int bm,
+                        int32_t* __restrict__ counts, int32_t* __restrict__ starts,
+                        int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
+                        int32_t* __restrict__ expert_ids, int64_t max_rows,
+                        int32_t* __restrict__ active, int32_t* __restrict__ n_active) {
+  __shared__ int warp_tot[33];
+  __shared__ int s_cnt[1024], s_start[1024];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int e = tid;
+  int c_tot = 0;
+  if (e < E)
+    for (int c = 0; c < chunks; ++c) c_tot += cc[static_cast<int64_t>(c) * E + e];
+  const int padded = (c_tot + bm - 1) / bm * bm;
+  int total = 0;
+  const int start = block_exclusive_scan(e < E ? padded : 0, warp_tot, total);
+  if (e < E) {
+    int run = start;
+    for (int c = 0; c < chunks; ++c) {
+      const int64_t i = static_cast<int64_t>(c) * E + e;
+      const int v = cc[i];
+      cc[i] = run;
+      run += v;
+    }
+    s_cnt[e] = c_tot;
+    s_start[e] = start;
+    counts[e] = c_tot;
+    starts[e] = start;
+  }
+  __syncthreads();
+  for (int ee = warp; ee < E; ee += kPermuteThreads / 32) {
+    const int c = s_cnt[ee], s = s_start[ee];
+    const int pd = (c + bm - 1) / bm * bm;
+    for (int i = c + lane; i < pd; i += 32) sorted_ids[s + i] = P;
+    for (int b = lane; b * bm < pd; b += 32) expert_ids[s / bm + b] = ee;
+  }
+  for (int64_t r = total + tid; r < max_rows; r += kPermuteThreads) sorted_ids[r] = P;
+  for (int64_t b = total / bm + tid; b < max_rows / bm; b += kPermuteThreads) expert_ids[b] = -1;
+  if (tid == 0) total_out[0] = total;
+  if (active) {
+    int n = 0;
+    const int flag = (e < E && c_tot > 0) ? 1 : 0;
+    const int pos = block_exclusive_scan(flag, warp_tot, n);
+    if (flag) active[pos] = e;
+    if (tid == 0 && n_active) n_active[0] = n;
+  }
+}
+
+__global__ void __launch_bounds__(kPermuteThreads)
+    permute_scatter_kernel(const int64_t* __restrict__ ids, int P, int E, int chunk,
+                           const int32_t* __restrict__ cc, int32_t* __restrict__ sorted_ids,
+                           int32_t* __restrict__ inv_rows) {
+  extern __shared__ int sm[];
+  int* cursor = sm;        // [E]
+  int* wcnt = sm + E;      // [32][E]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += kPermuteThreads) cursor[e] = cc[static_cast<int64_t>(blockIdx.x) * E + e];
+  for (int i = tid; i < 32 * E; i += kPermuteThreads) wcnt[i] = 0;
+  __syncthreads();
+  const int p0 = blockIdx.x * chunk, p1 = min(P, p0 + chunk);
+  for (int base = p0; base < p1; base += kPermuteThreads) {
+    const int p = base + tid;
+    int e = -1;
+    if (p < p1) {
+      const int64_t v = ids[p];
+      e = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const bool leader = rank == 0;
+    if (e >= 0 && leader) wcnt[warp * E + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int pre = 0;
+      for (int w2 = 0; w2 < warp; ++w2) pre += wcnt[w2 * E + e];
+      const int pos = cursor[e] + pre + rank;
+      sorted_ids[pos] = p;
+      if (inv_rows) inv_rows[p] = pos;
+    } else if (p < p1 && inv_rows) {
+      inv_rows[p] = -1;
+    }
+    __syncthreads();
+    if (e >= 0 && leader) {
+      atomicAdd(&cursor[e], __popc(peers));
+      wcnt[warp * E + e] = 0;
+    }
+    __syncthreads();
+  }
+}
+
 // Decode-size fusion of route_topk and permute in one CTA: the ids never leave
 // shared memory between the two. T*k <= kFusedMaxPairs.
 constexpr int kFusedMaxPairs = 4096;
@@ -392,6 +627,21 @@ void launch_router_logits(const void* x, int64_t x_stride, const void* w, const 
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
                           cudaStream_t s) {
   if (T <= 0 || R <= 0) return;
+  if (T >= kRouterTiledMinTokens) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+      cudaFuncSetAttribute(router_logits_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kRtSmem));
+      if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    dim3 grid((R + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
+    router_logits_tiled_kernel<<<grid, kRtThreads, kRtSmem, s>>>(
+        static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
+        nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
+    return;
+  }
   dim3 grid((R + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
   const size_t smem = static_cast<size_t>(kRouterTokens) * H * 2;  // <= 48 KB for H <= 3072
   router_logits_kernel<<<grid, 256, smem, s>>>(
@@ -418,14 +668,15 @@ int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, i
                          int k, const float* bias, int64_t* ids, void* weights, int weights_dtype,
                          int block_m, int32_t* counts, int32_t* starts, int32_t* total,
                          int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
-                         int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s) {
+                         int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s,
+                         int32_t* scratch) {
   if (T <= 0) return D3_OK;
   if (static_cast<int64_t>(T) * k > kFusedMaxPairs) {
     launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype, s);
     int rc = check_launch("route_topk");
     if (rc) return rc;
     return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
-                          max_rows, inv_rows, active, n_active, s);
+                          max_rows, inv_rows, active, n_active, s, scratch);
   }
   const size_t smem = (static_cast<size_t>(kFusedMaxPairs) + static_cast<size_t>(E) * 35) * sizeof(int);
   const int f32_in = logits_dtype == D3_DTYPE_F32, f32_out = weights_dtype == D3_DTYPE_F32;
@@ -450,10 +701,35 @@ int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, i
   return launch(route_permute_kernel<kMaxPerLane>);
 }
 
+size_t permute_scratch_ints(int E) { return static_cast<size_t>(kMaxPermuteChunks) * E; }
+
 int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t* counts,
                    int32_t* starts, int32_t* total, int32_t* sorted_ids, int32_t* expert_ids,
                    int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,
-                   cudaStream_t s) {
+                   cudaStream_t s, int32_t* scratch) {
+  const int P = T * k;
+  if (scratch && P >= kChunkedPermuteMinPairs) {
+    const int chunk = permute_chunk_pairs(P);
+    const int chunks = (P + chunk - 1) / chunk;
+    const size_t scatter_smem = static_cast<size_t>(E) * 33 * sizeof(int);
+    static bool conf_scatter[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (scatter_smem > 48 * 1024 && dev >= 0 && dev < 64 && !conf_scatter[dev]) {
+      if (cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               33 * 1024 * 4) != cudaSuccess)
+        return set_error(D3_ECUDA, "permute: cannot raise the shared-memory limit");
+      conf_scatter[dev] = true;
+    }
+    permute_hist_kernel<<<chunks, kPermuteThreads, static_cast<size_t>(E) * sizeof(int), s>>>(
+        ids, P, E, chunk, scratch);
+    permute_scan_kernel<<<1, kPermuteThreads, 0, s>>>(scratch, chunks, P, E, block_m, counts,
+                                                      starts, total, sorted_ids, expert_ids,
+                                                      max_rows, active, n_active);
+    permute_scatter_kernel<<<chunks, kPermuteThreads, scatter_smem, s>>>(ids, P, E, chunk, scratch,
+                                                                         sorted_ids, inv_rows);
+    return check_launch("moe_permute (chunked)");
+  }
   const size_t smem = static_cast<size_t>(E) * 35 * sizeof(int);
   static bool configured[64] = {false};
   int dev = 0;
@@ -513,6 +789,32 @@ extern "C" int d3_moe_permute(const int64_t* ids, int T, int k, int E, int block
   D3_REQUIRE(max_rows % block_m == 0, "moe_permute: max_rows must be a multiple of block_m");
   return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
                         max_rows, inv_rows, active, n_active, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int d3_moe_permute_scratch_size(int E, size_t* bytes) {
+  D3_REQUIRE(bytes != nullptr && E > 0 && E <= 1024, "moe_permute_scratch_size: bad arguments");
+  *bytes = permute_scratch_ints(E) * sizeof(int32_t);
+  return D3_OK;
+}
+
+extern "C" int d3_moe_permute_chunked(const int64_t* ids, int T, int k, int E, int block_m,
+                                      int32_t* counts, int32_t* starts, int32_t* total,
+                                      int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
+                                      int32_t* inv_rows, int32_t* active, int32_t* n_active,
+                                      int32_t* scratch, size_t scratch_bytes, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && E > 0 && E <= 1024, "moe_permute: E=%d must be in [1, 1024]", E);
+  D3_REQUIRE(block_m > 0, "moe_permute: block_m must be positive");
+  const int64_t P = static_cast<int64_t>(T) * k;
+  D3_REQUIRE(P < (1ll << 30), "moe_permute: too many pairs");
+  const int64_t need = (P + (P < E ? P : E) * (block_m - 1) + block_m - 1) / block_m * block_m;
+  D3_REQUIRE(max_rows >= need, "moe_permute: max_rows %lld < required %lld", (long long)max_rows, (long long)need);
+  D3_REQUIRE(max_rows % block_m == 0, "moe_permute: max_rows must be a multiple of block_m");
+  D3_REQUIRE(scratch != nullptr && aligned(scratch, 16) &&
+                 scratch_bytes >= permute_scratch_ints(E) * sizeof(int32_t),
+             "moe_permute_chunked: scratch must hold %zu bytes", permute_scratch_ints(E) * sizeof(int32_t));
+  return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
+                        max_rows, inv_rows, active, n_active, reinterpret_cast<cudaStream_t>(stream),
+                        scratch);
 }
 
 extern "C" int d3_ep_plan(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,

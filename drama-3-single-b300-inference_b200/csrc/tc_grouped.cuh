@@ -7,18 +7,30 @@
 //            W13 (the same i range), K = H;
 //   down:    rows = 128 tokens (requantised activations), cols = 256 rows of
 //            W2, K = I.
-// Warp roles (10 warps): warp 0 issues TMA loads of A [128 x 128 B] and B
-// [256 x 128 B] per 128-wide K block into a 4-stage ring; warp 1 owns TMEM
-// (512 columns = two 256-column accumulators) and issues 4 MMAs
-// (M=128, N=256, K=32, kind::f8f6f4, E4M3 x E4M3 -> fp32) per K block into one
-// accumulator; warps 2..9 are two epilogue warpgroups that, per K block, read
-// that block's partial product from TMEM and fold it into fp32 registers with
-// act_scale[row][kb] * weight_scale[col block][kb] (the 128x128 block-scale
-// promotion: the scales are arbitrary fp32, so they cannot ride in the MMA),
-// while the MMA of the next K block fills the other accumulator.
-// The tile epilogue is the same arithmetic as the decode engine: gate_up
-// rounds gate and up to bf16, a = bf16(silu(gate)) * up, requantises a per
-// 128-group to E4M3; down stores fp32 rows for the fixed-order combine.
+// Warp roles (12 warps, three warpgroups):
+//   warp 0      TMA: A [128 x 128 B] and B [256 x 128 B] per 128-wide K block
+//               into a 3-stage (gate_up) / 4-stage (down) ring;
+//   warp 1      owns TMEM (512 columns = two 256-column accumulators) and
+//               issues 4 MMAs (M=128, N=256, K=32, kind::f8f6f4, E4M3 x E4M3
+//               -> fp32) per K block into one accumulator;
+//   warps 2-3   gate_up only: activation warps (see below);
+//   warps 4-11  promotion: per K block they read that block's partial product
+//               from TMEM and fold it into fp32 registers with
+//               act_scale[row][kb] * weight_scale[col block][kb] (the 128x128
+//               block-scale promotion: the scales are arbitrary fp32, so they
+//               cannot ride in the MMA), while the MMA of the next K block fills
+//               the other accumulator.
+// Warpgroup 0 runs on 40 registers a thread and the promotion warpgroups on
+// 232 (setmaxnreg), which lets a promotion thread hold its 128 accumulators
+// plus 64 freshly loaded TMEM columns.
+// Tile epilogues:
+//   gate_up  the promotion warps compute a = bf16(silu(bf16(gate))) * bf16(up)
+//            and its per-row amax in registers and hand a over in shared memory
+//            ([128 rows][128] fp32, 64 KB); the two activation warps (a row per
+//            thread) turn it into the row's 1x128 E4M3 scale and bytes and store
+//            them, while the promotion warps already work on the next tile;
+//   down     the promotion warps store the fp32 rows for the fixed-order
+//            combine through a small per-warp staging tile (coalesced stores).
 #pragma once
 
 #include "d3_common.cuh"
@@ -52,22 +64,33 @@ struct TcArgs {
   int32_t* status;
 };
 
-constexpr int kTcStages = 4;
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 384;
+constexpr int kTcRegsLow = 40, kTcRegsHigh = 232;  // 128*40 + 256*232 = 384*168
+constexpr int kTcLaunchRegs = 168;
+static_assert(128 * kTcRegsLow + 256 * kTcRegsHigh <= kTcThreads * kTcLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr int kTcABytes = 128 * 128;
 constexpr int kTcBBytes = 256 * 128;
 constexpr int kTcStageBytes = kTcABytes + kTcBBytes;
 constexpr int kTcMaxGroups = 1025;
 
+template <int KIND>
 struct TcSmem {
-  static constexpr int kRing = kTcStages * kTcStageBytes;
-  static constexpr int kBars = kRing;                                   // full[S], empty[S], tfull[2], tempty[2]
-  static constexpr int kTmemSlot = kBars + (2 * kTcStages + 4) * 8;
+  static constexpr int kStages = KIND == TC_GATE_UP ? 3 : 4;
+  static constexpr int kRing = kStages * kTcStageBytes;
+  // full[S], empty[S], tfull[2], tempty[2], hfull, hempty
+  static constexpr int kBars = kRing;
+  static constexpr int kTmemSlot = kBars + (2 * kStages + 6) * 8;
   static constexpr int kAbort = kTmemSlot + 16;
-  static constexpr int kAmax = kAbort + 16;                             // [2][128] f32
-  static constexpr int kPrefix = kAmax + 2 * 128 * 4;                   // [groups + 1] int
-  static constexpr size_t bytes() { return 1024 + kPrefix + (kTcMaxGroups + 1) * 4; }
+  static constexpr int kPrefix = kAbort + 16;  // [groups + 1] int
+  // gate_up: handoff tile [128 rows][32 chunks of 4 fp32] + row amax [2][128]
+  // down:    staging tiles [8 warps][32 rows][4 chunks of 4 floats]
+  static constexpr int kAux = (kPrefix + (kTcMaxGroups + 1) * 4 + 1023) / 1024 * 1024;
+  static constexpr int kAuxBytes = KIND == TC_GATE_UP ? 128 * 128 * 4 + 2 * 128 * 4 : 8 * 32 * 16 * 4;
+  static constexpr size_t bytes() { return 1024 + kAux + kAuxBytes; }
 };
+static_assert(TcSmem<TC_GATE_UP>::bytes() <= 227 * 1024, "gate_up shared memory");
+static_assert(TcSmem<TC_DOWN>::bytes() <= 227 * 1024, "down shared memory");
 
 struct TcTile {
   int group, mt, nt;
@@ -117,22 +140,36 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   return false;
 }
 
+// Two floats rounded to bf16 in one conversion: returns the bf16x2 word
+// (lo in the low half) and writes the rounded values back.
+__device__ __forceinline__ uint32_t bf16x2_round(float& lo, float& hi) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+  lo = __uint_as_float(p << 16);
+  hi = __uint_as_float(p & 0xffff0000u);
+  return p;
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_kernel(const __grid_constant__ CUtensorMap tm_act,
                       const __grid_constant__ CUtensorMap tm_w,
                       const __grid_constant__ CUtensorMap tm_w_sh, const TcArgs args) {
+  using L = TcSmem<KIND>;
+  constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TcSmem::kBars);
-  uint64_t* empty = full + kTcStages;
-  uint64_t* tfull = empty + kTcStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBars);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + TcSmem::kTmemSlot);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::kAbort);
-  float* amax_x = reinterpret_cast<float*>(smem + TcSmem::kAmax);
-  int* prefix = reinterpret_cast<int*>(smem + TcSmem::kPrefix);
+  uint64_t* hfull = tempty + 2;
+  uint64_t* hempty = hfull + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
+  int* prefix = reinterpret_cast<int*>(smem + L::kPrefix);
+  uint8_t* aux = smem + L::kAux;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ngroups = args.E + args.has_shared;
@@ -160,7 +197,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) prefix[ngroups] = running;
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -168,6 +205,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);
     }
+    mbar_init(hfull, 8);   // promotion warps
+    mbar_init(hempty, 2);  // activation warps
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -181,117 +220,180 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tbase = *tslot;
   const int total_tiles = prefix[ngroups];
 
-  if (warp == 0) {
-    // -------------------------------------------------------------- TMA --
-    if (lane == 0) {
-      prefetch_tensormap(&tm_act);
-      prefetch_tensormap(&tm_w);
-      if (args.has_shared) prefetch_tensormap(&tm_w_sh);
-      uint32_t it = 0;
-      int last_parity[kTcStages];
+  if (warp < 4) {
+    tc::setmaxnreg_dec<kTcRegsLow>();
+    if (warp == 0) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- TMA --
+        prefetch_tensormap(&tm_act);
+        prefetch_tensormap(&tm_w);
+        if (args.has_shared) prefetch_tensormap(&tm_w_sh);
+        uint32_t it = 0;
+        int last_parity[S];
 #pragma unroll
-      for (int s = 0; s < kTcStages; ++s) last_parity[s] = -1;
-      bool ok = true;
-      for (int i = blockIdx.x; i < total_tiles && ok; i += gridDim.x) {
+        for (int s = 0; s < S; ++s) last_parity[s] = -1;
+        bool ok = true;
+        for (int i = blockIdx.x; i < total_tiles && ok; i += gridDim.x) {
+          const TcTile t = tc_tile(args, prefix, ngroups, i);
+          const CUtensorMap* wmap = t.shared ? &tm_w_sh : &tm_w;
+          for (int kb = 0; kb < args.KB; ++kb, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1;
+            if (!tc_wait(&empty[s], ph ^ 1, abort_flag, args.status)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + s * kTcStageBytes;
+            mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+#pragma unroll
+            for (int q = 0; q < S; ++q)
+              if (q == s) last_parity[q] = static_cast<int>(ph);
+            tma_load_2d(st, &tm_act, kb * 128, t.row0, &full[s]);
+            tma_load_2d(st + kTcABytes, wmap, kb * 128, t.wrow, &full[s]);
+            tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box, &full[s]);
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+          if (last_parity[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(last_parity[s]));
+      }
+    } else if (warp == 1) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- MMA --
+        const uint32_t idesc = tc::idesc_e4m3_f32(128, 256);
+        uint32_t it = 0, kbc = 0;
+        int last_tfull[2] = {-1, -1};
+        bool ok = true;
+        for (int i = blockIdx.x; i < total_tiles && ok; i += gridDim.x) {
+          for (int kb = 0; kb < args.KB; ++kb, ++it, ++kbc) {
+            const int s = it % S;
+            const uint32_t b = kbc & 1;
+            if (!tc_wait(&full[s], (it / S) & 1, abort_flag, args.status) ||
+                !tc_wait(&tempty[b], ((kbc >> 1) & 1) ^ 1, abort_flag, args.status)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_thread_sync();
+            const uint32_t a0 = smem_u32(smem + s * kTcStageBytes);
+            const uint32_t b0 = a0 + kTcABytes;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              tc::mma_f8f6f4(tbase + b * 256, tc::smem_desc_sw128(a0 + ks * 32),
+                             tc::smem_desc_sw128(b0 + ks * 32), idesc, ks > 0 ? 1u : 0u);
+            tc::mma_commit(&empty[s]);
+            tc::mma_commit(&tfull[b]);
+            if (b == 0) last_tfull[0] = static_cast<int>((kbc >> 1) & 1);
+            else last_tfull[1] = static_cast<int>((kbc >> 1) & 1);
+          }
+        }
+        // TMEM is freed below: make sure no MMA of this thread is still running
+        if (last_tfull[0] >= 0) mbar_wait(&tfull[0], static_cast<uint32_t>(last_tfull[0]));
+        if (last_tfull[1] >= 0) mbar_wait(&tfull[1], static_cast<uint32_t>(last_tfull[1]));
+      }
+    } else if constexpr (KIND == TC_GATE_UP) {
+      // ------------------------------------------------------- activation --
+      // Thread t (0..63) of the two activation warps owns rows t and t + 64 of
+      // each handed-over tile: scale = max(row amax halves) / 448, then the
+      // row's 128 values are quantised and stored (128 contiguous bytes).
+      const int at = threadIdx.x - 64;
+      const uint4* hbuf = reinterpret_cast<const uint4*>(aux);
+      const float* hamax = reinterpret_cast<const float*>(aux + 128 * 128 * 4);
+      uint32_t n = 0;
+      for (int i = blockIdx.x; i < total_tiles; i += gridDim.x, ++n) {
         const TcTile t = tc_tile(args, prefix, ngroups, i);
-        const CUtensorMap* wmap = t.shared ? &tm_w_sh : &tm_w;
-        for (int kb = 0; kb < args.KB; ++kb, ++it) {
-          const int s = it % kTcStages;
-          const uint32_t ph = (it / kTcStages) & 1;
-          if (!tc_wait(&empty[s], ph ^ 1, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + s * kTcStageBytes;
-          mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-          last_parity[s] = static_cast<int>(ph);
-          tma_load_2d(st, &tm_act, kb * 128, t.row0, &full[s]);
-          tma_load_2d(st + kTcABytes, wmap, kb * 128, t.wrow, &full[s]);
-          tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box, &full[s]);
-        }
-      }
-      for (int s = 0; s < kTcStages; ++s)
-        if (last_parity[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(last_parity[s]));
-    }
-  } else if (warp == 1) {
-    // -------------------------------------------------------------- MMA --
-    if (lane == 0) {
-      const uint32_t idesc = tc::idesc_e4m3_f32(128, 256);
-      uint32_t it = 0, kbc = 0;
-      int last_tfull[2] = {-1, -1};
-      bool ok = true;
-      for (int i = blockIdx.x; i < total_tiles && ok; i += gridDim.x) {
-        for (int kb = 0; kb < args.KB; ++kb, ++it, ++kbc) {
-          const int s = it % kTcStages;
-          const uint32_t b = kbc & 1;
-          if (!tc_wait(&full[s], (it / kTcStages) & 1, abort_flag, args.status) ||
-              !tc_wait(&tempty[b], ((kbc >> 1) & 1) ^ 1, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after_thread_sync();
-          const uint32_t a0 = smem_u32(smem + s * kTcStageBytes);
-          const uint32_t b0 = a0 + kTcABytes;
+        tc_wait(hfull, n & 1, abort_flag, args.status);
+        __syncwarp();
+#pragma unroll 1
+        for (int rr = 0; rr < 2; ++rr) {
+          const int r = at + 64 * rr;
+          if (r < t.mvalid) {
+            const uint4* hrow = hbuf + r * 32;
+            const int sw = r & 7;
+            const float sc = act_scale_from_amax(fmaxf(hamax[r], hamax[128 + r]));
+            const float rs = __frcp_rn(sc);
+            const int64_t grow = t.row0 + r;
+            uint4* q = reinterpret_cast<uint4*>(args.out_q + grow * args.I + t.nt * 128);
+#pragma unroll 2
+            for (int c8 = 0; c8 < 8; ++c8) {
+              uint32_t word[4];
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            tc::mma_f8f6f4(tbase + b * 256, tc::smem_desc_sw128(a0 + ks * 32),
-                           tc::smem_desc_sw128(b0 + ks * 32), idesc, ks > 0 ? 1u : 0u);
-          tc::mma_commit(&empty[s]);
-          tc::mma_commit(&tfull[b]);
-          last_tfull[b] = static_cast<int>((kbc >> 1) & 1);
+              for (int c = 0; c < 4; ++c) {
+                const uint4 v = hrow[(4 * c8 + c) ^ sw];
+                const float x[4] = {__uint_as_float(v.x), __uint_as_float(v.y),
+                                    __uint_as_float(v.z), __uint_as_float(v.w)};
+                float qv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  qv[e] = fminf(fmaxf(div_by_scale(x[e], sc, rs), -448.0f), 448.0f);
+                word[c] = static_cast<uint32_t>(f32x2_to_e4m3x2(qv[0], qv[1])) |
+                          (static_cast<uint32_t>(f32x2_to_e4m3x2(qv[2], qv[3])) << 16);
+              }
+              q[c8] = make_uint4(word[0], word[1], word[2], word[3]);
+            }
+            args.out_qs[grow * (args.I / 128) + t.nt] = sc;
+          }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(hempty);
       }
-      // TMEM is freed below: make sure no MMA of this thread is still running
-      for (int b = 0; b < 2; ++b)
-        if (last_tfull[b] >= 0) mbar_wait(&tfull[b], static_cast<uint32_t>(last_tfull[b]));
     }
   } else {
-    // --------------------------------------------------------- epilogue --
-    const int ew = warp - 2;           // 0..7
+    // ---------------------------------------------------------- promotion --
+    tc::setmaxnreg_inc<kTcRegsHigh>();
+    const int ew = warp - 4;           // 0..7
     const int quad = warp & 3;         // TMEM lane quadrant this warp may access
     const int wg = ew >> 2;            // column half
     const int row = quad * 32 + lane;  // tile row of this thread
-    uint32_t kbc = 0;
-    for (int i = blockIdx.x; i < total_tiles; i += gridDim.x) {
-      const TcTile t = tc_tile(args, prefix, ngroups, i);
+    const int KB = args.KB;
+    // columns of this thread: gate_up -> [64wg, 64wg+64) gate and [128+64wg, ...) up;
+    // down -> [128wg, 128wg+128) as two runs of 64
+    const uint32_t c0 = KIND == TC_GATE_UP ? 64 * wg : 128 * wg;
+    const uint32_t c1 = KIND == TC_GATE_UP ? 128 + 64 * wg : 128 * wg + 64;
+    // scale of (row, kb) and the two weight blocks of this thread's columns
+    auto load_scales = [&](const TcTile& t, int kb, float& sa, float& w0, float& w1) {
       const float* wscale = t.shared ? args.wscale_sh : args.wscale;
+      const int sb0 = KIND == TC_GATE_UP ? t.wrow / 128 : (t.wrow + 128 * wg) / 128;
+      const int sb1 = KIND == TC_GATE_UP ? (t.wrow + args.second_box) / 128 : sb0;
       const int grow = t.row0 + row;
-      const bool row_ok = grow < args.act_rows;
-      // weight-scale rows of this thread's columns
-      int sb0, sb1;
-      if (KIND == TC_GATE_UP) {
-        sb0 = (t.wrow + 0) / 128;                       // gate block
-        sb1 = (t.wrow + args.second_box) / 128;         // up block
-      } else {
-        sb0 = (t.wrow + 128 * wg) / 128;                // this half's block
-        sb1 = sb0;
-      }
+      sa = grow < args.act_rows ? __ldg(args.act_scale + static_cast<int64_t>(grow) * KB + kb) : 0.f;
+      w0 = __ldg(wscale + sb0 * KB + kb);
+      w1 = __ldg(wscale + sb1 * KB + kb);
+    };
+    uint32_t kbc = 0, n = 0;
+    int i = blockIdx.x;
+    TcTile t{};
+    float p_sa = 0.f, p_w0 = 0.f, p_w1 = 0.f;
+    if (i < total_tiles) {
+      t = tc_tile(args, prefix, ngroups, i);
+      load_scales(t, 0, p_sa, p_w0, p_w1);
+    }
+    for (; i < total_tiles; i += gridDim.x, ++n) {
+      const int inext = i + gridDim.x;
+      TcTile tn{};
+      if (inext < total_tiles) tn = tc_tile(args, prefix, ngroups, inext);
       float acc0[64], acc1[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc0[j] = acc1[j] = 0.f;
-      for (int kb = 0; kb < args.KB; ++kb, ++kbc) {
+      for (int kb = 0; kb < KB; ++kb, ++kbc) {
         const uint32_t b = kbc & 1;
-        const float sa = row_ok ? args.act_scale[static_cast<int64_t>(grow) * args.KB + kb] : 0.f;
-        const float f0 = sa * wscale[sb0 * args.KB + kb];
-        const float f1 = sa * wscale[sb1 * args.KB + kb];
+        const float f0 = p_sa * p_w0, f1 = p_sa * p_w1;
+        // scales of the next K block (or the next tile's first) load under this one
+        if (kb + 1 < KB) load_scales(t, kb + 1, p_sa, p_w0, p_w1);
+        else if (inext < total_tiles) load_scales(tn, 0, p_sa, p_w0, p_w1);
         tc_wait(&tfull[b], (kbc >> 1) & 1, abort_flag, args.status);
         __syncwarp();  // the TMEM loads below are warp-collective
         tc::fence_after_thread_sync();
         const uint32_t tl = tbase + b * 256 + (static_cast<uint32_t>(quad * 32) << 16);
-        // columns of this thread: gate_up -> [64wg, 64wg+64) and [128+64wg, ...);
-        // down -> [128wg, 128wg+128) split as two runs of 64
-        const uint32_t c0 = KIND == TC_GATE_UP ? 64 * wg : 128 * wg;
-        const uint32_t c1 = KIND == TC_GATE_UP ? 128 + 64 * wg : 128 * wg + 64;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          float r0[16], r1[16];
-          tc::tmem_ld_32x32b_x16(tl + c0 + 16 * ch, r0);
-          tc::tmem_ld_32x32b_x16(tl + c1 + 16 * ch, r1);
+        for (int h = 0; h < 2; ++h) {
+          float r0[32], r1[32];
+          tc::tmem_ld_32x32b_x32(tl + c0 + 32 * h, r0);
+          tc::tmem_ld_32x32b_x32(tl + c1 + 32 * h, r1);
           tc::tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            acc0[16 * ch + j] = fmaf(r0[j], f0, acc0[16 * ch + j]);
-            acc1[16 * ch + j] = fmaf(r1[j], f1, acc1[16 * ch + j]);
+          for (int j = 0; j < 32; j += 2) {
+            ffma2(acc0[32 * h + j], acc0[32 * h + j + 1], r0[j], r0[j + 1], f0);
+            ffma2(acc1[32 * h + j], acc1[32 * h + j + 1], r1[j], r1[j + 1], f1);
           }
         }
         tc::fence_before_thread_sync();
@@ -299,51 +401,64 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
       // ------------------------------------------------------ tile epilogue --
-      const bool store = row < t.mvalid;
       if constexpr (KIND == TC_GATE_UP) {
+        // a = bf16(silu(g)) * u with g, u the bf16-rounded gate and up and
+        // silu(g) = g / (1 + exp(-g)) on the fast exponential and divide; a goes
+        // to the activation warps as fp32 (16-byte chunk c of row r at chunk
+        // c ^ (r & 7): conflict-free by row and by chunk) with this half's amax
         float amax = 0.f;
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float gv = bf16_round(acc0[j]);
-          const float uv = bf16_round(acc1[j]);
-          const float sg = bf16_round(gv * (1.0f / (1.0f + expf(-gv))));
-          acc0[j] = sg * uv;
-          amax = fmaxf(amax, fabsf(acc0[j]));
+        for (int j = 0; j < 64; j += 2) {
+          bf16x2_round(acc0[j], acc1[j]);
+          bf16x2_round(acc0[j + 1], acc1[j + 1]);
+          float s0 = __fdividef(acc0[j], 1.0f + __expf(-acc0[j]));
+          float s1 = __fdividef(acc0[j + 1], 1.0f + __expf(-acc0[j + 1]));
+          bf16x2_round(s0, s1);
+          acc0[j] = s0 * acc1[j];
+          acc0[j + 1] = s1 * acc1[j + 1];
+          amax = fmaxf(amax, fmaxf(fabsf(acc0[j]), fabsf(acc0[j + 1])));
         }
-        amax_x[wg * 128 + row] = amax;
-        named_bar_sync(1, 256);
-        const float sc = act_scale_from_amax(fmaxf(amax_x[row], amax_x[128 + row]));
-        if (store) {
-          uint8_t* q = args.out_q + static_cast<int64_t>(grow) * args.I + t.nt * 128 + 64 * wg;
+        tc_wait(hempty, (n & 1) ^ 1, abort_flag, args.status);
+        __syncwarp();
+        uint4* hbuf = reinterpret_cast<uint4*>(aux);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint32_t word = 0;
-#pragma unroll
-              for (int b8 = 0; b8 < 4; ++b8)
-                word |= static_cast<uint32_t>(act_quant(acc0[16 * v + 4 * u + b8], sc)) << (8 * b8);
-              w4[u] = word;
-            }
-            reinterpret_cast<uint4*>(q)[v] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-          }
-          if (wg == 0) args.out_qs[static_cast<int64_t>(grow) * (args.I / 128) + t.nt] = sc;
-        }
-        named_bar_sync(1, 256);  // amax_x is reused by the next tile
+        for (int c = 0; c < 16; ++c)
+          hbuf[row * 32 + ((16 * wg + c) ^ (row & 7))] =
+              make_uint4(__float_as_uint(acc0[4 * c]), __float_as_uint(acc0[4 * c + 1]),
+                         __float_as_uint(acc0[4 * c + 2]), __float_as_uint(acc0[4 * c + 3]));
+        reinterpret_cast<float*>(aux + 128 * 128 * 4)[wg * 128 + row] = amax;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(hfull);
       } else {
-        if (store) {
-          float* o = args.out_rows + static_cast<int64_t>(grow) * args.out_ld + t.nt * 256 + 128 * wg;
+        // fp32 rows through a per-warp staging tile [32 rows][16 floats] whose
+        // 16-byte chunks are swizzled by (row >> 1) & 3 (conflict-free vector
+        // stores by row and loads by chunk): each global store instruction then
+        // writes 8 rows x 64 contiguous bytes instead of 32 scattered 16 bytes
+        float4* stg = reinterpret_cast<float4*>(aux) + ew * 32 * 4;
+        const int sr = lane >> 2, c4 = lane & 3;
+        float* obase = args.out_rows + static_cast<int64_t>(t.row0 + quad * 32) * args.out_ld +
+                       t.nt * 256 + 128 * wg;
 #pragma unroll
-          for (int v = 0; v < 16; ++v)
-            reinterpret_cast<float4*>(o)[v] =
-                make_float4(acc0[4 * v], acc0[4 * v + 1], acc0[4 * v + 2], acc0[4 * v + 3]);
+        for (int ch = 0; ch < 8; ++ch) {
 #pragma unroll
-          for (int v = 0; v < 16; ++v)
-            reinterpret_cast<float4*>(o + 64)[v] =
-                make_float4(acc1[4 * v], acc1[4 * v + 1], acc1[4 * v + 2], acc1[4 * v + 3]);
+          for (int c = 0; c < 4; ++c) {
+            const int j = 16 * (ch & 3) + 4 * c;
+            const float4 v = ch < 4 ? make_float4(acc0[j], acc0[j + 1], acc0[j + 2], acc0[j + 3])
+                                    : make_float4(acc1[j], acc1[j + 1], acc1[j + 2], acc1[j + 3]);
+            stg[lane * 4 + (c ^ ((lane >> 1) & 3))] = v;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int r = sr + 8 * q;
+            if (quad * 32 + r < t.mvalid)
+              *reinterpret_cast<float4*>(obase + static_cast<int64_t>(r) * args.out_ld + 16 * ch + 4 * c4) =
+                  stg[r * 4 + (c4 ^ ((r >> 1) & 3))];
+          }
+          __syncwarp();
         }
       }
+      t = tn;
     }
   }
   tc::fence_before_thread_sync();

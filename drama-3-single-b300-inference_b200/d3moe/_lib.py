@@ -63,6 +63,12 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
          _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "d3_moe_permute_scratch_size": (_i32, [_i32, ctypes.POINTER(ctypes.c_size_t)]),
+    "d3_moe_permute_chunked": (
+        _i32,
+        [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    ),
     "d3_silu_mul": (_i32, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p]),
     "d3_silu_mul_quant": (_i32, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_combine_experts": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p]),

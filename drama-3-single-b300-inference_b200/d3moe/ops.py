@@ -119,9 +119,10 @@ def route_topk(logits: torch.Tensor, k: int = 8, bias: torch.Tensor | None = Non
     return w, ids
 
 
-def moe_permute(topk_ids: torch.Tensor, num_experts: int, block_m: int = 16):
+def moe_permute(topk_ids: torch.Tensor, num_experts: int, block_m: int = 16, chunked: bool = False):
     """Reference bucketing buffers (src/drama3/kernels.py:711-731):
-    (counts, starts, total, sorted_ids, expert_ids, inverse_rows, active, n_active)."""
+    (counts, starts, total, sorted_ids, expert_ids, inverse_rows, active, n_active).
+    chunked=True runs the multi-CTA form (used by the layer from 8192 pairs)."""
     _require_cuda(topk_ids)
     if topk_ids.dtype != torch.int64 or not topk_ids.is_contiguous():
         raise ValueError("topk_ids must be contiguous int64")
@@ -139,9 +140,18 @@ def moe_permute(topk_ids: torch.Tensor, num_experts: int, block_m: int = 16):
     inv = torch.empty(max(P, 1), **i32)
     active = torch.empty(num_experts, **i32)
     n_active = torch.empty(1, **i32)
-    call("d3_moe_permute", topk_ids.data_ptr(), T, k, num_experts, block_m, counts.data_ptr(),
-         starts.data_ptr(), total.data_ptr(), sorted_ids.data_ptr(), expert_ids.data_ptr(),
-         max_rows, inv.data_ptr(), active.data_ptr(), n_active.data_ptr(), _stream(dev))
+    if chunked:
+        nbytes = ctypes.c_size_t()
+        call("d3_moe_permute_scratch_size", num_experts, ctypes.byref(nbytes))
+        scratch = torch.empty(nbytes.value, dtype=torch.uint8, device=dev)
+        call("d3_moe_permute_chunked", topk_ids.data_ptr(), T, k, num_experts, block_m,
+             counts.data_ptr(), starts.data_ptr(), total.data_ptr(), sorted_ids.data_ptr(),
+             expert_ids.data_ptr(), max_rows, inv.data_ptr(), active.data_ptr(), n_active.data_ptr(),
+             scratch.data_ptr(), scratch.numel(), _stream(dev))
+    else:
+        call("d3_moe_permute", topk_ids.data_ptr(), T, k, num_experts, block_m, counts.data_ptr(),
+             starts.data_ptr(), total.data_ptr(), sorted_ids.data_ptr(), expert_ids.data_ptr(),
+             max_rows, inv.data_ptr(), active.data_ptr(), n_active.data_ptr(), _stream(dev))
     return counts, starts, total, sorted_ids, expert_ids, inv[:P], active, n_active
 
 

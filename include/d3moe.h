@@ -115,6 +115,18 @@ D3_API int d3_moe_permute(const int64_t* ids, int T, int k, int E, int block_m, 
                    int64_t max_rows, int32_t* inv_rows, int32_t* active, int32_t* n_active,
                    d3_stream_t stream);
 
+/* Same outputs as d3_moe_permute, computed by three multi-CTA kernels (per-chunk
+ * histogram, one-CTA scan, per-chunk stable scatter) when T*k >= 8192; the
+ * caller provides d3_moe_permute_scratch_size(E) bytes of device scratch.
+ * Prefill sizes: the reference's multi-program expert_counts / offsets /
+ * scatter kernels (src/drama3/kernels.py:658-699) split the same way. */
+D3_API int d3_moe_permute_scratch_size(int E, size_t* bytes);
+D3_API int d3_moe_permute_chunked(const int64_t* ids, int T, int k, int E, int block_m,
+                           int32_t* counts, int32_t* starts, int32_t* total, int32_t* sorted_ids,
+                           int32_t* expert_ids, int64_t max_rows, int32_t* inv_rows,
+                           int32_t* active, int32_t* n_active, int32_t* scratch,
+                           size_t scratch_bytes, d3_stream_t stream);
+
 /* ----------------------------------------------------- (a6) SiLU * mul --
  * out bf16 [rows, W] = bf16(bf16(silu(gate)) * up), gate = in[:, :W],
  * up = in[:, W:2W]. Replaces silu_mul (src/drama3/kernels.py:386-402). */

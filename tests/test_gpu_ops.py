@@ -66,7 +66,11 @@ def test_quant_act_matches_oracle_bytes(d3, T):
 
 
 # ------------------------------------------------------------------- (a1) --
-@pytest.mark.parametrize("T,R,H", [(1, 129, 2048), (64, 129, 2048), (13, 257, 2048), (5, 33, 384)])
+# T >= 256 runs the tiled prefill kernel (32-token x 16-row tiles through a
+# cp.async ring) in the same summation order; 300 and 129/33 rows leave ragged
+# tiles, H=384 a half-filled last 256-wide block.
+@pytest.mark.parametrize("T,R,H", [(1, 129, 2048), (64, 129, 2048), (13, 257, 2048), (5, 33, 384),
+                                   (256, 129, 2048), (300, 129, 2048), (513, 33, 384)])
 def test_router_logits_bit_exact(d3, T, R, H):
     rng = np.random.default_rng(R + T)
     x = O.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
@@ -118,14 +122,18 @@ def test_permute_golden(d3, golden, T, bm):
     assert (sorted_ids.cpu().numpy()[tot:] == T * 8).all()
 
 
-@pytest.mark.parametrize("T,E,bm", [(64, 128, 1), (2048, 128, 64), (8192, 128, 128), (3, 1000, 16)])
-def test_permute_matches_oracle(d3, T, E, bm):
+@pytest.mark.parametrize("chunked", [False, True])
+@pytest.mark.parametrize("T,E,bm", [(64, 128, 1), (2048, 128, 64), (8192, 128, 128), (3, 1000, 16),
+                                    (8192, 128, 1), (40000, 1000, 1)])
+def test_permute_matches_oracle(d3, T, E, bm, chunked):
+    """chunked=True: three multi-CTA kernels from 8192 pairs (below that the
+    entry falls back to the one-CTA kernel); outputs must be identical."""
     rng = np.random.default_rng(T + E)
     hot = rng.zipf(1.5, size=(T, 8)) % E  # skewed, with duplicate experts across tokens
     ids = np.stack([rng.permutation(E)[:8] if t % 3 else (hot[t] + np.arange(8)) % E for t in range(T)])
     ids = ids.astype(np.int64)
     counts, starts, total, sorted_ids, expert_ids, inv, active, n_active = d3["ops"].moe_permute(
-        torch.from_numpy(ids).cuda(), E, bm)
+        torch.from_numpy(ids).cuda(), E, bm, chunked=chunked)
     c, s, tot, so, eo = O.moe_permute(ids, E, bm)
     assert int(total.item()) == tot
     np.testing.assert_array_equal(counts.cpu().numpy(), c)
