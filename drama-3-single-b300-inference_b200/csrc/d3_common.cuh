@@ -223,6 +223,20 @@ __device__ __forceinline__ float bf16_round_alu(float v) {
   return __uint_as_float(u & 0xffff0000u);
 }
 
+// acc = fma(hi(x), hi(w), fma(lo(x), lo(w), acc)) for bf16x2 words x, w: the
+// mixed-precision FMA takes bf16 operands directly (their products are exact
+// in fp32), so no bf16 -> fp32 unpacking is needed.
+__device__ __forceinline__ float fma_bf16x2_seq(uint32_t x, uint32_t w, float acc) {
+  asm("{\n\t.reg .b16 xl, xh, wl, wh;\n\t"
+      "mov.b32 {xl, xh}, %1;\n\t"
+      "mov.b32 {wl, wh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, xl, wl, %0;\n\t"
+      "fma.rn.f32.bf16 %0, xh, wh, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(x), "r"(w));
+  return acc;
+}
+
 // (a0, a1) += (x0, x1) * s as one packed fp32x2 FMA (two IEEE fp32 FMAs).
 __device__ __forceinline__ void ffma2(float& a0, float& a1, float x0, float x1, float s) {
   asm("{\n\t.reg .b64 d, x, s2, c;\n\t"
@@ -265,11 +279,13 @@ __device__ __forceinline__ uint8_t act_quant(float x, float scale) {
 // step (Markstein, IBM J. Res. Dev. 34(1), 1990): q0 = RN(x*rs), the remainder
 // r = x - q0*scale is exact in one FMA, and RN(q0 + r*rs) is the correctly
 // rounded quotient for the normal range the activation quantiser works in
-// (|x/scale| <= 448). Costs 3 operations per element instead of a division.
+// (|x/scale| <= 448). A zero remainder means q0 is already exact; keeping it
+// also keeps the sign of a zero quotient (x = -0 gives -0, like the division).
+// Costs 3 operations per element instead of a division.
 __device__ __forceinline__ float div_by_scale(float x, float scale, float rs) {
   const float q0 = x * rs;
   const float r = fmaf(-q0, scale, x);
-  return fmaf(r, rs, q0);
+  return r == 0.0f ? q0 : fmaf(r, rs, q0);
 }
 
 // Two floats -> two E4M3 bytes (lo in the low byte), round-to-nearest-even,
@@ -278,6 +294,20 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// act_quant with rs = __frcp_rn(scale) computed once per group: the same
+// bytes (x / scale is correctly rounded by div_by_scale).
+__device__ __forceinline__ float act_quant_value(float x, float scale, float rs) {
+  return fminf(fmaxf(div_by_scale(x, scale, rs), -448.0f), 448.0f);
+}
+__device__ __forceinline__ uint32_t act_quant4(float x0, float x1, float x2, float x3, float scale,
+                                               float rs) {
+  return static_cast<uint32_t>(f32x2_to_e4m3x2(act_quant_value(x0, scale, rs),
+                                               act_quant_value(x1, scale, rs))) |
+         (static_cast<uint32_t>(f32x2_to_e4m3x2(act_quant_value(x2, scale, rs),
+                                                act_quant_value(x3, scale, rs)))
+          << 16);
 }
 
 }  // namespace d3

@@ -7,12 +7,13 @@
 
 namespace d3 {
 
-// x rows -> e4m3 rows gathered in expert-sorted order. Row r < P takes token
-// sorted_pairs[r] / k (a sentinel >= P gives a zero row); rows P..P+T-1 (when
-// with_shared) take tokens 0..T-1 for the shared expert.
-void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
-                         const int32_t* sorted_pairs, int P, int with_shared, uint8_t* xq,
-                         float* sx, cudaStream_t s);
+
+// Activation quantisation into expert order: token t is quantised once (1x128
+// groups, e4m3 + f32 scale) and written to rows inv_rows[t*k + j] (negative =
+// skipped) and, with with_shared, to row P + t. Rows not named are untouched.
+void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
+                          const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
+                          cudaStream_t s);
 
 // Weight-only GEMV activation prep: x bf16 [T,K] -> f16 [T,K] scaled by a
 // power of two per 1x128 group (exact), inv f32 [T,K/128] = the inverse factor.
@@ -27,6 +28,8 @@ void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const v
                          int T, int k, int with_shared, const void* gate, int64_t gate_stride,
                          void* routed_out, void* shared_out, void* out, cudaStream_t s);
 
+// Router projection (fixed fp32 summation order); from 256 tokens a tiled
+// kernel (same order) streams 32-token x 16-row tiles.
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
                           cudaStream_t s);

@@ -27,12 +27,9 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& v, float (&f)[8]) {
 }
 
 __device__ __forceinline__ uint2 quant8(const float (&f)[8], float scale) {
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) lo |= static_cast<uint32_t>(act_quant(f[i], scale)) << (8 * i);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) hi |= static_cast<uint32_t>(act_quant(f[4 + i], scale)) << (8 * i);
-  return make_uint2(lo, hi);
+  const float rs = __frcp_rn(scale);
+  return make_uint2(act_quant4(f[0], f[1], f[2], f[3], scale, rs),
+                    act_quant4(f[4], f[5], f[6], f[7], scale, rs));
 }
 
 __device__ __forceinline__ float half_warp_max(float v) {
@@ -106,35 +103,23 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
     logits[static_cast<int64_t>(row) * E + e] = __bfloat162float(r[e]);
 }
 
-// One warp per expert-ordered row: every 16-byte load of the row is issued
-// before any group is reduced (H <= 2*128*kGatherMaxPairs), so a warp keeps a
-// whole row in flight instead of one group pair.
+// Rows of up to 2*128*kGatherMaxPairs elements are held in registers.
 constexpr int kGatherMaxPairs = 16;  // H <= 4096
 
-__global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
-                                    int H, int k, const int32_t* __restrict__ sorted_pairs, int P,
-                                    int rows, uint8_t* __restrict__ xq, float* __restrict__ sx) {
+// One warp per token: x[t] is read and quantised once, then written to each
+// row the token occupies in expert order (inv_rows[t*k + j], j < k; skipped
+// when negative) and, with with_shared, to the shared-expert row P + t. Same
+// bytes as quantising each expert-ordered row, with the quantisation done
+// once per token instead of once per (token, expert) pair.
+__global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
+                                     int H, int k, const int32_t* __restrict__ inv_rows, int P,
+                                     int with_shared, uint8_t* __restrict__ xq,
+                                     float* __restrict__ sx) {
   const int G = H / 128, GP = (G + 1) / 2;
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  const int t = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (t >= T) return;
   const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-  int token;
-  if (row < P) {
-    const int p = sorted_pairs[row];
-    token = (p >= 0 && p < P) ? p / k : -1;
-  } else {
-    token = row - P;
-  }
-  uint8_t* qrow = xq + static_cast<int64_t>(row) * H;
-  float* srow = sx + static_cast<int64_t>(row) * G;
-  if (token < 0 || token >= T) {
-    for (int g = half; g < G; g += 2) {
-      reinterpret_cast<uint2*>(qrow + g * 128)[hl] = make_uint2(0, 0);
-      if (hl == 0) srow[g] = 0.f;
-    }
-    return;
-  }
-  const __nv_bfloat16* xr = x + static_cast<int64_t>(token) * x_stride;
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * x_stride;
   uint4 v[kGatherMaxPairs];
 #pragma unroll
   for (int i = 0; i < kGatherMaxPairs; ++i) {
@@ -142,20 +127,34 @@ __global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t
     v[i] = (i < GP && g < G) ? __ldg(reinterpret_cast<const uint4*>(xr + g * 128 + hl * 8))
                              : make_uint4(0, 0, 0, 0);
   }
+  uint2 qb[kGatherMaxPairs];
+  float scl[kGatherMaxPairs];
 #pragma unroll
   for (int i = 0; i < kGatherMaxPairs; ++i) {
-    if (i >= GP) break;
-    const int g = 2 * i + half;
-    float f[8];
-    unpack_bf16x8(v[i], f);
-    float amax = 0.f;
+    if (i < GP) {
+      float f[8];
+      unpack_bf16x8(v[i], f);
+      float amax = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
-    amax = half_warp_max(amax);
-    const float scale = act_scale_from_amax(amax);
-    if (g < G) {
-      *reinterpret_cast<uint2*>(qrow + g * 128 + hl * 8) = quant8(f, scale);
-      if (hl == 0) srow[g] = scale;
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+      amax = half_warp_max(amax);
+      scl[i] = act_scale_from_amax(amax);
+      qb[i] = quant8(f, scl[i]);
+    }
+  }
+  const int ndest = k + (with_shared ? 1 : 0);
+  for (int j = 0; j < ndest; ++j) {
+    const int d = j < k ? inv_rows[static_cast<int64_t>(t) * k + j] : P + t;
+    if (d < 0) continue;
+    uint8_t* qrow = xq + static_cast<int64_t>(d) * H;
+    float* srow = sx + static_cast<int64_t>(d) * G;
+#pragma unroll
+    for (int i = 0; i < kGatherMaxPairs; ++i) {
+      const int g = 2 * i + half;
+      if (i < GP && g < G) {
+        *reinterpret_cast<uint2*>(qrow + g * 128 + hl * 8) = qb[i];
+        if (hl == 0) srow[g] = scl[i];
+      }
     }
   }
 }
@@ -483,15 +482,13 @@ inline unsigned pair_blocks(int rows, int cols) {
 
 }  // namespace
 
-void launch_quant_gather(const void* x, int64_t x_stride, int T, int H, int k,
-                         const int32_t* sorted_pairs, int P, int with_shared, uint8_t* xq,
-                         float* sx, cudaStream_t s) {
-  const int rows = P + (with_shared ? T : 0);
-  if (rows <= 0) return;
-  const unsigned blocks = static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps);
-  quant_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                                       x_stride, T, H, k, sorted_pairs, P, rows,
-                                                       xq, sx);
+void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
+                          const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
+                          cudaStream_t s) {
+  if (T <= 0) return;
+  const unsigned blocks = static_cast<unsigned>((T + kRowWarps - 1) / kRowWarps);
+  quant_scatter_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride, T, H,
+                                              k, inv_rows, P, with_shared, xq, sx);
 }
 
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,

@@ -332,9 +332,10 @@ __device__ __forceinline__ void consume_group(const EngineArgs& args, const Cons
           for (int w2 = 0; w2 < kEngineConsumerWarps; ++w2)
             am = fmaxf(am, cx.amax_sm[w2 * kTokensPerGroup + t]);
           const float sc = act_scale_from_amax(am);
+          const float rs = __frcp_rn(sc);
           uint8_t* qrow = args.out_q + static_cast<int64_t>(out_row0 + t) * I;
-          qrow[col0] = act_quant(acc[0][c][u], sc);
-          qrow[col0 + 8] = act_quant(acc[0][c][u + 2], sc);
+          qrow[col0] = f32_to_e4m3(act_quant_value(acc[0][c][u], sc, rs));
+          qrow[col0 + 8] = f32_to_e4m3(act_quant_value(acc[0][c][u + 2], sc, rs));
           if (warp == 0 && g == 0)
             args.out_qs[static_cast<int64_t>(out_row0 + t) * (I / 128) + w.tile] = sc;
         }

@@ -3,7 +3,7 @@
 // Pipeline for T tokens, top-k, E experts (P = T*k pairs, R = P + T rows when
 // a shared expert runs):
 //   1. permute      ids -> counts, starts, sorted pairs, inverse rows, active list
-//   2. quant_gather x -> e4m3 rows in expert order (+ T shared rows), scales
+//   2. quant_scatter x -> e4m3 rows in expert order (+ T shared rows), scales
 //   3. gate_up      engine EPI_GATE_UP: a e4m3 [R, I], sa [R, I/128]
 //   4. down         engine EPI_DOWN:    d f32 [R, H]
 //   5. combine      routed/shared/out bf16 [T, H] in fixed rank order
@@ -216,8 +216,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
                         b.inv, b.active, b.n_active, s, b.permute_scratch);
     if (rc) return rc;
   }
-  launch_quant_gather(x, x_stride, T, H, k, b.sorted, P, has_shared, b.xq, b.sx, s);
-  if ((rc = check_launch("quant_gather"))) return rc;
+  launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s);
+  if ((rc = check_launch("quant_scatter"))) return rc;
 
   const int sms = sm_count();
   stage_mark(1, s);

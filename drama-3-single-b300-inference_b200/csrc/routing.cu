@@ -66,11 +66,7 @@ __global__ void __launch_bounds__(256)
         for (int u = 0; u < 4; ++u) {
           const uint32_t xx[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            acc[u] = fmaf(__uint_as_float(ww[j] << 16), __uint_as_float(xx[j] << 16), acc[u]);
-            acc[u] = fmaf(__uint_as_float(ww[j] & 0xffff0000u),
-                          __uint_as_float(xx[j] & 0xffff0000u), acc[u]);
-          }
+          for (int j = 0; j < 4; ++j) acc[u] = fma_bf16x2_seq(xx[j], ww[j], acc[u]);
         }
       }
     }
@@ -162,12 +158,8 @@ __global__ void __launch_bounds__(kRtThreads)
 #pragma unroll
           for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              float& a = acc[u][8 * h + r];
-              a = fmaf(__uint_as_float(ww[r][j] << 16), __uint_as_float(xx[u][j] << 16), a);
-              a = fmaf(__uint_as_float(ww[r][j] & 0xffff0000u),
-                       __uint_as_float(xx[u][j] & 0xffff0000u), a);
-            }
+            for (int r = 0; r < 8; ++r)
+              acc[u][8 * h + r] = fma_bf16x2_seq(xx[u][j], ww[r][j], acc[u][8 * h + r]);
       }
     }
     __syncthreads();
@@ -753,7 +745,9 @@ using namespace d3;
 extern "C" int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H,
                                 int T, void* logits, int64_t logits_stride, d3_stream_t stream) {
   D3_REQUIRE(T >= 0 && R > 0 && H > 0 && H % 128 == 0, "router_logits: bad shape R=%d H=%d", R, H);
-  D3_REQUIRE(H <= 256 * kRouterMaxIters, "router_logits: H=%d above the %d this kernel holds in registers", H, 256 * kRouterMaxIters);
+  D3_REQUIRE(T >= kRouterTiledMinTokens || H <= 256 * kRouterMaxIters,
+             "router_logits: H=%d above the %d the decode kernel holds in registers", H,
+             256 * kRouterMaxIters);
   D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "router_logits: x row stride must be >= H and a multiple of 8");
   D3_REQUIRE(logits_stride >= R, "router_logits: logits row stride must be >= R");
   D3_REQUIRE(aligned(x, 16) && aligned(w, 16), "router_logits: misaligned pointer");

@@ -319,14 +319,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
               for (int c = 0; c < 4; ++c) {
                 const uint4 v = hrow[(4 * c8 + c) ^ sw];
-                const float x[4] = {__uint_as_float(v.x), __uint_as_float(v.y),
-                                    __uint_as_float(v.z), __uint_as_float(v.w)};
-                float qv[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  qv[e] = fminf(fmaxf(div_by_scale(x[e], sc, rs), -448.0f), 448.0f);
-                word[c] = static_cast<uint32_t>(f32x2_to_e4m3x2(qv[0], qv[1])) |
-                          (static_cast<uint32_t>(f32x2_to_e4m3x2(qv[2], qv[3])) << 16);
+                word[c] = act_quant4(__uint_as_float(v.x), __uint_as_float(v.y),
+                                     __uint_as_float(v.z), __uint_as_float(v.w), sc, rs);
               }
               q[c8] = make_uint4(word[0], word[1], word[2], word[3]);
             }
@@ -384,17 +378,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();  // the TMEM loads below are warp-collective
         tc::fence_after_thread_sync();
         const uint32_t tl = tbase + b * 256 + (static_cast<uint32_t>(quad * 32) << 16);
+        // four 16-column quarters of both runs, software-pipelined: the loads
+        // of quarter q+1 are in flight while quarter q is folded in
+        float qa[2][16], qb[2][16];
+        tc::tmem_ld_32x32b_x16(tl + c0, qa[0]);
+        tc::tmem_ld_32x32b_x16(tl + c1, qb[0]);
+        tc::tmem_ld_wait_regs(qa[0], qb[0]);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float r0[32], r1[32];
-          tc::tmem_ld_32x32b_x32(tl + c0 + 32 * h, r0);
-          tc::tmem_ld_32x32b_x32(tl + c1 + 32 * h, r1);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            ffma2(acc0[32 * h + j], acc0[32 * h + j + 1], r0[j], r0[j + 1], f0);
-            ffma2(acc1[32 * h + j], acc1[32 * h + j + 1], r1[j], r1[j + 1], f1);
+        for (int q = 0; q < 4; ++q) {
+          if (q < 3) {
+            tc::tmem_ld_32x32b_x16(tl + c0 + 16 * (q + 1), qa[(q + 1) & 1]);
+            tc::tmem_ld_32x32b_x16(tl + c1 + 16 * (q + 1), qb[(q + 1) & 1]);
           }
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            ffma2(acc0[16 * q + j], acc0[16 * q + j + 1], qa[q & 1][j], qa[q & 1][j + 1], f0);
+            ffma2(acc1[16 * q + j], acc1[16 * q + j + 1], qb[q & 1][j], qb[q & 1][j + 1], f1);
+          }
+          if (q < 3) tc::tmem_ld_wait_regs(qa[(q + 1) & 1], qb[(q + 1) & 1]);
         }
         tc::fence_before_thread_sync();
         __syncwarp();

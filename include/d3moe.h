@@ -89,6 +89,7 @@ D3_API int d3_prepare_moe_input(const void* x, int64_t x_stride, const void* rou
 D3_API int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H, int T,
                      void* logits, int64_t logits_stride, d3_stream_t stream);
 
+
 /* ------------------------------------------------------------ (a2) route --
  * fp32 softmax over E logits, top-k by (logit, lower index first), weights
  * renormalised over the k picks. logits bf16 or f32 [T,E] with row stride;

@@ -68,9 +68,10 @@ def test_quant_act_matches_oracle_bytes(d3, T):
 # ------------------------------------------------------------------- (a1) --
 # T >= 256 runs the tiled prefill kernel (32-token x 16-row tiles through a
 # cp.async ring) in the same summation order; 300 and 129/33 rows leave ragged
-# tiles, H=384 a half-filled last 256-wide block.
+# tiles, H=384 a half-filled last 256-wide block, H=4096 is beyond the decode
+# kernel's register-held weight row.
 @pytest.mark.parametrize("T,R,H", [(1, 129, 2048), (64, 129, 2048), (13, 257, 2048), (5, 33, 384),
-                                   (256, 129, 2048), (300, 129, 2048), (513, 33, 384)])
+                                   (256, 129, 2048), (300, 129, 2048), (513, 33, 384), (260, 17, 4096)])
 def test_router_logits_bit_exact(d3, T, R, H):
     rng = np.random.default_rng(R + T)
     x = O.bf16_round(rng.standard_normal((T, H)).astype(np.float32))

@@ -28,8 +28,8 @@ def _fma32(a, b, c):
 
 def test_corrected_reciprocal_division_is_ieee_division():
     """The prefill epilogue quantises x / scale as q0 = x * rs, r = fma(-q0,
-    scale, x), q = fma(r, rs, q0) with rs = RN(1/scale) (Markstein's
-    correction). Over the quantiser's domain (scale = max(amax,1e-10)/448,
+    scale, x), q = r == 0 ? q0 : fma(r, rs, q0) with rs = RN(1/scale)
+    (Markstein's correction). Over the quantiser's domain (scale = max(amax,1e-10)/448,
     |x| <= amax) that must equal IEEE float32 division bit for bit."""
     rng = np.random.default_rng(0)
     n = 400_000
@@ -38,10 +38,12 @@ def test_corrected_reciprocal_division_is_ieee_division():
     x = (amax * rng.uniform(-1, 1, n)).astype(f32)
     x[:500], x[500:1000] = amax[:500], -amax[500:1000]      # the group maximum itself
     x[1000:1500] = (amax[1000:1500] * f32(2.0 ** -20)).astype(f32)  # tiny members
+    x[1500:1600], x[1600:1700] = f32(0.0), f32(-0.0)  # signed zeros keep their sign
     sc = (np.maximum(amax, f32(1e-10)) / f32(448)).astype(f32)
     rs = (f32(1) / sc).astype(f32)
     ieee = (x / sc).astype(f32)
     q0 = (x * rs).astype(f32)
-    q = _fma32(_fma32(-q0, sc, x), rs, q0)
+    r = _fma32(-q0, sc, x)
+    q = np.where(r == 0, q0, _fma32(r, rs, q0))
     np.testing.assert_array_equal(q.view(np.uint32), ieee.view(np.uint32))
     assert (q0 != ieee).any()  # the correction is doing work
