@@ -645,8 +645,8 @@ def main() -> None:
                   None if ids_buf is None else ids_buf.data_ptr(), wts.data_ptr(),
                   ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), sptr)
 
-    # (act prep + engine) x 2 GEMVs; router, route+permute, gather, gate_up, down, combine
-    launches_per_step = 2 * 2 + 6
+    # (act prep + engine) x 2 GEMVs; router, route, permute, quant_scatter, gate_up, down, combine
+    launches_per_step = 2 * 2 + 7
 
     # per-step stage events (gate_up / down engine launches) inside the timed region
     stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
@@ -758,7 +758,7 @@ def main() -> None:
                             "algorithmic_bytes_per_launch": down_bytes},
             "moe_layer_ms": statistics.mean(moe_ms),
             "stage_ms": {"qkv_gemv": statistics.mean(qkv_ms), "o_proj_gemv": statistics.mean(oproj_ms),
-                         "router_route_permute_gather": statistics.mean(pre_ms),
+                         "router_route_permute_quant": statistics.mean(pre_ms),
                          "gate_up": gate_avg, "down": down_avg, "combine": statistics.mean(post_ms)},
             "step_bytes": total_bytes,
             "step_achieved_gbs": total_bytes / (ms * 1e-3) / 1e9,

@@ -71,7 +71,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         subprocess.run(cmd, check=True)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [cc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs, "-lcudart"]
+    cmd = [cc, *ARCH_FLAGS, "-shared", "-Xlinker", "--no-undefined", "-o", str(tmp), *objs, "-lcudart"]
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB)
     return LIB

@@ -38,7 +38,7 @@ void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int
                        const float* bias, int64_t* ids, void* weights, int weights_dtype,
                        cudaStream_t s);
 
-// route_topk + permute; one fused single-CTA kernel when T*k <= 4096.
+// route_topk followed by permute (two launches).
 int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, int T, int E,
                          int k, const float* bias, int64_t* ids, void* weights, int weights_dtype,
                          int block_m, int32_t* counts, int32_t* starts, int32_t* total,

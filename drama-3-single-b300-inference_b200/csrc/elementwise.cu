@@ -103,59 +103,40 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
     logits[static_cast<int64_t>(row) * E + e] = __bfloat162float(r[e]);
 }
 
-// Rows of up to 2*128*kGatherMaxPairs elements are held in registers.
-constexpr int kGatherMaxPairs = 16;  // H <= 4096
-
-// One warp per token: x[t] is read and quantised once, then written to each
-// row the token occupies in expert order (inv_rows[t*k + j], j < k; skipped
-// when negative) and, with with_shared, to the shared-expert row P + t. Same
-// bytes as quantising each expert-ordered row, with the quantisation done
-// once per token instead of once per (token, expert) pair.
+// One warp per (token, pair of 128-groups): the two groups of x[t] are read
+// and quantised once, then written to each row the token occupies in expert
+// order (inv_rows[t*k + j], j < k; skipped when negative) and, with
+// with_shared, to the shared-expert row P + t. Same bytes as quantising each
+// expert-ordered row, with the quantisation done once per token instead of
+// once per (token, expert) pair.
 __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                      int H, int k, const int32_t* __restrict__ inv_rows, int P,
                                      int with_shared, uint8_t* __restrict__ xq,
                                      float* __restrict__ sx) {
-  const int G = H / 128, GP = (G + 1) / 2;
-  const int t = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int G = H / 128;
+  const RowPair rp = row_pair(G);
+  const int t = rp.row;
   if (t >= T) return;
   const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-  const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * x_stride;
-  uint4 v[kGatherMaxPairs];
+  const int g = 2 * rp.gp + half;
+  const bool valid = g < G;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * x_stride + g * 128 + hl * 8));
+  float f[8];
+  unpack_bf16x8(v, f);
+  float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < kGatherMaxPairs; ++i) {
-    const int g = 2 * i + half;
-    v[i] = (i < GP && g < G) ? __ldg(reinterpret_cast<const uint4*>(xr + g * 128 + hl * 8))
-                             : make_uint4(0, 0, 0, 0);
-  }
-  uint2 qb[kGatherMaxPairs];
-  float scl[kGatherMaxPairs];
-#pragma unroll
-  for (int i = 0; i < kGatherMaxPairs; ++i) {
-    if (i < GP) {
-      float f[8];
-      unpack_bf16x8(v[i], f);
-      float amax = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
-      amax = half_warp_max(amax);
-      scl[i] = act_scale_from_amax(amax);
-      qb[i] = quant8(f, scl[i]);
-    }
-  }
+  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+  amax = half_warp_max(amax);
+  const float scale = act_scale_from_amax(amax);
+  const uint2 qb = quant8(f, scale);
+  if (!valid) return;
   const int ndest = k + (with_shared ? 1 : 0);
   for (int j = 0; j < ndest; ++j) {
-    const int d = j < k ? inv_rows[static_cast<int64_t>(t) * k + j] : P + t;
+    const int d = j < k ? __ldg(inv_rows + static_cast<int64_t>(t) * k + j) : P + t;
     if (d < 0) continue;
-    uint8_t* qrow = xq + static_cast<int64_t>(d) * H;
-    float* srow = sx + static_cast<int64_t>(d) * G;
-#pragma unroll
-    for (int i = 0; i < kGatherMaxPairs; ++i) {
-      const int g = 2 * i + half;
-      if (i < GP && g < G) {
-        *reinterpret_cast<uint2*>(qrow + g * 128 + hl * 8) = qb[i];
-        if (hl == 0) srow[g] = scl[i];
-      }
-    }
+    *reinterpret_cast<uint2*>(xq + static_cast<int64_t>(d) * H + g * 128 + hl * 8) = qb;
+    if (hl == 0) sx[static_cast<int64_t>(d) * G + g] = scale;
   }
 }
 
@@ -486,8 +467,7 @@ void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
                           cudaStream_t s) {
   if (T <= 0) return;
-  const unsigned blocks = static_cast<unsigned>((T + kRowWarps - 1) / kRowWarps);
-  quant_scatter_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride, T, H,
+  quant_scatter_kernel<<<pair_blocks(T, H), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride, T, H,
                                               k, inv_rows, P, with_shared, xq, sx);
 }
 

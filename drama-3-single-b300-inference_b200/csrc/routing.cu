@@ -552,31 +552,6 @@ __global__ void __launch_bounds__(kPermuteThreads)
   }
 }
 
-// Decode-size fusion of route_topk and permute in one CTA: the ids never leave
-// shared memory between the two. T*k <= kFusedMaxPairs.
-constexpr int kFusedMaxPairs = 4096;
-
-template <int PER_LANE>
-__global__ void __launch_bounds__(kPermuteThreads)
-    route_permute_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T, int E,
-                         int k, const float* __restrict__ bias, int64_t* __restrict__ ids,
-                         void* __restrict__ weights, int f32_out, int bm,
-                         int32_t* __restrict__ counts, int32_t* __restrict__ starts,
-                         int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
-                         int32_t* __restrict__ expert_ids, int64_t max_rows,
-                         int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
-                         int32_t* __restrict__ n_active) {
-  extern __shared__ int sm[];
-  int* ids_s = sm;                     // [kFusedMaxPairs]
-  int* work = sm + kFusedMaxPairs;     // permute scratch
-  for (int t = threadIdx.x >> 5; t < T; t += kPermuteThreads / 32)
-    route_token<PER_LANE>(logits, f32_in, stride, t, E, k, bias, ids, weights, f32_out, ids_s);
-  __syncthreads();
-  auto id_at = [&](int p) -> int { return ids_s[p]; };
-  permute_body(id_at, T * k, E, bm, work, counts, starts, total_out, sorted_ids, expert_ids,
-               max_rows, inv_rows, active, n_active);
-}
-
 // Expert-parallel dispatch plan. Experts are owned contiguously by ranks
 // (rank = id / experts_per_rank). Pairs are bucketed by destination rank with
 // the same stable counting sort as permute (ascending pair order within a
@@ -663,34 +638,13 @@ int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, i
                          int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s,
                          int32_t* scratch) {
   if (T <= 0) return D3_OK;
-  if (static_cast<int64_t>(T) * k > kFusedMaxPairs) {
-    launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype, s);
-    int rc = check_launch("route_topk");
-    if (rc) return rc;
-    return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
-                          max_rows, inv_rows, active, n_active, s, scratch);
-  }
-  const size_t smem = (static_cast<size_t>(kFusedMaxPairs) + static_cast<size_t>(E) * 35) * sizeof(int);
-  const int f32_in = logits_dtype == D3_DTYPE_F32, f32_out = weights_dtype == D3_DTYPE_F32;
-  const int per_lane = (E + 31) / 32;
-  auto launch = [&](auto kern) -> int {
-    static int configured[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && configured[dev] < static_cast<int>(smem)) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(smem)) != cudaSuccess)
-        return set_error(D3_ECUDA, "route_permute: cannot raise the shared-memory limit");
-      configured[dev] = static_cast<int>(smem);
-    }
-    kern<<<1, kPermuteThreads, smem, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights,
-                                          f32_out, block_m, counts, starts, total, sorted_ids,
-                                          expert_ids, max_rows, inv_rows, active, n_active);
-    return check_launch("route_permute");
-  };
-  if (per_lane <= 4) return launch(route_permute_kernel<4>);
-  if (per_lane <= 8) return launch(route_permute_kernel<8>);
-  return launch(route_permute_kernel<kMaxPerLane>);
+  // routing spreads tokens over many CTAs (a warp each); a single-CTA fusion
+  // of routing and bucketing measured slower than the two launches
+  launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype, s);
+  int rc = check_launch("route_topk");
+  if (rc) return rc;
+  return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
+                        max_rows, inv_rows, active, n_active, s, scratch);
 }
 
 size_t permute_scratch_ints(int E) { return static_cast<size_t>(kMaxPermuteChunks) * E; }
