@@ -1,6 +1,7 @@
 // Error string, launch checks, SM count and tensor-map encoding for the C ABI.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -41,6 +42,14 @@ int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(D3_ECUDA, "%s: %s", what, cudaGetErrorString(e));
   return D3_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("D3MOE_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 int sm_count() {

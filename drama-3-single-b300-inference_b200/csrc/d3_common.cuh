@@ -30,6 +30,17 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
   return t;
 }
 
+// Programmatic dependent launch. Every kernel of this library calls pdl_wait()
+// before it reads anything a preceding kernel wrote: when it was launched
+// with programmatic stream serialisation it may have started while that
+// kernel was still running, and the wait returns once the predecessor has
+// completed and its writes are visible (a no-op otherwise). pdl_trigger()
+// lets the next kernel of the stream begin launching early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

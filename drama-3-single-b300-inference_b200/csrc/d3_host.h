@@ -27,6 +27,31 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t 
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Whether kernels are launched with programmatic stream serialisation (PDL):
+// on unless D3MOE_PDL=0 in the environment (read once).
+bool pdl_enabled();
+
+// Launches kern<<<grid, block, smem, s>>>(args...) through cudaLaunchKernelEx
+// with programmatic stream serialisation, so its launch and prologue overlap
+// the tail of the previous kernel in the stream; every kernel of this library
+// calls pdl_wait() before touching memory earlier kernels wrote. Errors are
+// left for check_launch() like a <<<>>> launch.
+template <typename... KArgs, typename... Args>
+void launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                   Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }

@@ -73,6 +73,7 @@ __device__ __forceinline__ RowPair row_pair(int G) {
 __global__ void quant_act_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                  int H, uint8_t* __restrict__ q, float* __restrict__ scales,
                                  int transposed) {
+  pdl_wait();
   const int G = H / 128;
   const RowPair rp = row_pair(G);
   if (rp.row >= T) return;
@@ -86,6 +87,7 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
                                int T, int H, int E, const void* row_slots, int slots64,
                                int64_t padding_start, uint8_t* __restrict__ q,
                                float* __restrict__ scales_t, float* __restrict__ logits) {
+  pdl_wait();
   const int G = H / 128;
   const RowPair rp = row_pair(G);
   const int row = rp.row;
@@ -113,6 +115,7 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
                                      int H, int k, const int32_t* __restrict__ inv_rows, int P,
                                      int with_shared, uint8_t* __restrict__ xq,
                                      float* __restrict__ sx) {
+  pdl_wait();
   const int G = H / 128;
   const RowPair rp = row_pair(G);
   const int t = rp.row;
@@ -146,6 +149,7 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
 // (expert_gemv.cuh).
 __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                       int K, __half* __restrict__ xh, float* __restrict__ inv) {
+  pdl_wait();
   const int G = K / 128;
   const RowPair rp = row_pair(G);
   const int row = rp.row;
@@ -191,6 +195,7 @@ __device__ __forceinline__ float silu_bf16(float gate_bf16) {
 
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride, int rows,
                                 int W, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = W / 8;
   if (idx >= static_cast<int64_t>(rows) * per_row) return;
@@ -213,6 +218,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t in
 __global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride,
                                       int rows, int W, uint8_t* __restrict__ q,
                                       float* __restrict__ scales) {
+  pdl_wait();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int G = W / 128;
@@ -254,6 +260,7 @@ __global__ void combine_experts_kernel(const __nv_bfloat16* __restrict__ routed,
                                        const __nv_bfloat16* __restrict__ shared,
                                        const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                        int T, int H, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = H / 8;
   if (idx >= static_cast<int64_t>(T) * per_row) return;
@@ -282,6 +289,7 @@ __global__ void combine_rows_kernel(const float* __restrict__ d, int H,
                                     int64_t gate_stride, __nv_bfloat16* __restrict__ routed_out,
                                     __nv_bfloat16* __restrict__ shared_out,
                                     __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = H / 4;
   if (idx >= static_cast<int64_t>(T) * per_row) return;
@@ -334,6 +342,7 @@ __global__ void combine_rows_kernel(const float* __restrict__ d, int H,
 // One CTA per 128x128 weight block; 256 threads x 64 elements.
 __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, int K,
                                     uint8_t* __restrict__ q, float* __restrict__ scales) {
+  pdl_wait();
   const int nb = blockIdx.x, kb = blockIdx.y, KB = K / 128;
   __shared__ float red[8];
   const int tid = threadIdx.x;
@@ -382,6 +391,7 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, 
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t src_stride,
                                    int T, int H, int k, const int32_t* __restrict__ sorted_pairs,
                                    int rows, __nv_bfloat16* __restrict__ dst) {
+  pdl_wait();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int p = sorted_pairs[row];
@@ -400,6 +410,7 @@ __global__ void combine_pairs_kernel(const __nv_bfloat16* __restrict__ rows, int
                                      const __nv_bfloat16* __restrict__ shared,
                                      const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                      __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = H / 8;
   if (idx >= static_cast<int64_t>(T) * per_row) return;
@@ -442,6 +453,7 @@ __global__ void ep_dispatch_meta_kernel(const int64_t* __restrict__ ids,
                                         int experts_per_rank, int ranks,
                                         int64_t* __restrict__ meta_ids,
                                         __nv_bfloat16* __restrict__ meta_w) {
+  pdl_wait();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n = static_cast<int64_t>(ranks) * T * k;
   if (idx >= n) return;
@@ -467,14 +479,14 @@ void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
                           cudaStream_t s) {
   if (T <= 0) return;
-  quant_scatter_kernel<<<pair_blocks(T, H), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride, T, H,
+  launch_kernel(quant_scatter_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), x_stride, T, H,
                                               k, inv_rows, P, with_shared, xq, sx);
 }
 
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
                            cudaStream_t s) {
   if (T <= 0) return;
-  dense_act_prep_kernel<<<pair_blocks(T, K), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+  launch_kernel(dense_act_prep_kernel, dim3(pair_blocks(T, K)), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x),
                                                       x_stride, T, K, xh, inv);
 }
 
@@ -483,7 +495,7 @@ void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const v
                          void* routed_out, void* shared_out, void* out, cudaStream_t s) {
   const int64_t n = static_cast<int64_t>(T) * (H / 4);
   if (n <= 0) return;
-  combine_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+  launch_kernel(combine_rows_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s, 
       d, H, inv_rows, static_cast<const __nv_bfloat16*>(weights), T, k, with_shared,
       static_cast<const __nv_bfloat16*>(gate), gate_stride,
       static_cast<__nv_bfloat16*>(routed_out), static_cast<__nv_bfloat16*>(shared_out),
@@ -500,7 +512,7 @@ extern "C" int d3_quant_act_fp8(const void* x, int64_t x_stride, int T, int H, u
   D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "quant_act_fp8: x row stride %lld must be >= H and a multiple of 8", (long long)x_stride);
   D3_REQUIRE(aligned(x, 16) && aligned(q, 16) && aligned(scales, 4), "quant_act_fp8: misaligned pointer");
   if (T == 0) return D3_OK;
-  quant_act_kernel<<<pair_blocks(T, H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(quant_act_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(x), x_stride, T, H, q, scales, scales_transposed);
   return check_launch("quant_act_fp8");
 }
@@ -516,7 +528,7 @@ extern "C" int d3_prepare_moe_input(const void* x, int64_t x_stride, const void*
   D3_REQUIRE((row_slots == nullptr) == (padding_start <= 0), "prepare_moe_input: reserved padding routing needs both row_slots and padding_start > 0");
   D3_REQUIRE(aligned(x, 16) && aligned(q, 16), "prepare_moe_input: misaligned pointer");
   if (T == 0) return D3_OK;
-  prepare_kernel<<<pair_blocks(T, H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(prepare_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(router),
       router_stride, T, H, E, row_slots, row_slots_int64, padding_start, q, scales_t, logits);
   return check_launch("prepare_moe_input");
@@ -529,8 +541,7 @@ extern "C" int d3_silu_mul(const void* in, int64_t in_stride, int rows, int W, v
   D3_REQUIRE(aligned(in, 16) && aligned(out, 16), "silu_mul: misaligned pointer");
   const int64_t n = static_cast<int64_t>(rows) * (W / 8);
   if (n == 0) return D3_OK;
-  silu_mul_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
-                    reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(silu_mul_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(in), in_stride, rows, W, static_cast<__nv_bfloat16*>(out));
   return check_launch("silu_mul");
 }
@@ -541,7 +552,7 @@ extern "C" int d3_silu_mul_quant(const void* in, int64_t in_stride, int rows, in
   D3_REQUIRE(in_stride >= 2 * W && in_stride % 8 == 0, "silu_mul_quant: input row stride must be >= 2W and a multiple of 8");
   D3_REQUIRE(aligned(in, 16) && aligned(q, 16), "silu_mul_quant: misaligned pointer");
   if (rows == 0) return D3_OK;
-  silu_mul_quant_kernel<<<row_blocks(rows), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(silu_mul_quant_kernel, dim3(row_blocks(rows)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(in), in_stride, rows, W, q, scales);
   return check_launch("silu_mul_quant");
 }
@@ -553,8 +564,7 @@ extern "C" int d3_combine_experts(const void* routed, const void* shared, const 
   D3_REQUIRE(aligned(routed, 16) && aligned(shared, 16) && aligned(out, 16), "combine_experts: misaligned pointer");
   const int64_t n = static_cast<int64_t>(T) * (H / 8);
   if (n == 0) return D3_OK;
-  combine_experts_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
-                           reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(combine_experts_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(routed), static_cast<const __nv_bfloat16*>(shared),
       static_cast<const __nv_bfloat16*>(gate), gate_stride, T, H,
       static_cast<__nv_bfloat16*>(out));
@@ -566,7 +576,7 @@ extern "C" int d3_fp8_quantize_weight(const void* w, int N, int K, uint8_t* q, f
   D3_REQUIRE(N > 0 && K > 0 && K % 128 == 0, "fp8_quantize_weight: K=%d must be a positive multiple of 128", K);
   D3_REQUIRE(aligned(w, 16) && aligned(q, 16), "fp8_quantize_weight: misaligned pointer");
   dim3 grid((N + 127) / 128, K / 128);
-  weight_quant_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(weight_quant_kernel, dim3(grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(w), N, K, q, scales);
   return check_launch("fp8_quantize_weight");
 }
@@ -578,7 +588,7 @@ extern "C" int d3_gather_rows(const void* src, int64_t src_stride, int T, int H,
   D3_REQUIRE(src_stride >= H && src_stride % 8 == 0, "gather_rows: src row stride must be >= H and a multiple of 8");
   D3_REQUIRE(aligned(src, 16) && aligned(dst, 16), "gather_rows: misaligned pointer");
   if (rows == 0) return D3_OK;
-  gather_rows_kernel<<<row_blocks(rows), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(gather_rows_kernel, dim3(row_blocks(rows)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(src), src_stride, T, H, k, sorted_pairs, rows,
       static_cast<__nv_bfloat16*>(dst));
   return check_launch("gather_rows");
@@ -591,8 +601,7 @@ extern "C" int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const
   D3_REQUIRE(aligned(rows, 16) && aligned(out, 16) && (!shared || aligned(shared, 16)), "combine_pairs: misaligned pointer");
   const int64_t n = static_cast<int64_t>(T) * (H / 8);
   if (n == 0) return D3_OK;
-  combine_pairs_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
-                         reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(combine_pairs_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(rows), H, inv_rows, static_cast<const __nv_bfloat16*>(weights),
       T, k, static_cast<const __nv_bfloat16*>(shared), static_cast<const __nv_bfloat16*>(gate),
       gate_stride, static_cast<__nv_bfloat16*>(out));
@@ -605,8 +614,7 @@ extern "C" int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int 
   D3_REQUIRE(T >= 0 && k > 0 && experts_per_rank > 0 && ranks > 0, "ep_dispatch_meta: bad arguments");
   const int64_t n = static_cast<int64_t>(ranks) * T * k;
   if (n == 0) return D3_OK;
-  ep_dispatch_meta_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
-                            reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(ep_dispatch_meta_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
       ids, static_cast<const __nv_bfloat16*>(weights), T, k, experts_per_rank, ranks, meta_ids,
       static_cast<__nv_bfloat16*>(meta_w));
   return check_launch("ep_dispatch_meta");

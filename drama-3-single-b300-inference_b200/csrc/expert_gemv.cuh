@@ -470,6 +470,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();  // routing metadata, activations and outputs belong to earlier kernels
 
   if (warp == kEngineConsumerWarps) {
     // ------------------------------------------------------------ producer --
@@ -570,6 +571,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
       }
       if (!have) break;
     }
+    pdl_trigger();  // every load of this CTA is issued: the next kernel may start launching
     // Never leave the CTA while a copy may still be writing its shared memory.
     asm volatile("cp.async.wait_all;" ::: "memory");
     if (leader)

@@ -118,7 +118,7 @@ int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUt
       return set_error(D3_ECUDA, "engine: cannot reserve %zu bytes of shared memory", smem);
     if (dev >= 0 && dev < 64) configured[dev] = static_cast<int>(smem);
   }
-  kern<<<grid, kEngineThreads, smem, s>>>(tw, twsh, ta, args);
+  launch_kernel(kern, dim3(grid), dim3(kEngineThreads), smem, s, tw, twsh, ta, args);
   return check_launch("expert engine");
 }
 
@@ -179,7 +179,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& t
       return set_error(D3_ECUDA, "tc grouped GEMM: cannot reserve %zu bytes of shared memory", smem);
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
-  kern<<<grid, kTcThreads, smem, s>>>(ta, tw, twsh, args);
+  launch_kernel(kern, dim3(grid), dim3(kTcThreads), smem, s, ta, tw, twsh, args);
   return check_launch("tc grouped GEMM");
 }
 

@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(256)
                          const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
                          int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
                          int64_t out_stride) {
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,6 +102,7 @@ __global__ void __launch_bounds__(kRtThreads)
                                const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
                                int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
                                int64_t out_stride) {
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -289,6 +291,7 @@ template <int PER_LANE>
 __global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T,
                              int E, int k, const float* __restrict__ bias,
                              int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out) {
+  pdl_wait();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
   route_token<PER_LANE>(logits, f32_in, stride, t, E, k, bias, ids, weights, f32_out, nullptr);
@@ -419,6 +422,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
                    int32_t* __restrict__ expert_ids, int64_t max_rows,
                    int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
                    int32_t* __restrict__ n_active) {
+  pdl_wait();
   extern __shared__ int sm[];
   auto id_at = [&](int p) -> int {
     const int64_t v = ids[p];
@@ -449,6 +453,7 @@ inline int permute_chunk_pairs(int P) {
 __global__ void __launch_bounds__(kPermuteThreads)
     permute_hist_kernel(const int64_t* __restrict__ ids, int P, int E, int chunk,
                         int32_t* __restrict__ cc) {
+  pdl_wait();
   extern __shared__ int cnt[];
   for (int e = threadIdx.x; e < E; e += kPermuteThreads) cnt[e] = 0;
   __syncthreads();
@@ -468,6 +473,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
                         int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
                         int32_t* __restrict__ expert_ids, int64_t max_rows,
                         int32_t* __restrict__ active, int32_t* __restrict__ n_active) {
+  pdl_wait();
   __shared__ int warp_tot[33];
   __shared__ int s_cnt[1024], s_start[1024];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -514,6 +520,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
     permute_scatter_kernel(const int64_t* __restrict__ ids, int P, int E, int chunk,
                            const int32_t* __restrict__ cc, int32_t* __restrict__ sorted_ids,
                            int32_t* __restrict__ inv_rows) {
+  pdl_wait();
   extern __shared__ int sm[];
   int* cursor = sm;        // [E]
   int* wcnt = sm + E;      // [32][E]
@@ -562,6 +569,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
                    int32_t* __restrict__ total, int32_t* __restrict__ sorted_pairs,
                    int32_t* __restrict__ scratch_tiles, int32_t* __restrict__ inv_rows,
                    int64_t* __restrict__ local_ids) {
+  pdl_wait();
   extern __shared__ int sm[];
   const int E = experts_per_rank * ranks;
   auto id_at = [&](int p) -> int {
@@ -584,7 +592,7 @@ int launch_ep_plan(const int64_t* ids, int P, int experts_per_rank, int ranks,
                    int32_t* sorted_pairs, int32_t* scratch_tiles, int32_t* inv_rows,
                    int64_t* local_ids, cudaStream_t s) {
   const size_t smem = static_cast<size_t>(ranks) * 35 * sizeof(int);
-  ep_plan_kernel<<<1, kPermuteThreads, smem, s>>>(ids, P, experts_per_rank, ranks, send_counts,
+  launch_kernel(ep_plan_kernel, dim3(1), dim3(kPermuteThreads), smem, s, ids, P, experts_per_rank, ranks, send_counts,
                                                   send_starts, total, sorted_pairs, scratch_tiles,
                                                   inv_rows, local_ids);
   return check_launch("ep_plan");
@@ -604,14 +612,14 @@ void launch_router_logits(const void* x, int64_t x_stride, const void* w, const 
       if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     dim3 grid((R + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
-    router_logits_tiled_kernel<<<grid, kRtThreads, kRtSmem, s>>>(
+    launch_kernel(router_logits_tiled_kernel, dim3(grid), dim3(kRtThreads), kRtSmem, s, 
         static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
         nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
     return;
   }
   dim3 grid((R + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
   const size_t smem = static_cast<size_t>(kRouterTokens) * H * 2;  // <= 48 KB for H <= 3072
-  router_logits_kernel<<<grid, 256, smem, s>>>(
+  launch_kernel(router_logits_kernel, dim3(grid), dim3(256), smem, s, 
       static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
       nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
 }
@@ -624,11 +632,11 @@ void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int
   const int f32_in = logits_dtype == D3_DTYPE_F32, f32_out = weights_dtype == D3_DTYPE_F32;
   const int per_lane = (E + 31) / 32;
   if (per_lane <= 4)
-    route_kernel<4><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+    launch_kernel(route_kernel<4>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
   else if (per_lane <= 8)
-    route_kernel<8><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+    launch_kernel(route_kernel<8>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
   else
-    route_kernel<kMaxPerLane><<<grid, 256, 0, s>>>(logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+    launch_kernel(route_kernel<kMaxPerLane>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
 }
 
 int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, int T, int E,
@@ -667,12 +675,12 @@ int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t
         return set_error(D3_ECUDA, "permute: cannot raise the shared-memory limit");
       conf_scatter[dev] = true;
     }
-    permute_hist_kernel<<<chunks, kPermuteThreads, static_cast<size_t>(E) * sizeof(int), s>>>(
+    launch_kernel(permute_hist_kernel, dim3(chunks), dim3(kPermuteThreads), static_cast<size_t>(E) * sizeof(int), s, 
         ids, P, E, chunk, scratch);
-    permute_scan_kernel<<<1, kPermuteThreads, 0, s>>>(scratch, chunks, P, E, block_m, counts,
+    launch_kernel(permute_scan_kernel, dim3(1), dim3(kPermuteThreads), 0, s, scratch, chunks, P, E, block_m, counts,
                                                       starts, total, sorted_ids, expert_ids,
                                                       max_rows, active, n_active);
-    permute_scatter_kernel<<<chunks, kPermuteThreads, scatter_smem, s>>>(ids, P, E, chunk, scratch,
+    launch_kernel(permute_scatter_kernel, dim3(chunks), dim3(kPermuteThreads), scatter_smem, s, ids, P, E, chunk, scratch,
                                                                          sorted_ids, inv_rows);
     return check_launch("moe_permute (chunked)");
   }
@@ -686,7 +694,7 @@ int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t
       return set_error(D3_ECUDA, "permute: cannot raise the shared-memory limit");
     configured[dev] = true;
   }
-  permute_kernel<<<1, kPermuteThreads, smem, s>>>(ids, T * k, E, block_m, counts, starts, total,
+  launch_kernel(permute_kernel, dim3(1), dim3(kPermuteThreads), smem, s, ids, T * k, E, block_m, counts, starts, total,
                                                    sorted_ids, expert_ids, max_rows, inv_rows,
                                                    active, n_active);
   return check_launch("moe_permute");

@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ngroups = args.E + args.has_shared;
 
+  pdl_wait();  // counts, activations and outputs belong to earlier kernels
   // tiles per group and their exclusive prefix (serial in one warp: <= 1025 groups)
   if (warp == 0) {
     int running = 0;
@@ -253,6 +254,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box, &full[s]);
           }
         }
+        pdl_trigger();  // every load of this CTA is issued
 #pragma unroll
         for (int s = 0; s < S; ++s)
           if (last_parity[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(last_parity[s]));
