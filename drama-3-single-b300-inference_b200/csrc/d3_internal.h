@@ -11,14 +11,16 @@ namespace d3 {
 // Activation quantisation into expert order: token t is quantised once (1x128
 // groups, e4m3 + f32 scale) and written to rows inv_rows[t*k + j] (negative =
 // skipped) and, with with_shared, to row P + t. Rows not named are untouched.
+// The first CTA also zeroes zero[0..nzero) (the engines' work counters).
 void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
-                          cudaStream_t s);
+                          cudaStream_t s, int32_t* zero = nullptr, int nzero = 0);
 
 // Weight-only GEMV activation prep: x bf16 [T,K] -> f16 [T,K] scaled by a
 // power of two per 1x128 group (exact), inv f32 [T,K/128] = the inverse factor.
+// The first CTA also zeroes zero[0..nzero) (split-K tile counters, status).
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
-                           cudaStream_t s);
+                           cudaStream_t s, int32_t* zero = nullptr, int nzero = 0);
 
 // Final combine of the expert rows (see d3_moe_experts / d3_moe_layer).
 //   routed[t] = bf16(sum_r w[t,r] * d[inv_rows[t*k+r]])

@@ -114,8 +114,10 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
 __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                      int H, int k, const int32_t* __restrict__ inv_rows, int P,
                                      int with_shared, uint8_t* __restrict__ xq,
-                                     float* __restrict__ sx) {
+                                     float* __restrict__ sx, int32_t* __restrict__ zero, int nzero) {
   pdl_wait();
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   const int G = H / 128;
   const RowPair rp = row_pair(G);
   const int t = rp.row;
@@ -148,8 +150,11 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
 // Within each 128-element block, element k is stored at dense_act_position(k)
 // (expert_gemv.cuh).
 __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
-                                      int K, __half* __restrict__ xh, float* __restrict__ inv) {
+                                      int K, __half* __restrict__ xh, float* __restrict__ inv,
+                                      int32_t* __restrict__ zero, int nzero) {
   pdl_wait();
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   const int G = K / 128;
   const RowPair rp = row_pair(G);
   const int row = rp.row;
@@ -477,17 +482,18 @@ inline unsigned pair_blocks(int rows, int cols) {
 
 void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
-                          cudaStream_t s) {
+                          cudaStream_t s, int32_t* zero, int nzero) {
   if (T <= 0) return;
-  launch_kernel(quant_scatter_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), x_stride, T, H,
-                                              k, inv_rows, P, with_shared, xq, sx);
+  launch_kernel(quant_scatter_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, s,
+                static_cast<const __nv_bfloat16*>(x), x_stride, T, H, k, inv_rows, P, with_shared, xq,
+                sx, zero, nzero);
 }
 
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
-                           cudaStream_t s) {
+                           cudaStream_t s, int32_t* zero, int nzero) {
   if (T <= 0) return;
-  launch_kernel(dense_act_prep_kernel, dim3(pair_blocks(T, K)), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x),
-                                                      x_stride, T, K, xh, inv);
+  launch_kernel(dense_act_prep_kernel, dim3(pair_blocks(T, K)), dim3(256), 0, s,
+                static_cast<const __nv_bfloat16*>(x), x_stride, T, K, xh, inv, zero, nzero);
 }
 
 void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,

@@ -95,6 +95,11 @@ struct EngineArgs {
   int kb_per_split;
   float* partials;
   int32_t* tile_counters;   // [tiles * token groups]
+  // Dynamic schedule: after its first item (blockIdx.x) a CTA takes the next
+  // item index from gridDim.x + atomicAdd(work_counter, 1), so CTAs that drew
+  // light items take more of them (zeroed before launch; nullptr: static
+  // round-robin i += gridDim.x).
+  int32_t* work_counter;
 };
 
 struct WorkItem {
@@ -499,8 +504,11 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
     bool ok = true;
-    for (int i = blockIdx.x; ok; i += gridDim.x) {
+    for (int i = blockIdx.x; ok;) {
       const bool have = i < n_items;
+      // claim the next item now; the atomic's latency hides behind this item
+      int next = i + gridDim.x;
+      if (have && args.work_counter && leader) next = gridDim.x + atomicAdd(args.work_counter, 1);
       WorkItem w{};
       if (have) w = engine_item(args, sm_active, sm_counts, sm_starts, i);
       const CUtensorMap* wmap = w.shared ? &tm_w_sh : &tm_w;
@@ -570,6 +578,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         ok = __shfl_sync(0xffffffffu, ok, 0);
       }
       if (!have) break;
+      i = args.work_counter ? __shfl_sync(0xffffffffu, next, 0) : next;
     }
     pdl_trigger();  // every load of this CTA is issued: the next kernel may start launching
     // Never leave the CTA while a copy may still be writing its shared memory.

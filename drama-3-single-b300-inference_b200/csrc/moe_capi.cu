@@ -50,6 +50,7 @@ struct MoeBuffers {
   int32_t* tile_experts;
   int32_t* inv;
   int32_t* permute_scratch;
+  int32_t* work;  // engine work counters: [0] gate_up, [1] down
   uint8_t* xq;
   float* sx;
   uint8_t* a;
@@ -76,6 +77,7 @@ MoeBuffers carve_moe(void* ws, int T, int k, int E, int I, int H, int has_shared
   b.tile_experts = c.take<int32_t>(P > 0 ? P : 1);
   b.inv = c.take<int32_t>(P > 0 ? P : 1);
   b.permute_scratch = c.take<int32_t>(permute_scratch_ints(E));
+  b.work = c.take<int32_t>(2);
   b.xq = c.take<uint8_t>(R * H);
   b.sx = c.take<float>(R * (H / 128));
   b.a = c.take<uint8_t>(R * I);
@@ -216,7 +218,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
                         b.inv, b.active, b.n_active, s, b.permute_scratch);
     if (rc) return rc;
   }
-  launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s);
+  launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2);
   if ((rc = check_launch("quant_scatter"))) return rc;
 
   const int sms = sm_count();
@@ -313,6 +315,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.out_qs = b.sa;
     a.out_cols = I;
     a.status = status;
+    a.work_counter = b.work;
     const int max_items = (E + a.shared_groups) * (I / 128);
     const int grid = max_items < sms ? max_items : sms;
     rc = launch_engine<EPI_GATE_UP, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s);
@@ -348,6 +351,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.out_rows = b.d;
     a.out_ld = H;
     a.status = status;
+    a.work_counter = b.work + 1;
     const int max_items = (E + a.shared_groups) * (H / 128);
     const int grid = max_items < sms ? max_items : sms;
     rc = launch_engine<EPI_DOWN, false, kStagesDown>(nch, tw, twsh, ta, a, grid, s);
@@ -512,12 +516,9 @@ extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, c
   split = split > KB ? KB : split;
   const int kbps = (KB + split - 1) / split;
   split = (KB + kbps - 1) / kbps;
-  if (split > 1) {
-    const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
-    if (cudaMemsetAsync(b.counters, 0, sizeof(int32_t) * tiles * groups, st) != cudaSuccess)
-      return set_error(D3_ECUDA, "fp8_gemv: counter reset failed");
-  }
-  launch_dense_act_prep(x, x_stride, T, K, b.xh, b.inv, st);
+  const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
+  // the split-K tile counters are zeroed by the activation prep kernel
+  launch_dense_act_prep(x, x_stride, T, K, b.xh, b.inv, st, b.counters, split > 1 ? tiles * groups : 0);
   int rc = check_launch("dense_act_prep");
   if (rc) return rc;
   CUtensorMap tw, ta;
@@ -628,11 +629,10 @@ extern "C" int d3_fp8_gemv_noalloc(const void* x, int64_t x_stride, const uint8_
   split = split > KB ? KB : split;
   const int kbps = (KB + split - 1) / split;
   split = (KB + kbps - 1) / kbps;
-  // the counters and status word left by the previous call are cleared here
-  if (cudaMemsetAsync(counters, 0, kNoAllocCounterBytes, st) != cudaSuccess ||
-      cudaMemsetAsync(status, 0, sizeof(int32_t), st) != cudaSuccess)
-    return set_error(D3_ECUDA, "fp8_gemv_noalloc: clearing the scratch counters failed");
-  launch_dense_act_prep(x, x_stride, T, K, xh, inv, st);
+  // the split-K counters left by the previous call are cleared by the
+  // activation prep kernel (the status word only records timeouts)
+  launch_dense_act_prep(x, x_stride, T, K, xh, inv, st, counters,
+                        static_cast<int>(kNoAllocCounterBytes / sizeof(int32_t)));
   if ((rc = check_launch("dense_act_prep"))) return rc;
   CUtensorMap tw, ta;
   if ((rc = encode_tmap_2d(&tw, wq, 1, K, N, K, 128, 128))) return rc;
