@@ -32,6 +32,13 @@ void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const v
 
 // Router projection (fixed fp32 summation order); from 256 tokens a tiled
 // kernel (same order) streams 32-token x 16-row tiles.
+// Fused layer exit: routed/shared rows combined as in
+// d3_combine_experts_add_norm, residual updated in place, out = RMSNorm.
+int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
+                                 const void* weights, int T, int k, const void* gate,
+                                 int64_t gate_stride, void* residual, const void* norm_w, float eps,
+                                 void* out, cudaStream_t s);
+
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
                           cudaStream_t s);

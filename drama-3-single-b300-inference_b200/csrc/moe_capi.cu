@@ -204,10 +204,30 @@ int check_experts(const d3_experts_t* e, const char* what) {
 
 // Steps 1-5 on an already carved workspace. ids/weights are device tensors
 // [T,k]; gate (nullable) feeds the shared-expert combine.
+struct AddNorm {
+  void* residual = nullptr;     // bf16 [T, H], updated in place
+  const void* weight = nullptr; // bf16 [H]
+  float eps = 0.f;
+};
+
+// Step 5: the fixed-order combine, or (with an AddNorm) the combine fused with
+// the residual update and RMSNorm of the layer exit.
+int finish_layer(const MoeBuffers& b, int H, const void* weights, int T, int k, int has_shared,
+                 const void* gate, int64_t gate_stride, void* routed_out, void* shared_out,
+                 void* out, const AddNorm& an, cudaStream_t s) {
+  if (an.residual)
+    return launch_combine_rows_add_norm(b.d, H, b.inv, weights, T, k, gate, gate_stride,
+                                        an.residual, an.weight, an.eps, out, s);
+  launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
+                      shared_out, out, s);
+  return check_launch("combine_rows");
+}
+
 int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
                 int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
                 int64_t gate_stride, void* routed_out, void* shared_out, void* out,
-                const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted) {
+                const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted,
+                const AddNorm& an = AddNorm{}) {
   const int E = ex->E, I = ex->I, H = ex->H;
   const int P = T * k;
   const int has_shared = sh ? 1 : 0;
@@ -276,9 +296,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
       if (rc) return rc;
     }
     stage_mark(3, s);
-    launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
-                        shared_out, out, s);
-    rc = check_launch("combine_rows");
+    rc = finish_layer(b, H, weights, T, k, has_shared, gate, gate_stride, routed_out, shared_out,
+                      out, an, s);
     stage_mark(4, s);
     return rc;
   }
@@ -358,9 +377,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     if (rc) return rc;
   }
   stage_mark(3, s);
-  launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
-                      shared_out, out, s);
-  rc = check_launch("combine_rows");
+  rc = finish_layer(b, H, weights, T, k, has_shared, gate, gate_stride, routed_out, shared_out, out,
+                    an, s);
   stage_mark(4, s);
   return rc;
 }
@@ -431,11 +449,11 @@ extern "C" int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* id
                      shared_out, nullptr, b, status ? status : b.status, s, false);
 }
 
-extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w,
-                            const float* router_bias, int T, int k, const d3_experts_t* experts,
-                            const d3_experts_t* shared, void* out, int64_t* ids_out,
-                            void* weights_out, void* workspace, size_t workspace_bytes,
-                            int32_t* status, d3_stream_t stream) {
+static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
+                          const float* router_bias, int T, int k, const d3_experts_t* experts,
+                          const d3_experts_t* shared, void* out, int64_t* ids_out,
+                          void* weights_out, void* workspace, size_t workspace_bytes,
+                          int32_t* status, d3_stream_t stream, const AddNorm& an) {
   int rc = check_common(x, x_stride, T, k, experts, shared, workspace, workspace_bytes,
                         "moe_layer");
   if (rc) return rc;
@@ -457,7 +475,34 @@ extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_
                             b.tile_experts, P, b.inv, b.active, b.n_active, s, b.permute_scratch);
   if (rc) return rc;
   return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
-                     nullptr, out, b, status ? status : b.status, s, true);
+                     nullptr, out, b, status ? status : b.status, s, true, an);
+}
+
+extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w,
+                            const float* router_bias, int T, int k, const d3_experts_t* experts,
+                            const d3_experts_t* shared, void* out, int64_t* ids_out,
+                            void* weights_out, void* workspace, size_t workspace_bytes,
+                            int32_t* status, d3_stream_t stream) {
+  return moe_layer_impl(x, x_stride, router_w, router_bias, T, k, experts, shared, out, ids_out,
+                        weights_out, workspace, workspace_bytes, status, stream, AddNorm{});
+}
+
+extern "C" int d3_moe_layer_add_norm(const void* x, int64_t x_stride, const void* router_w,
+                                     const float* router_bias, int T, int k,
+                                     const d3_experts_t* experts, const d3_experts_t* shared,
+                                     void* residual, const void* norm_weight, float eps, void* out,
+                                     int64_t* ids_out, void* weights_out, void* workspace,
+                                     size_t workspace_bytes, int32_t* status, d3_stream_t stream) {
+  D3_REQUIRE(residual && norm_weight && aligned(residual, 16) && aligned(norm_weight, 16),
+             "moe_layer_add_norm: null or misaligned residual / norm weight");
+  D3_REQUIRE(experts && experts->H % 8 == 0 && experts->H <= 8192,
+             "moe_layer_add_norm: H must be a multiple of 8 up to 8192");
+  AddNorm an;
+  an.residual = residual;
+  an.weight = norm_weight;
+  an.eps = eps;
+  return moe_layer_impl(x, x_stride, router_w, router_bias, T, k, experts, shared, out, ids_out,
+                        weights_out, workspace, workspace_bytes, status, stream, an);
 }
 
 namespace {

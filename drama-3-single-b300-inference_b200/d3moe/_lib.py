@@ -72,6 +72,12 @@ SIGNATURES: dict[str, tuple] = {
     "d3_silu_mul": (_i32, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p]),
     "d3_silu_mul_quant": (_i32, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_combine_experts": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p]),
+    "d3_add_norm": (_i32, [_c_void_p, _c_void_p, _c_void_p, ctypes.c_float, _i32, _i32, _c_void_p, _c_void_p]),
+    "d3_combine_experts_add_norm": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32, _i32, _c_void_p, _c_void_p,
+         ctypes.c_float, _c_void_p, _c_void_p],
+    ),
     "d3_fp8_quantize_weight": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_fp8_gemv_workspace_size": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_size_t)]),
     "d3_fp8_gemv": (
@@ -107,6 +113,12 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.POINTER(D3Experts),
          ctypes.POINTER(D3Experts), _c_void_p, _c_void_p, _c_void_p, _c_void_p, _size_t,
          _c_void_p, _c_void_p],
+    ),
+    "d3_moe_layer_add_norm": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.POINTER(D3Experts),
+         ctypes.POINTER(D3Experts), _c_void_p, _c_void_p, ctypes.c_float, _c_void_p, _c_void_p,
+         _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
 }
 

@@ -51,6 +51,21 @@ def combine_experts(routed, shared, gate):
     return ops.combine_experts(routed, shared, gate)
 
 
+def add_norm(x, residual, weight, epsilon):
+    """kernels.py:418-423: mutates `residual`, returns the normalised rows."""
+    return ops.add_norm(x, residual, weight, epsilon)
+
+
+def combine_experts_add_norm(routed, shared, gate, residual, weight, epsilon):
+    """kernels.py:483-499: mutates `residual`, returns the normalised rows."""
+    return ops.combine_experts_add_norm(routed, shared, gate, residual, weight, epsilon)
+
+
+def combine_experts_add_norm_inverse(routed, shared, gate, inverse, residual, weight, epsilon):
+    """kernels.py:540-556: compact routed/shared rows gathered by `inverse`."""
+    return ops.combine_experts_add_norm(routed, shared, gate, residual, weight, epsilon, inverse=inverse)
+
+
 def moe_permute(topk_ids: torch.Tensor, num_experts: int, block_m: int = 16):
     """The device bucketing of native_moe (kernels.py:711-731):
     (counts, starts, total, sorted_ids, expert_ids)."""

@@ -187,6 +187,55 @@ def combine_experts(routed: torch.Tensor, shared: torch.Tensor, gate: torch.Tens
     return out
 
 
+def _norm_args(residual: torch.Tensor, weight: torch.Tensor):
+    if residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+        raise ValueError("residual must be contiguous bf16 [T, W]")
+    W = residual.shape[-1]
+    if weight.numel() != W:
+        raise ValueError(f"norm weight has {weight.numel()} elements, expected {W}")
+    return weight.to(torch.bfloat16).contiguous()
+
+
+def add_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, epsilon: float) -> torch.Tensor:
+    """residual <- bf16(x + residual) in place; returns RMSNorm(residual) * (1 + weight)."""
+    _require_cuda(x, residual, weight)
+    w = _norm_args(residual, weight)
+    if x.shape != residual.shape or x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise ValueError("x must be contiguous bf16 with the residual's shape")
+    out = torch.empty_like(residual)
+    T, W = residual.shape
+    call("d3_add_norm", x.data_ptr(), residual.data_ptr(), w.data_ptr(), float(epsilon), T, W,
+         out.data_ptr(), _stream(x.device))
+    return out
+
+
+def combine_experts_add_norm(routed: torch.Tensor, shared: torch.Tensor, gate: torch.Tensor,
+                             residual: torch.Tensor, weight: torch.Tensor, epsilon: float,
+                             inverse: torch.Tensor | None = None) -> torch.Tensor:
+    """residual <- bf16(fma_bf16(shared, bf16(sigmoid(gate)), routed) + residual) in
+    place; returns RMSNorm(residual) * (1 + weight). With `inverse`, row t reads
+    routed/shared/gate row inverse[t]."""
+    _require_cuda(routed, shared, gate, residual, weight)
+    w = _norm_args(residual, weight)
+    if not routed.is_contiguous() or not shared.is_contiguous() or routed.shape != shared.shape:
+        raise ValueError("routed and shared must be contiguous and of one shape")
+    T, W = residual.shape
+    if routed.shape[-1] != W:
+        raise ValueError("routed/shared width differs from the residual's")
+    inv = None
+    if inverse is not None:
+        inv = inverse.to(torch.int32).contiguous()
+        if inv.numel() != T:
+            raise ValueError("inverse must hold one source row per residual row")
+    elif routed.shape[0] != T:
+        raise ValueError("routed rows differ from residual rows (pass inverse)")
+    out = torch.empty_like(residual)
+    call("d3_combine_experts_add_norm", routed.data_ptr(), shared.data_ptr(), gate.data_ptr(),
+         gate.stride(0), _ptr(inv), T, W, residual.data_ptr(), w.data_ptr(), float(epsilon),
+         out.data_ptr(), _stream(routed.device))
+    return out
+
+
 def fp8_quantize_weight(weight: torch.Tensor):
     """bf16 [N,K] -> (e4m3 [Npad,K], f32 [Npad/128, K/128])."""
     _require_cuda(weight)
@@ -282,8 +331,12 @@ def moe_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
 def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, experts, shared, k: int = 8,
               router_bias: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
               out: torch.Tensor | None = None, return_routing: bool = False,
-              status: torch.Tensor | None = None):
-    """Whole MoE layer: out = routed + bf16(shared * bf16(sigmoid(gate)))."""
+              status: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+              norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6):
+    """Whole MoE layer: out = routed + bf16(shared * bf16(sigmoid(gate))).
+    With `residual` and `norm_weight` the layer exit is fused in: residual is
+    updated in place with the bf16-fma combine (combine_experts_add_norm) and
+    out = RMSNorm(residual) * (1 + norm_weight)."""
     _require_cuda(x, router_weight, router_bias)
     ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
     sv = shared if isinstance(shared, ExpertView) else ExpertView(shared)
@@ -298,9 +351,21 @@ def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, experts, shared, k: 
     wts = torch.empty((T, k), dtype=torch.bfloat16, device=x.device) if return_routing else None
     if router_bias is not None:
         router_bias = router_bias.to(torch.float32).contiguous()
-    call("d3_moe_layer", x.data_ptr(), _row_stride(x), router_weight.data_ptr(), _ptr(router_bias),
-         T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct), out.data_ptr(), _ptr(ids), _ptr(wts),
-         workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(x.device))
+    if residual is not None:
+        if norm_weight is None:
+            raise ValueError("the fused layer exit needs norm_weight with residual")
+        _require_cuda(residual, norm_weight)
+        nw = _norm_args(residual, norm_weight)
+        if residual.shape != (T, H):
+            raise ValueError("residual must be [T, H]")
+        call("d3_moe_layer_add_norm", x.data_ptr(), _row_stride(x), router_weight.data_ptr(),
+             _ptr(router_bias), T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct),
+             residual.data_ptr(), nw.data_ptr(), float(norm_eps), out.data_ptr(), _ptr(ids), _ptr(wts),
+             workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(x.device))
+    else:
+        call("d3_moe_layer", x.data_ptr(), _row_stride(x), router_weight.data_ptr(), _ptr(router_bias),
+             T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct), out.data_ptr(), _ptr(ids), _ptr(wts),
+             workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(x.device))
     if return_routing:
         return out, ids, wts
     return out

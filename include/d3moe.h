@@ -148,6 +148,25 @@ D3_API int d3_silu_mul_quant(const void* in, int64_t in_stride, int rows, int W,
 D3_API int d3_combine_experts(const void* routed, const void* shared, const void* gate,
                        int64_t gate_stride, int T, int H, void* out, d3_stream_t stream);
 
+/* ------------------------------------------ (f1) residual + RMSNorm exit --
+ * residual bf16 [T,W] (updated in place) <- bf16(x + residual) in fp32;
+ * out bf16 [T,W] = bf16(residual * rsqrt(mean(residual^2) + eps) * (1 + weight)),
+ * weight bf16 [W]. W a multiple of 8, at most 8192.
+ * Replaces add_norm (src/drama3/kernels.py:405-423). */
+D3_API int d3_add_norm(const void* x, void* residual, const void* weight, float eps, int T, int W,
+                void* out, d3_stream_t stream);
+
+/* Same exit with the expert combine in front of it:
+ *   combined = fma.rn.bf16(shared, bf16(sigmoid(gate)), routed)   (one rounding)
+ *   residual <- bf16(combined + residual), out = RMSNorm as above.
+ * With inverse (int32 [T], may be NULL) the routed/shared/gate rows of row t
+ * are taken from row inverse[t]. Replaces combine_experts_add_norm and
+ * combine_experts_add_norm_inverse (src/drama3/kernels.py:448-556). */
+D3_API int d3_combine_experts_add_norm(const void* routed, const void* shared, const void* gate,
+                                int64_t gate_stride, const int32_t* inverse, int T, int W,
+                                void* residual, const void* weight, float eps, void* out,
+                                d3_stream_t stream);
+
 /* ------------------------------------------------ (a10) dense FP8 GEMV --
  * 128x128 block weight quantisation: scale = max(amax,1e-8)/448 per block,
  * q = e4m3(w/scale). w bf16 [N,K] (K multiple of 128); q e4m3 [Npad,K],
@@ -228,6 +247,18 @@ D3_API int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w, c
                  int T, int k, const d3_experts_t* experts, const d3_experts_t* shared, void* out,
                  int64_t* ids_out, void* weights_out, void* workspace, size_t workspace_bytes,
                  int32_t* status, d3_stream_t stream);
+
+/* d3_moe_layer with the layer exit fused into its final kernel: the combine
+ * of d3_combine_experts_add_norm (bf16 fma of shared and gate onto routed),
+ * residual bf16 [T,H] updated in place, out = RMSNorm(residual) * (1 + norm_weight).
+ * The routed/shared bf16 tensors of moe_parts + combine_experts_add_norm
+ * (src/drama3/model.py:506-517, kernels.py:448-499) never reach HBM. */
+D3_API int d3_moe_layer_add_norm(const void* x, int64_t x_stride, const void* router_w,
+                          const float* router_bias, int T, int k, const d3_experts_t* experts,
+                          const d3_experts_t* shared, void* residual, const void* norm_weight,
+                          float eps, void* out, int64_t* ids_out, void* weights_out,
+                          void* workspace, size_t workspace_bytes, int32_t* status,
+                          d3_stream_t stream);
 
 /* ---------------------------------------------- (e) expert parallelism --
  * The reference runs on one GPU and has no expert parallelism; these entry

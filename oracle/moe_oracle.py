@@ -319,6 +319,50 @@ def combine_experts(routed, shared, gate):
     return bf16_round((np.asarray(routed, dtype=np.float32) + weighted).astype(np.float32))
 
 
+def bf16_fma(a, b, c):
+    """PTX fma.rn.bf16: a*b + c computed exactly, rounded once to bf16. For
+    bf16 operands the exact value fits a float64 (a*b has at most 16
+    significant bits)."""
+    exact = (np.asarray(a, np.float64) * np.asarray(b, np.float64)) + np.asarray(c, np.float64)
+    return bf16_round(exact)
+
+
+def _rms_scale(value, weight, eps):
+    """value * rsqrt(mean(value^2) + eps) * (1 + weight), fp32 (the norm half of
+    src/drama3/kernels.py:413-415 and :478-480)."""
+    v = np.asarray(value, dtype=np.float32)
+    ms = (np.sum(v * v, axis=-1, dtype=np.float32) / F32(v.shape[-1])).astype(np.float32)
+    r = (F32(1.0) / np.sqrt((ms + F32(eps)).astype(np.float32))).astype(np.float32)
+    out = (v * r[:, None]).astype(np.float32)
+    out = (out * (F32(1.0) + np.asarray(weight, dtype=np.float32))[None, :]).astype(np.float32)
+    return bf16_round(out)
+
+
+def add_norm(x, residual, weight, eps):
+    """src/drama3/kernels.py:405-423 (add_norm_kernel): residual <- bf16(x +
+    residual) (fp32 add), out = bf16(rmsnorm(residual) * (1 + weight)).
+    Returns (out, new_residual)."""
+    value = bf16_round((np.asarray(x, np.float32) + np.asarray(residual, np.float32)).astype(np.float32))
+    return _rms_scale(value, weight, eps), value
+
+
+def combine_experts_add_norm(routed, shared, gate, residual, weight, eps, inverse=None):
+    """src/drama3/kernels.py:448-499 (and the _inverse form :502-556): combined =
+    fma.rn.bf16(shared, bf16(sigmoid(gate)), routed) on the (optionally
+    inverse-gathered) rows, residual <- bf16(combined + residual) (fp32 add),
+    out = bf16(rmsnorm(residual) * (1 + weight)). Returns (out, new_residual)."""
+    routed = np.asarray(routed, np.float32)
+    shared = np.asarray(shared, np.float32)
+    g = np.asarray(gate, dtype=np.float32).reshape(-1)
+    if inverse is not None:
+        inv = np.asarray(inverse).reshape(-1)
+        routed, shared, g = routed[inv], shared[inv], g[inv]
+    sg = bf16_round((F32(1.0) / (F32(1.0) + np.exp(-g))).astype(np.float32))
+    combined = bf16_fma(shared, sg[:, None], routed)
+    value = bf16_round((combined + np.asarray(residual, np.float32)).astype(np.float32))
+    return _rms_scale(value, weight, eps), value
+
+
 def fp8_gemv(x, wq, scales, n=None):
     """src/drama3/experimental_fp8.py:21-29 (_gemv): y = sum_k w*scale*x with
     bf16 activations (no activation quantisation), stored bf16. The sum is

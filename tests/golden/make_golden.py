@@ -261,6 +261,17 @@ def main() -> None:
     experimental_fp8._gemv_grouped[(triton.cdiv(N, 4),)](xd, qd, sd, yg, N, Kd, 4, num_warps=4)
     np.savez_compressed(OUT / "dense_fp8.npz", w=bits(wd), qf32=bits(qf), q=bits(qd), s=bits(sd),
                         x=bits(xd), y=bits(yd), y_grouped=bits(yg))
+
+    # ---- add_norm (kernels.py:405-423): residual update + Gemma RMSNorm
+    T = 6
+    xa = bf16(rng.standard_normal((T, 2048)) * 0.5)
+    res = bf16(rng.standard_normal((T, 2048)) * 2.0)
+    res[3] = 0.0  # a row whose update is x itself
+    wn = bf16(rng.standard_normal(2048) * 0.1)
+    res_in = res.clone()
+    on = kernels.add_norm(xa, res, wn, 1e-6)
+    np.savez_compressed(OUT / "add_norm.npz", x=bits(xa), residual_in=bits(res_in), weight=bits(wn),
+                        residual_out=bits(res), out=bits(on), eps=np.float32(1e-6))
     print("golden fixtures written to", OUT)
 
 

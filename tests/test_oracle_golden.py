@@ -155,3 +155,40 @@ def test_router_logits_order_is_a_permutation_of_the_dot_product():
     got = O.router_logits(x, w)
     ref = O.bf16_round((x.astype(np.float64) @ w.T.astype(np.float64)).astype(np.float32))
     assert ulps_bf16(got, ref).max() <= 1
+
+
+def test_add_norm_matches_reference(golden):
+    """add_norm (kernels.py:405-423) golden from the reference kernel: the
+    residual update and the normalised rows are both bit-exact."""
+    g = golden("add_norm")
+    out, res = O.add_norm(O.bf16_from_bits(g["x"]), O.bf16_from_bits(g["residual_in"]),
+                          O.bf16_from_bits(g["weight"]), float(g["eps"]))
+    np.testing.assert_array_equal(O.bf16_to_bits(res), g["residual_out"])
+    np.testing.assert_array_equal(O.bf16_to_bits(out), g["out"])
+
+
+def test_bf16_fma_rounds_once():
+    """fma.rn.bf16 semantics of the combine in combine_experts_add_norm
+    (kernels.py:464-472): one rounding of the exact a*b + c, which differs from
+    rounding the product first (the combine_experts form) on some inputs."""
+    rng = np.random.default_rng(3)
+    a = O.bf16_round(rng.standard_normal(20000).astype(np.float32))
+    b = O.bf16_round(rng.uniform(0, 1, 20000).astype(np.float32))
+    c = O.bf16_round(rng.standard_normal(20000).astype(np.float32))
+    once = O.bf16_fma(a, b, c)
+    exact = a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)
+    assert (np.abs(once - exact) <= np.abs(O.bf16_round(exact.astype(np.float32)) - exact) + 0).all()
+    twice = O.bf16_round((O.bf16_round((a * b).astype(np.float32)) + c).astype(np.float32))
+    assert (once != twice).any()
+
+
+def test_combine_add_norm_with_zero_shared_is_add_norm(golden):
+    """With shared = 0 the fused combine leaves routed unchanged, so
+    combine_experts_add_norm reduces to add_norm(routed, residual)."""
+    g = golden("add_norm")
+    x, res, w = (O.bf16_from_bits(g[k]) for k in ("x", "residual_in", "weight"))
+    gate = np.zeros((x.shape[0], 1), np.float32)
+    out_c, res_c = O.combine_experts_add_norm(x, np.zeros_like(x), gate, res, w, float(g["eps"]))
+    out_a, res_a = O.add_norm(x, res, w, float(g["eps"]))
+    np.testing.assert_array_equal(res_c, res_a)
+    np.testing.assert_array_equal(out_c, out_a)
