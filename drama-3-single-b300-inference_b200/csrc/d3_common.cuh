@@ -1,7 +1,7 @@
 // Shared device helpers for the d3moe sm_100a kernels.
 //
 // Everything here is hand-written inline PTX or plain CUDA: mbarrier rings with
-// bounded waits, 2-D TMA tile loads (no multicast anywhere in this library),
+// bounded waits, 2-D TMA tile loads into the issuing CTA's own shared memory,
 // ldmatrix / mma.sync fragments, and the number formats of the FP8 MoE path
 // (E4M3 activations and weights, BF16 tensors, FP32 block scales).
 #pragma once
