@@ -751,7 +751,9 @@ def main() -> None:
             "unit": "GB/s",
             "frac": achieved / pk["hbm_gbs"],
             "peak_source": pk["source"],
-            "traffic": None,
+            # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch
+            # (profiles/expert_gemv_T64_full.md, same workload)
+            "traffic": 404.45e6,
             "algorithmic_bytes_per_launch": gate_bytes,
             "avg_launch_ms": gate_avg,
             "down_kernel": {"achieved": down_bytes / (down_avg * 1e-3) / 1e9, "avg_launch_ms": down_avg,
