@@ -751,8 +751,8 @@ def main() -> None:
             "unit": "GB/s",
             "frac": achieved / pk["hbm_gbs"],
             "peak_source": pk["source"],
-            # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch
-            # (profiles/expert_gemv_T64_full.md, same workload)
+            # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch,
+            # from an ncu --set full capture of this workload
             "traffic": 404.45e6,
             "algorithmic_bytes_per_launch": gate_bytes,
             "avg_launch_ms": gate_avg,
