@@ -395,7 +395,7 @@ def run_prefill(args, dev) -> None:
 
     from d3moe import _lib, ops, synth
 
-    lens = prefill_lengths()
+    lens = [args.prefill_tokens] if args.prefill_tokens > 0 else prefill_lengths()
     T = sum(lens)
     lib = _lib.load()
     layers = [synth.make_layer(E, I, H, seed=3 + li, device=dev, router_bias="zipf") for li in range(2)]
@@ -484,8 +484,9 @@ def run_prefill(args, dev) -> None:
         "dtype": "fp8_e4m3 x fp8_e4m3 -> f32 (tcgen05 kind::f8f6f4)",
         "data": "synthetic",
         "config": {
-            "workload": f"prefill: 64 ragged prompts uniform in [16,512] (seed 3), T={T} tokens, one MoE "
-                        "layer (H=2048, E=128, I=768, top-8, shared expert), Zipf(1.1) router bias",
+            "workload": (f"prefill: 64 ragged prompts uniform in [16,512] (seed 3), T={T} tokens"
+                         if args.prefill_tokens <= 0 else f"prefill: one batch of T={T} tokens")
+                        + ", one MoE layer (H=2048, E=128, I=768, top-8, shared expert), Zipf(1.1) router bias",
             "tokens": T,
             "l2": "every step writes > 1 GB of activations/partials (8x the 126 MB L2) and alternates "
                   "two 620 MB weight sets",
@@ -561,6 +562,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: the default 64-token step; prefill: ~8k ragged tokens, one GPU")
+    ap.add_argument("--prefill-tokens", type=int, default=0,
+                    help="prefill: a flat batch of this many tokens instead of the ragged 64-prompt batch")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1: independent full-layer replicas instead of expert parallelism")
     args = ap.parse_args()

@@ -2,11 +2,13 @@
 //
 // Pipeline for T tokens, top-k, E experts (P = T*k pairs, R = P + T rows when
 // a shared expert runs):
-//   1. permute      ids -> counts, starts, sorted pairs, inverse rows, active list
+//   1. permute       ids -> counts, starts, inverse rows, active list
 //   2. quant_scatter x -> e4m3 rows in expert order (+ T shared rows), scales
-//   3. gate_up      engine EPI_GATE_UP: a e4m3 [R, I], sa [R, I/128]
-//   4. down         engine EPI_DOWN:    d f32 [R, H]
-//   5. combine      routed/shared/out bf16 [T, H] in fixed rank order
+//   3. gate_up       engine EPI_GATE_UP (decode) or tcgen05 grouped GEMM
+//                    (prefill): a e4m3 [R, I], sa [R, I/128]
+//   4. down          engine EPI_DOWN or tcgen05 grouped GEMM: d f32 [R, H]
+//   5. combine       routed/shared/out bf16 [T, H] in fixed rank order, or the
+//                    combine fused with the residual update and RMSNorm
 // All buffers live in the caller's workspace; nothing is allocated here.
 #include <atomic>
 #include <cstdlib>
@@ -46,8 +48,6 @@ struct MoeBuffers {
   int32_t* total;
   int32_t* active;
   int32_t* n_active;
-  int32_t* sorted;
-  int32_t* tile_experts;
   int32_t* inv;
   int32_t* permute_scratch;
   int32_t* work;  // engine work counters: [0] gate_up, [1] down
@@ -73,8 +73,6 @@ MoeBuffers carve_moe(void* ws, int T, int k, int E, int I, int H, int has_shared
   b.total = c.take<int32_t>(1);
   b.active = c.take<int32_t>(E);
   b.n_active = c.take<int32_t>(1);
-  b.sorted = c.take<int32_t>(P > 0 ? P : 1);
-  b.tile_experts = c.take<int32_t>(P > 0 ? P : 1);
   b.inv = c.take<int32_t>(P > 0 ? P : 1);
   b.permute_scratch = c.take<int32_t>(permute_scratch_ints(E));
   b.work = c.take<int32_t>(2);
@@ -234,7 +232,9 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
   const int R = P + (has_shared ? T : 0);
   int rc = D3_OK;
   if (!permuted) {
-    rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, b.sorted, b.tile_experts, P,
+    // the pipeline reads counts, starts, the inverse map and the active list;
+    // the reference's sorted-pair and per-tile expert buffers are not written
+    rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
                         b.inv, b.active, b.n_active, s, b.permute_scratch);
     if (rc) return rc;
   }
@@ -471,8 +471,8 @@ static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
   if ((rc = check_launch("router_logits"))) return rc;
   const int P = T * k;
   rc = launch_route_permute(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts,
-                            D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, b.sorted,
-                            b.tile_experts, P, b.inv, b.active, b.n_active, s, b.permute_scratch);
+                            D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
+                            b.inv, b.active, b.n_active, s, b.permute_scratch);
   if (rc) return rc;
   return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
                      nullptr, out, b, status ? status : b.status, s, true, an);

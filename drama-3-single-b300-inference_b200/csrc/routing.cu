@@ -379,7 +379,7 @@ __device__ __forceinline__ void permute_body(IdAt id_at, int P, int E, int bm, i
       int pre = 0;
       for (int w2 = 0; w2 < warp; ++w2) pre += wcnt[w2 * E + e];
       const int pos = start[e] + cursor[e] + pre + rank;
-      sorted_ids[pos] = p;
+      if (sorted_ids) sorted_ids[pos] = p;
       if (inv_rows) inv_rows[p] = pos;
     } else if (p < P && inv_rows) {
       inv_rows[p] = -1;
@@ -395,15 +395,19 @@ __device__ __forceinline__ void permute_body(IdAt id_at, int P, int E, int bm, i
   for (int e = warp; e < E; e += kPermuteThreads / 32) {
     const int c = cnt[e], s = start[e];
     const int padded = (c + bm - 1) / bm * bm;
-    for (int i = c + lane; i < padded; i += 32) sorted_ids[s + i] = P;
-    for (int b = lane; b * bm < padded; b += 32) expert_ids[s / bm + b] = e;
+    if (sorted_ids)
+      for (int i = c + lane; i < padded; i += 32) sorted_ids[s + i] = P;
+    if (expert_ids)
+      for (int b = lane; b * bm < padded; b += 32) expert_ids[s / bm + b] = e;
     if (lane == 0) {
       counts[e] = c;
       starts[e] = s;
     }
   }
-  for (int64_t r = total + tid; r < max_rows; r += kPermuteThreads) sorted_ids[r] = P;
-  for (int64_t b = total / bm + tid; b < max_rows / bm; b += kPermuteThreads) expert_ids[b] = -1;
+  if (sorted_ids)
+    for (int64_t r = total + tid; r < max_rows; r += kPermuteThreads) sorted_ids[r] = P;
+  if (expert_ids)
+    for (int64_t b = total / bm + tid; b < max_rows / bm; b += kPermuteThreads) expert_ids[b] = -1;
   if (tid == 0) total_out[0] = total;
   if (active) {
     int n = 0;
@@ -501,11 +505,15 @@ __global__ void __launch_bounds__(kPermuteThreads)
   for (int ee = warp; ee < E; ee += kPermuteThreads / 32) {
     const int c = s_cnt[ee], s = s_start[ee];
     const int pd = (c + bm - 1) / bm * bm;
-    for (int i = c + lane; i < pd; i += 32) sorted_ids[s + i] = P;
-    for (int b = lane; b * bm < pd; b += 32) expert_ids[s / bm + b] = ee;
+    if (sorted_ids)
+      for (int i = c + lane; i < pd; i += 32) sorted_ids[s + i] = P;
+    if (expert_ids)
+      for (int b = lane; b * bm < pd; b += 32) expert_ids[s / bm + b] = ee;
   }
-  for (int64_t r = total + tid; r < max_rows; r += kPermuteThreads) sorted_ids[r] = P;
-  for (int64_t b = total / bm + tid; b < max_rows / bm; b += kPermuteThreads) expert_ids[b] = -1;
+  if (sorted_ids)
+    for (int64_t r = total + tid; r < max_rows; r += kPermuteThreads) sorted_ids[r] = P;
+  if (expert_ids)
+    for (int64_t b = total / bm + tid; b < max_rows / bm; b += kPermuteThreads) expert_ids[b] = -1;
   if (tid == 0) total_out[0] = total;
   if (active) {
     int n = 0;
@@ -545,7 +553,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
       int pre = 0;
       for (int w2 = 0; w2 < warp; ++w2) pre += wcnt[w2 * E + e];
       const int pos = cursor[e] + pre + rank;
-      sorted_ids[pos] = p;
+      if (sorted_ids) sorted_ids[pos] = p;
       if (inv_rows) inv_rows[p] = pos;
     } else if (p < p1 && inv_rows) {
       inv_rows[p] = -1;
