@@ -11,9 +11,10 @@ Synthetic seeded weights (N(0,0.02) quantised per 128x128 block), bf16 N(0,1)
 inputs. Steps rotate over `--layers` independent weight sets (4 x ~620 MB by
 default, > 2x the 126 MB L2), so weights stream from HBM every step.
 
-With torchrun (N > 1) every rank runs the same per-GPU workload on its own
-replica of the layer ("replicas"); the expert-parallel layer is measured by
-`--ep`. Timing: CUDA events on the launching stream, barrier + synchronize on
+With torchrun (N > 1) the expert-parallel layer runs (experts sharded over the
+ranks, NCCL all-to-all dispatch and combine); `--replicas` runs independent
+full-layer replicas instead. `--workload prefill` (ragged ~8k-token batch) and
+`--workload mixed` (64 decode + 1280 packed prompt rows) run on one GPU. Timing: CUDA events on the launching stream, barrier + synchronize on
 both sides, max over ranks.
 
 --impl reference times the reference's arithmetic on the host CPU (the oracle
@@ -520,6 +521,201 @@ def run_prefill(args, dev) -> None:
     print(json.dumps(line), flush=True)
 
 
+def mixed_rows(reuse: bool):
+    """Rows of the mixed decode + packed-prefill call of the reference's D64/P1280
+    graph (src/drama3/mixed_graph.py:33-50): 64 decode rows (the last 6 padding
+    with reserved slots), then 6 prompts of 1121 rows in total and 159 rows of
+    padding (the row counts of its mixed-call profile). With `reuse`, the third
+    prompt starts with all 240 rows of the second and the fifth with the first
+    60 rows of the fourth (300 rows removed), and the MoE runs on the row-reuse
+    plan's 1088-row bucket."""
+    import numpy as np
+    import torch
+
+    from d3moe import mixed
+
+    lens = [256, 240, 300, 120, 128, 77] if reuse else [220, 190, 205, 160, 176, 170]
+    assert sum(lens) == 1121
+    prompts = []
+    for i, n in enumerate(lens):
+        p = torch.zeros((n, 11), dtype=torch.int64)
+        p[:, 0] = 1 + i
+        p[:, 1] = torch.arange(n)
+        prompts.append(p)
+    if reuse:
+        prompts[2][:240] = prompts[1]
+        prompts[4][:60] = prompts[3][:60]
+    d, cap = 64, 1280
+    dslots = list(range(58)) + [MIXED_PAD + 1 + i for i in range(6)]
+    slots = mixed.packed_row_slots(dslots, lens, [100 + i for i in range(6)] + [MIXED_PAD + 100], cap)
+    plan = mixed.plan_row_reuse(prompts, d, cap, (1088,)) if reuse else None
+    if reuse and plan is None:
+        raise RuntimeError("the reuse prompts do not fit the 1088-row bucket")
+    return np.asarray(slots), plan
+
+
+MIXED_PAD = 512
+
+
+def run_mixed(args, dev) -> None:
+    """One FP8 MoE layer over the mixed decode + packed-prefill rows (M = 1344),
+    with the padding-router rule on the row slots and the layer exit (residual
+    update + RMSNorm) fused, through d3_moe_layer_rows. At this M the expert
+    GEMMs stream every expert's weights once, so the roofline is HBM."""
+    import numpy as np
+    import torch
+
+    from d3moe import _lib, ops, synth
+
+    Ex, Ix = args.experts, args.inter
+    slots_np, plan = mixed_rows(args.row_reuse)
+    M = len(slots_np)
+    T = plan.compact_rows if plan is not None else M
+    lib = _lib.load()
+    layers = [synth.make_layer(Ex, Ix, H, seed=11 + li, device=dev, router_bias="normal")
+              for li in range(args.layers)]
+    views = [(ops.ExpertView(l.experts), ops.ExpertView(l.shared)) for l in layers]
+    ws = ops.moe_workspace(T, TOPK, Ex, Ix, H, True, dev)
+    gin = torch.Generator(device=dev)
+    gin.manual_seed(5)
+    xs = torch.randn((2, M, H), generator=gin, device=dev).to(torch.bfloat16)
+    res = torch.randn((M, H), generator=gin, device=dev).to(torch.bfloat16)
+    nw = (torch.randn(H, generator=gin, device=dev) * 0.1).to(torch.bfloat16)
+    y = torch.empty((M, H), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((T, TOPK), dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    slots = torch.from_numpy(slots_np).to(dev)
+    keep = inverse = None
+    if plan is not None:
+        keep, inverse = plan.keep.to(dev), plan.inverse.to(dev)
+        slots = slots.index_select(0, keep)
+    rows = _lib.D3Rows(None if keep is None else keep.data_ptr(), M,
+                       None if inverse is None else inverse.data_ptr(), M, slots.data_ptr(), 1,
+                       MIXED_PAD)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    def step(i, x, r, ids_out=None):
+        lw = layers[i % len(layers)]
+        ev, sv = views[i % len(layers)]
+        _lib.call("d3_moe_layer_rows", x.data_ptr(), x.stride(0), lw.router.data_ptr(),
+                  lw.router_bias.data_ptr(), T, TOPK, ctypes.byref(ev.struct), ctypes.byref(sv.struct),
+                  ctypes.byref(rows), r.data_ptr(), nw.data_ptr(), 1e-6, y.data_ptr(),
+                  None if ids_out is None else ids_out.data_ptr(), None, ws.data_ptr(), ws.numel(),
+                  status.data_ptr(), sptr)
+
+    stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    for evs in stage_events:
+        for e in evs:
+            e.record(stream)
+    stage_arrays = [(ctypes.c_void_p * 5)(*[e._as_parameter_.value for e in evs]) for evs in stage_events]
+    prev = lib.d3_set_prefill_min_tokens(args.prefill_min) if args.prefill_min > 0 else None
+    for i in range(args.warmup):
+        step(i, xs[i % 2], res)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            lib.d3_set_stage_events(stage_arrays[i], 5)
+            step(i, xs[i % 2], res, ids if i == 0 else None)
+            lib.d3_set_stage_events(None, 0)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status word {int(status.item())}")
+    ms = start.elapsed_time(end) / args.steps
+    gate_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in stage_events)
+    down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in stage_events)
+    pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in stage_events)
+    post_ms = statistics.mean(e[3].elapsed_time(e[4]) for e in stage_events)
+
+    # end to end with host buffers: x and the residual in, out and residual back
+    hx = xs[0].cpu().pin_memory()
+    hr = res.cpu().pin_memory()
+    hy = torch.empty((M, H), dtype=torch.bfloat16).pin_memory()
+    hr2 = torch.empty((M, H), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((M, H), dtype=torch.bfloat16, device=dev)
+    dr = torch.empty((M, H), dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i):
+        dx.copy_(hx, non_blocking=True)
+        dr.copy_(hr, non_blocking=True)
+        step(i, dx, dr)
+        hy.copy_(y, non_blocking=True)
+        hr2.copy_(dr, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if prev is not None:
+        lib.d3_set_prefill_min_tokens(prev)
+
+    counts = np.bincount(ids.cpu().numpy().reshape(-1), minlength=Ex)
+    active = int((counts > 0).sum())
+    w13_bytes = (2 * Ix) * H + (2 * Ix // 128) * (H // 128) * 4
+    w2_bytes = H * Ix + (H // 128) * (Ix // 128) * 4
+    R = T * TOPK + T
+    gate_bytes = (active + 1) * w13_bytes + R * (H + H // 128 * 4) + R * (Ix + Ix // 128 * 4)
+    down_bytes = (active + 1) * w2_bytes + R * (Ix + Ix // 128 * 4) + R * H * 4
+    pk = peaks()
+    tc = T >= (args.prefill_min if args.prefill_min > 0 else 1024)
+    achieved = gate_bytes / (gate_ms * 1e-3) / 1e9
+    line = {
+        "metric": "fp8_moe_layer_mixed_rows_per_s",
+        "value": M / (ms * 1e-3),
+        "unit": "rows/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8_e4m3 x fp8_e4m3 -> f32",
+        "data": "synthetic",
+        "config": {
+            "workload": f"mixed decode + packed prefill: 64 decode rows (6 padding) + 6 prompts of 1121 rows "
+                        f"+ 159 padding rows = {M} rows"
+                        + (f", row reuse onto {T} compact rows" if plan is not None else "")
+                        + f", one MoE layer (H={H}, E={Ex}, I={Ix}, top-8, shared expert) with the fused "
+                          "residual + RMSNorm exit, N(0,1) router bias",
+            "rows": M, "moe_rows": T, "expert_path": "tcgen05 grouped" if tc else "decode engine",
+            "l2": f"{args.layers} weight sets of {Ex * (w13_bytes + w2_bytes) / 1e6:.0f} MB rotated",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "gate_up (" + ("tc_grouped_kernel<TC_GATE_UP>" if tc else "expert_gemv_kernel<EPI_GATE_UP>") + ")",
+            "achieved": achieved,
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "traffic": None,
+            "algorithmic_bytes_per_launch": gate_bytes,
+            "avg_launch_ms": gate_ms,
+            "active_experts": active,
+            "down_kernel": {"achieved": down_bytes / (down_ms * 1e-3) / 1e9, "avg_launch_ms": down_ms,
+                            "algorithmic_bytes_per_launch": down_bytes},
+            "stage_ms": {"router_route_permute_quant": pre_ms, "gate_up": gate_ms, "down": down_ms,
+                         "exit_add_norm": post_ms},
+        },
+        "e2e": {"value": M / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": 2 * M * H * 2,
+                "d2h_bytes_per_step": 2 * M * H * 2, "ms_per_step": e2e_ms},
+        # router, route, permute (hist, scan, scatter), quant_scatter, gate_up, down, exit
+        "gpu_launches": 9 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def cpu_prefill_baseline(layer, seconds: float) -> dict:
     """Oracle port on the host cores over a bounded slice of the prefill batch
     (the first prompts, 512 tokens), repeated until `seconds` have passed."""
@@ -560,8 +756,14 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=4, help="weight sets rotated across steps")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: the default 64-token step; prefill: ~8k ragged tokens, one GPU")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed"],
+                    help="decode: the default 64-token step; prefill: ~8k ragged tokens, one GPU; "
+                         "mixed: 64 decode + 1280 packed prompt rows in one call, one GPU")
+    ap.add_argument("--row-reuse", action="store_true", help="mixed: run the MoE on the row-reuse bucket")
+    ap.add_argument("--experts", type=int, default=E, help="mixed: routed experts")
+    ap.add_argument("--inter", type=int, default=I, help="mixed: expert intermediate size")
+    ap.add_argument("--prefill-min", type=int, default=0,
+                    help="mixed: MoE rows from which the tcgen05 path runs (0: the library default)")
     ap.add_argument("--prefill-tokens", type=int, default=0,
                     help="prefill: a flat batch of this many tokens instead of the ragged 64-prompt batch")
     ap.add_argument("--replicas", action="store_true",
@@ -581,10 +783,15 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if args.workload == "prefill":
+    if args.workload in ("prefill", "mixed"):
         if world > 1:
-            raise SystemExit("--workload prefill runs on one GPU")
-        run_prefill(args, dev)
+            raise SystemExit(f"--workload {args.workload} runs on one GPU")
+        if args.workload == "mixed":
+            if args.layers == 4:
+                args.layers = 2
+            run_mixed(args, dev)
+        else:
+            run_prefill(args, dev)
         return
     if world > 1:
         import datetime

@@ -66,14 +66,15 @@ __global__ void __launch_bounds__(kNormThreads)
                     const int32_t* __restrict__ inverse, const int32_t* __restrict__ inv_rows,
                     const __nv_bfloat16* __restrict__ weights, int k, int P,
                     __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ norm_w,
-                    float eps, int W, __nv_bfloat16* __restrict__ out) {
+                    float eps, int W, __nv_bfloat16* __restrict__ out, RowGather rows) {
   pdl_wait();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   const int nchunks = W / 8;
   float v[kNormMaxChunks][8];
   float ss = 0.f;
-  const int src = (SRC == NS_COMBINE && inverse) ? inverse[row] : row;
+  const int src = (SRC == NS_COMBINE && inverse) ? inverse[row]
+                  : SRC == NS_ROWS ? static_cast<int>(gather_row(rows, row)) : row;
   float g = 0.f;
   if (SRC != NS_ADD) g = sigmoid_bf16(gate + static_cast<int64_t>(src) * gate_stride);
 #pragma unroll
@@ -98,16 +99,16 @@ __global__ void __launch_bounds__(kNormThreads)
         const float* d = static_cast<const float*>(p0);
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int r = 0; r < k; ++r) {
-          const int dr = inv_rows[row * k + r];
+          const int dr = inv_rows[src * k + r];
           if (dr < 0) continue;
-          const float w = __bfloat162float(weights[row * k + r]);
+          const float w = __bfloat162float(weights[src * k + r]);
           const float4 lo = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(dr) * W + c);
           const float4 hi = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(dr) * W + c + 4);
           acc[0] += lo.x * w; acc[1] += lo.y * w; acc[2] += lo.z * w; acc[3] += lo.w * w;
           acc[4] += hi.x * w; acc[5] += hi.y * w; acc[6] += hi.z * w; acc[7] += hi.w * w;
         }
-        const float4 slo = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + row) * W + c);
-        const float4 shi = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + row) * W + c + 4);
+        const float4 slo = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + src) * W + c);
+        const float4 shi = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + src) * W + c + 4);
         const float sh[8] = {slo.x, slo.y, slo.z, slo.w, shi.x, shi.y, shi.z, shi.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -161,15 +162,22 @@ int check_norm_args(const void* residual, const void* norm_w, const void* out, i
 int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
                                  const void* weights, int T, int k, const void* gate,
                                  int64_t gate_stride, void* residual, const void* norm_w, float eps,
-                                 void* out, cudaStream_t s) {
+                                 void* out, cudaStream_t s, const int64_t* inverse, int T_out,
+                                 int32_t* status) {
   if (T <= 0) return D3_OK;
-  launch_kernel(add_norm_kernel<NS_ROWS>, dim3(T), dim3(kNormThreads), 0, s,
+  RowGather rows;
+  rows.keep = inverse;
+  rows.x_rows = T;
+  rows.status = status;
+  const int nrows = inverse ? T_out : T;
+  if (nrows <= 0) return D3_OK;
+  launch_kernel(add_norm_kernel<NS_ROWS>, dim3(nrows), dim3(kNormThreads), 0, s,
                 static_cast<const void*>(d), static_cast<const void*>(nullptr),
                 static_cast<const __nv_bfloat16*>(gate), gate_stride,
                 static_cast<const int32_t*>(nullptr), inv_rows,
                 static_cast<const __nv_bfloat16*>(weights), k, T * k,
                 static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(norm_w), eps,
-                W, static_cast<__nv_bfloat16*>(out));
+                W, static_cast<__nv_bfloat16*>(out), rows);
   return check_launch("combine_rows_add_norm");
 }
 
@@ -189,7 +197,7 @@ extern "C" int d3_add_norm(const void* x, void* residual, const void* weight, fl
                 static_cast<const int32_t*>(nullptr), static_cast<const int32_t*>(nullptr),
                 static_cast<const __nv_bfloat16*>(nullptr), 0, 0,
                 static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(weight), eps,
-                W, static_cast<__nv_bfloat16*>(out));
+                W, static_cast<__nv_bfloat16*>(out), RowGather{});
   return check_launch("add_norm");
 }
 
@@ -208,6 +216,6 @@ extern "C" int d3_combine_experts_add_norm(const void* routed, const void* share
                 static_cast<const __nv_bfloat16*>(gate), gate_stride, inverse,
                 static_cast<const int32_t*>(nullptr), static_cast<const __nv_bfloat16*>(nullptr), 0, 0,
                 static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(weight), eps,
-                W, static_cast<__nv_bfloat16*>(out));
+                W, static_cast<__nv_bfloat16*>(out), RowGather{});
   return check_launch("combine_experts_add_norm");
 }

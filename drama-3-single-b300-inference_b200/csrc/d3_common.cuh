@@ -13,13 +13,35 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "d3_internal.h"
+
 namespace d3 {
 
 // Status codes a kernel writes into its caller-provided status word.
 enum DeviceStatus : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // an mbarrier or dependency wait gave up (bounded spin)
+  kDevBadRow = 2,       // a row map named a row outside its tensor (row 0 was used)
 };
+
+// Row gather (RowGather, d3_internal.h): a keep value outside [0, x_rows)
+// records kDevBadRow in the status word and reads row 0 instead, so no access
+// leaves the tensor.
+
+__device__ __forceinline__ int64_t gather_row(const RowGather& g, int64_t t) {
+  if (g.keep == nullptr) return t;
+  const int64_t r = __ldg(g.keep + t);
+  if (r >= 0 && r < g.x_rows) return r;
+  if (g.status) atomicExch(g.status, kDevBadRow);
+  return 0;
+}
+
+__device__ __forceinline__ bool padding_row(const PaddingRoute& p, int64_t t) {
+  if (p.slots == nullptr) return false;
+  const int64_t slot = p.slots_i64 ? __ldg(static_cast<const int64_t*>(p.slots) + t)
+                                   : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(p.slots) + t));
+  return slot >= p.padding_start;
+}
 
 // Upper bound of any device-side wait, in nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

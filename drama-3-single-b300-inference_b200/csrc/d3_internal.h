@@ -7,6 +7,24 @@
 
 namespace d3 {
 
+// Row maps of a mixed decode + packed-prefill layer call
+// (src/drama3/mixed_model.py:193-246). MoE row t reads x row keep[t]
+// (keep == nullptr: row t); keep values must lie in [0, x_rows).
+struct RowGather {
+  const int64_t* keep = nullptr;
+  int64_t x_rows = 0;
+  int32_t* status = nullptr;
+};
+
+// Reserved padding rows (src/drama3/moe_input.py:32-36): a row whose slot
+// (int32 or int64) is at or above padding_start routes with row 0's logits.
+// slots == nullptr: no such rows.
+struct PaddingRoute {
+  const void* slots = nullptr;
+  int slots_i64 = 0;
+  int64_t padding_start = 0;
+};
+
 
 // Activation quantisation into expert order: token t is quantised once (1x128
 // groups, e4m3 + f32 scale) and written to rows inv_rows[t*k + j] (negative =
@@ -14,7 +32,8 @@ namespace d3 {
 // The first CTA also zeroes zero[0..nzero) (the engines' work counters).
 void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
-                          cudaStream_t s, int32_t* zero = nullptr, int nzero = 0);
+                          cudaStream_t s, int32_t* zero = nullptr, int nzero = 0,
+                          const RowGather& rg = RowGather{});
 
 // Weight-only GEMV activation prep: x bf16 [T,K] -> f16 [T,K] scaled by a
 // power of two per 1x128 group (exact), inv f32 [T,K/128] = the inverse factor.
@@ -30,22 +49,24 @@ void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const v
                          int T, int k, int with_shared, const void* gate, int64_t gate_stride,
                          void* routed_out, void* shared_out, void* out, cudaStream_t s);
 
-// Router projection (fixed fp32 summation order); from 256 tokens a tiled
-// kernel (same order) streams 32-token x 16-row tiles.
 // Fused layer exit: routed/shared rows combined as in
-// d3_combine_experts_add_norm, residual updated in place, out = RMSNorm.
+// d3_combine_experts_add_norm, residual updated in place, out = RMSNorm. With
+// `inverse` (int64 [T_out]) residual row t takes MoE row inverse[t].
 int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
                                  const void* weights, int T, int k, const void* gate,
                                  int64_t gate_stride, void* residual, const void* norm_w, float eps,
-                                 void* out, cudaStream_t s);
+                                 void* out, cudaStream_t s, const int64_t* inverse = nullptr,
+                                 int T_out = 0, int32_t* status = nullptr);
 
+// Router projection (fixed fp32 summation order); from 256 tokens a tiled
+// kernel (same order) streams 32-token x 16-row tiles.
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
-                          cudaStream_t s);
+                          cudaStream_t s, const RowGather& rg = RowGather{});
 
 void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
                        const float* bias, int64_t* ids, void* weights, int weights_dtype,
-                       cudaStream_t s);
+                       cudaStream_t s, const PaddingRoute& pr = PaddingRoute{});
 
 // route_topk followed by permute (two launches).
 int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, int T, int E,
@@ -53,7 +74,7 @@ int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, i
                          int block_m, int32_t* counts, int32_t* starts, int32_t* total,
                          int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
                          int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s,
-                         int32_t* scratch = nullptr);
+                         int32_t* scratch = nullptr, const PaddingRoute& pr = PaddingRoute{});
 
 // Stable token->expert bucketing. With `scratch` (permute_scratch_ints(E)
 // ints) and T*k >= 8192 pairs it runs as three multi-CTA kernels; otherwise as

@@ -114,7 +114,8 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
 __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                      int H, int k, const int32_t* __restrict__ inv_rows, int P,
                                      int with_shared, uint8_t* __restrict__ xq,
-                                     float* __restrict__ sx, int32_t* __restrict__ zero, int nzero) {
+                                     float* __restrict__ sx, int32_t* __restrict__ zero, int nzero,
+                                     RowGather rg) {
   pdl_wait();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
@@ -126,7 +127,7 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
   const int g = 2 * rp.gp + half;
   const bool valid = g < G;
   uint4 v = make_uint4(0, 0, 0, 0);
-  if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * x_stride + g * 128 + hl * 8));
+  if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + gather_row(rg, t) * x_stride + g * 128 + hl * 8));
   float f[8];
   unpack_bf16x8(v, f);
   float amax = 0.f;
@@ -482,11 +483,11 @@ inline unsigned pair_blocks(int rows, int cols) {
 
 void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           const int32_t* inv_rows, int P, int with_shared, uint8_t* xq, float* sx,
-                          cudaStream_t s, int32_t* zero, int nzero) {
+                          cudaStream_t s, int32_t* zero, int nzero, const RowGather& rg) {
   if (T <= 0) return;
   launch_kernel(quant_scatter_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, s,
                 static_cast<const __nv_bfloat16*>(x), x_stride, T, H, k, inv_rows, P, with_shared, xq,
-                sx, zero, nzero);
+                sx, zero, nzero, rg);
 }
 
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,

@@ -203,9 +203,12 @@ int check_experts(const d3_experts_t* e, const char* what) {
 // Steps 1-5 on an already carved workspace. ids/weights are device tensors
 // [T,k]; gate (nullable) feeds the shared-expert combine.
 struct AddNorm {
-  void* residual = nullptr;     // bf16 [T, H], updated in place
-  const void* weight = nullptr; // bf16 [H]
+  void* residual = nullptr;         // bf16 [T (or T_out), H], updated in place
+  const void* weight = nullptr;     // bf16 [H]
   float eps = 0.f;
+  const int64_t* inverse = nullptr; // [T_out]: residual row t takes MoE row inverse[t]
+  int T_out = 0;
+  int32_t* status = nullptr;        // receives kDevBadRow for an inverse value outside [0, T)
 };
 
 // Step 5: the fixed-order combine, or (with an AddNorm) the combine fused with
@@ -215,7 +218,8 @@ int finish_layer(const MoeBuffers& b, int H, const void* weights, int T, int k, 
                  void* out, const AddNorm& an, cudaStream_t s) {
   if (an.residual)
     return launch_combine_rows_add_norm(b.d, H, b.inv, weights, T, k, gate, gate_stride,
-                                        an.residual, an.weight, an.eps, out, s);
+                                        an.residual, an.weight, an.eps, out, s, an.inverse,
+                                        an.T_out, an.status);
   launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
                       shared_out, out, s);
   return check_launch("combine_rows");
@@ -225,7 +229,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
                 int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
                 int64_t gate_stride, void* routed_out, void* shared_out, void* out,
                 const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted,
-                const AddNorm& an = AddNorm{}) {
+                const AddNorm& an = AddNorm{}, const RowGather& rg = RowGather{}) {
   const int E = ex->E, I = ex->I, H = ex->H;
   const int P = T * k;
   const int has_shared = sh ? 1 : 0;
@@ -238,7 +242,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
                         b.inv, b.active, b.n_active, s, b.permute_scratch);
     if (rc) return rc;
   }
-  launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2);
+  launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2, rg);
   if ((rc = check_launch("quant_scatter"))) return rc;
 
   const int sms = sm_count();
@@ -453,7 +457,8 @@ static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
                           const float* router_bias, int T, int k, const d3_experts_t* experts,
                           const d3_experts_t* shared, void* out, int64_t* ids_out,
                           void* weights_out, void* workspace, size_t workspace_bytes,
-                          int32_t* status, d3_stream_t stream, const AddNorm& an) {
+                          int32_t* status, d3_stream_t stream, const AddNorm& an_in,
+                          const d3_rows_t* rows = nullptr) {
   int rc = check_common(x, x_stride, T, k, experts, shared, workspace, workspace_bytes,
                         "moe_layer");
   if (rc) return rc;
@@ -466,16 +471,31 @@ static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int64_t* ids = ids_out ? ids_out : b.ids;
   void* wts = weights_out ? weights_out : static_cast<void*>(b.weights);
+  int32_t* st = status ? status : b.status;
+  RowGather rg;
+  PaddingRoute pr;
+  AddNorm an = an_in;
+  if (rows) {
+    rg.keep = rows->keep;
+    rg.x_rows = rows->x_rows;
+    rg.status = st;
+    pr.slots = rows->row_slots;
+    pr.slots_i64 = rows->row_slots_int64;
+    pr.padding_start = rows->padding_start;
+    an.inverse = rows->inverse;
+    an.T_out = rows->T_out;
+    an.status = st;
+  }
   stage_mark(0, s);
-  launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s);
+  launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s, rg);
   if ((rc = check_launch("router_logits"))) return rc;
   const int P = T * k;
   rc = launch_route_permute(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts,
                             D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
-                            b.inv, b.active, b.n_active, s, b.permute_scratch);
+                            b.inv, b.active, b.n_active, s, b.permute_scratch, pr);
   if (rc) return rc;
   return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
-                     nullptr, out, b, status ? status : b.status, s, true, an);
+                     nullptr, out, b, st, s, true, an, rg);
 }
 
 extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w,
@@ -503,6 +523,35 @@ extern "C" int d3_moe_layer_add_norm(const void* x, int64_t x_stride, const void
   an.eps = eps;
   return moe_layer_impl(x, x_stride, router_w, router_bias, T, k, experts, shared, out, ids_out,
                         weights_out, workspace, workspace_bytes, status, stream, an);
+}
+
+extern "C" int d3_moe_layer_rows(const void* x, int64_t x_stride, const void* router_w,
+                                 const float* router_bias, int T, int k,
+                                 const d3_experts_t* experts, const d3_experts_t* shared,
+                                 const d3_rows_t* rows, void* residual, const void* norm_weight,
+                                 float eps, void* out, int64_t* ids_out, void* weights_out,
+                                 void* workspace, size_t workspace_bytes, int32_t* status,
+                                 d3_stream_t stream) {
+  if (rows) {
+    D3_REQUIRE(rows->keep == nullptr || rows->x_rows > 0,
+               "moe_layer_rows: keep needs the row count of x (x_rows > 0)");
+    D3_REQUIRE(rows->inverse == nullptr || (residual != nullptr && rows->T_out >= 0),
+               "moe_layer_rows: an inverse map needs the fused exit (residual) and T_out >= 0");
+    D3_REQUIRE(rows->row_slots == nullptr || rows->padding_start > 0,
+               "moe_layer_rows: padding_start must be a positive reserved-slot boundary");
+  }
+  AddNorm an;
+  if (residual) {
+    D3_REQUIRE(norm_weight && aligned(residual, 16) && aligned(norm_weight, 16),
+               "moe_layer_rows: null or misaligned residual / norm weight");
+    D3_REQUIRE(experts && experts->H % 8 == 0 && experts->H <= 8192,
+               "moe_layer_rows: H must be a multiple of 8 up to 8192");
+    an.residual = residual;
+    an.weight = norm_weight;
+    an.eps = eps;
+  }
+  return moe_layer_impl(x, x_stride, router_w, router_bias, T, k, experts, shared, out, ids_out,
+                        weights_out, workspace, workspace_bytes, status, stream, an, rows);
 }
 
 namespace {

@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(256)
     router_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
                          const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
                          int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
-                         int64_t out_stride) {
+                         int64_t out_stride, RowGather rg) {
   pdl_wait();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(256)
   for (int idx = threadIdx.x; idx < nt * chunks; idx += blockDim.x) {
     const int t = idx / chunks, c = idx - t * chunks;
     reinterpret_cast<uint4*>(xs + t * H)[c] =
-        __ldg(reinterpret_cast<const uint4*>(x + (t0 + t) * x_stride) + c);
+        __ldg(reinterpret_cast<const uint4*>(x + gather_row(rg, t0 + t) * x_stride) + c);
   }
   __syncthreads();
   if (r >= R) return;
@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kRtThreads)
     router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
                                const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
                                int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
-                               int64_t out_stride) {
+                               int64_t out_stride, RowGather rg) {
   pdl_wait();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw);
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kRtThreads)
       const int k0 = 256 * i + 8 * c;
       if (k0 >= H) continue;  // half-filled last block: those lanes skip it below
       const __nv_bfloat16* src =
-          row < kRtTok ? x + static_cast<int64_t>(t0 + min(row, nt - 1)) * x_stride + k0
+          row < kRtTok ? x + gather_row(rg, t0 + min(row, nt - 1)) * x_stride + k0
                        : w + static_cast<int64_t>(r0 + min(row - kRtTok, nr - 1)) * H + k0;
       cp_async_16(st + row * 256 + 8 * c, src);
     }
@@ -213,7 +213,7 @@ __device__ __forceinline__ uint64_t route_key(float v, int col) {
 // written out.
 template <int PER_LANE>
 __device__ __forceinline__ void route_token(const void* __restrict__ logits, int f32_in,
-                                            int64_t stride, int t, int E, int k,
+                                            int64_t stride, int t, int lt, int E, int k,
                                             const float* __restrict__ bias,
                                             int64_t* __restrict__ ids, void* __restrict__ weights,
                                             int f32_out, int* ids_smem) {
@@ -225,8 +225,8 @@ __device__ __forceinline__ void route_token(const void* __restrict__ logits, int
   for (int i = 0; i < PER_LANE; ++i) {
     const int c = lane + 32 * i;
     if (c < E) {
-      float l = f32_in ? static_cast<const float*>(logits)[t * stride + c]
-                       : __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[t * stride + c]);
+      float l = f32_in ? static_cast<const float*>(logits)[lt * stride + c]
+                       : __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[lt * stride + c]);
       if (bias) l += bias[c];
       v[i] = l;
       key[i] = route_key(l, c);
@@ -287,14 +287,19 @@ __device__ __forceinline__ void route_token(const void* __restrict__ logits, int
   }
 }
 
+// Reserved padding rows (slot >= padding_start; src/drama3/moe_input.py:32-36)
+// route with row 0's logits; their ids and weights are still written to their
+// own row.
 template <int PER_LANE>
 __global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_t stride, int T,
                              int E, int k, const float* __restrict__ bias,
-                             int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out) {
+                             int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out,
+                             PaddingRoute pr) {
   pdl_wait();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
-  route_token<PER_LANE>(logits, f32_in, stride, t, E, k, bias, ids, weights, f32_out, nullptr);
+  route_token<PER_LANE>(logits, f32_in, stride, t, padding_row(pr, t) ? 0 : t, E, k, bias, ids,
+                        weights, f32_out, nullptr);
 }
 
 // ---------------------------------------------------------------- permute --
@@ -608,7 +613,7 @@ int launch_ep_plan(const int64_t* ids, int P, int experts_per_rank, int ranks,
 
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
-                          cudaStream_t s) {
+                          cudaStream_t s, const RowGather& rg) {
   if (T <= 0 || R <= 0) return;
   if (T >= kRouterTiledMinTokens) {
     static bool configured[64] = {false};
@@ -622,29 +627,29 @@ void launch_router_logits(const void* x, int64_t x_stride, const void* w, const 
     dim3 grid((R + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
     launch_kernel(router_logits_tiled_kernel, dim3(grid), dim3(kRtThreads), kRtSmem, s, 
         static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
-        nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
+        nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride, rg);
     return;
   }
   dim3 grid((R + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
   const size_t smem = static_cast<size_t>(kRouterTokens) * H * 2;  // <= 48 KB for H <= 3072
   launch_kernel(router_logits_kernel, dim3(grid), dim3(256), smem, s, 
       static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(w), bias,
-      nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride);
+      nbias, R, H, T, static_cast<__nv_bfloat16*>(logits), logits_stride, rg);
 }
 
 void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
                        const float* bias, int64_t* ids, void* weights, int weights_dtype,
-                       cudaStream_t s) {
+                       cudaStream_t s, const PaddingRoute& pr) {
   if (T <= 0) return;
   const unsigned grid = static_cast<unsigned>((T + 7) / 8);
   const int f32_in = logits_dtype == D3_DTYPE_F32, f32_out = weights_dtype == D3_DTYPE_F32;
   const int per_lane = (E + 31) / 32;
   if (per_lane <= 4)
-    launch_kernel(route_kernel<4>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+    launch_kernel(route_kernel<4>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out, pr);
   else if (per_lane <= 8)
-    launch_kernel(route_kernel<8>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+    launch_kernel(route_kernel<8>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out, pr);
   else
-    launch_kernel(route_kernel<kMaxPerLane>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out);
+    launch_kernel(route_kernel<kMaxPerLane>, dim3(grid), dim3(256), 0, s, logits, f32_in, stride, T, E, k, bias, ids, weights, f32_out, pr);
 }
 
 int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, int T, int E,
@@ -652,11 +657,11 @@ int launch_route_permute(const void* logits, int logits_dtype, int64_t stride, i
                          int block_m, int32_t* counts, int32_t* starts, int32_t* total,
                          int32_t* sorted_ids, int32_t* expert_ids, int64_t max_rows,
                          int32_t* inv_rows, int32_t* active, int32_t* n_active, cudaStream_t s,
-                         int32_t* scratch) {
+                         int32_t* scratch, const PaddingRoute& pr) {
   if (T <= 0) return D3_OK;
   // routing spreads tokens over many CTAs (a warp each); a single-CTA fusion
   // of routing and bucketing measured slower than the two launches
-  launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype, s);
+  launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype, s, pr);
   int rc = check_launch("route_topk");
   if (rc) return rc;
   return launch_permute(ids, T, k, E, block_m, counts, starts, total, sorted_ids, expert_ids,
@@ -736,6 +741,26 @@ extern "C" int d3_route_topk(const void* logits, int logits_dtype, int64_t strid
   D3_REQUIRE(weights_dtype == D3_DTYPE_BF16 || weights_dtype == D3_DTYPE_F32, "route_topk: weights must be bf16 or f32");
   launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype,
                     reinterpret_cast<cudaStream_t>(stream));
+  return check_launch("route_topk");
+}
+
+extern "C" int d3_route_topk_rows(const void* logits, int logits_dtype, int64_t stride, int T,
+                                  int E, int k, const float* bias, const void* row_slots,
+                                  int row_slots_int64, int64_t padding_start, int64_t* ids,
+                                  void* weights, int weights_dtype, d3_stream_t stream) {
+  D3_REQUIRE(row_slots == nullptr || padding_start > 0,
+             "route_topk_rows: padding_start must be a positive reserved-slot boundary");
+  D3_REQUIRE(T >= 0 && E > 0 && E <= 1024, "route_topk: E=%d must be in [1, 1024]", E);
+  D3_REQUIRE(k > 0 && k <= 32 && k <= E, "route_topk: k=%d must be in [1, min(32, E)]", k);
+  D3_REQUIRE(stride >= E, "route_topk: logits row stride must be >= E");
+  D3_REQUIRE(logits_dtype == D3_DTYPE_BF16 || logits_dtype == D3_DTYPE_F32, "route_topk: logits must be bf16 or f32");
+  D3_REQUIRE(weights_dtype == D3_DTYPE_BF16 || weights_dtype == D3_DTYPE_F32, "route_topk: weights must be bf16 or f32");
+  PaddingRoute pr;
+  pr.slots = row_slots;
+  pr.slots_i64 = row_slots_int64 ? 1 : 0;
+  pr.padding_start = padding_start;
+  launch_route_topk(logits, logits_dtype, stride, T, E, k, bias, ids, weights, weights_dtype,
+                    reinterpret_cast<cudaStream_t>(stream), pr);
   return check_launch("route_topk");
 }
 

@@ -43,6 +43,20 @@ class D3Experts(ctypes.Structure):
     ]
 
 
+class D3Rows(ctypes.Structure):
+    """Mirror of d3_rows_t (row maps of the mixed decode + prefill call)."""
+
+    _fields_ = [
+        ("keep", _c_void_p),
+        ("x_rows", _i64),
+        ("inverse", _c_void_p),
+        ("T_out", _i32),
+        ("row_slots", _c_void_p),
+        ("row_slots_int64", _i32),
+        ("padding_start", _i64),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/d3moe.h declares.
 SIGNATURES: dict[str, tuple] = {
     "d3_version": (_i32, []),
@@ -102,6 +116,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
          _c_void_p, _c_void_p],
     ),
+    "d3_route_topk_rows": (
+        _i32,
+        [_c_void_p, _i32, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p, _i32, _i64, _c_void_p,
+         _c_void_p, _i32, _c_void_p],
+    ),
     "d3_ep_dispatch_meta": (_i32, [_c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_gather_rows": (_i32, [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p]),
     "d3_combine_pairs": (
@@ -119,6 +138,12 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.POINTER(D3Experts),
          ctypes.POINTER(D3Experts), _c_void_p, _c_void_p, ctypes.c_float, _c_void_p, _c_void_p,
          _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
+    ),
+    "d3_moe_layer_rows": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.POINTER(D3Experts),
+         ctypes.POINTER(D3Experts), ctypes.POINTER(D3Rows), _c_void_p, _c_void_p, ctypes.c_float,
+         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
 }
 

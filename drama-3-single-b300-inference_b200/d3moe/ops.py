@@ -15,7 +15,7 @@ import ctypes
 import torch
 
 from . import _lib
-from ._lib import D3Experts, call
+from ._lib import D3Experts, D3Rows, call
 
 FP8 = torch.float8_e4m3fn
 
@@ -100,22 +100,43 @@ def router_logits(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def _check_row_slots(row_slots, padding_start, T, device):
+    if (row_slots is None) != (padding_start is None):
+        raise ValueError("Reserved padding routing requires both row_slots and padding_start")
+    if row_slots is None:
+        return
+    if (row_slots.shape != (T,) or row_slots.stride(0) != 1 or row_slots.device != device
+            or row_slots.dtype not in (torch.int32, torch.int64)):
+        raise ValueError("Expected one contiguous integer slot per MoE row on the same device")
+    if not isinstance(padding_start, int) or padding_start <= 0:
+        raise ValueError("padding_start must be a positive reserved-slot boundary")
+
+
 def route_topk(logits: torch.Tensor, k: int = 8, bias: torch.Tensor | None = None,
-               weights_dtype: torch.dtype | None = None):
-    """Returns (weights [T,k], ids int64 [T,k]) like src/drama3/kernels.py:379-383."""
+               weights_dtype: torch.dtype | None = None, row_slots: torch.Tensor | None = None,
+               padding_start: int | None = None):
+    """Returns (weights [T,k], ids int64 [T,k]) like src/drama3/kernels.py:379-383.
+    With row_slots/padding_start, rows whose slot is >= padding_start route with
+    row 0's logits (src/drama3/moe_input.py:32-36)."""
     _require_cuda(logits, bias)
     if logits.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError("router logits must be bfloat16 or float32")
     T, E = logits.shape
+    _check_row_slots(row_slots, padding_start, T, logits.device)
     wdt = weights_dtype or logits.dtype
     ids = torch.empty((T, k), dtype=torch.int64, device=logits.device)
     w = torch.empty((T, k), dtype=wdt, device=logits.device)
     if bias is not None:
         bias = bias.to(torch.float32).contiguous()
-    call("d3_route_topk", logits.data_ptr(),
-         _lib.D3_DTYPE_F32 if logits.dtype == torch.float32 else _lib.D3_DTYPE_BF16,
-         _row_stride(logits), T, E, k, _ptr(bias), ids.data_ptr(), w.data_ptr(),
-         _lib.D3_DTYPE_F32 if wdt == torch.float32 else _lib.D3_DTYPE_BF16, _stream(logits.device))
+    ldt = _lib.D3_DTYPE_F32 if logits.dtype == torch.float32 else _lib.D3_DTYPE_BF16
+    wdt_tag = _lib.D3_DTYPE_F32 if wdt == torch.float32 else _lib.D3_DTYPE_BF16
+    if row_slots is not None:
+        call("d3_route_topk_rows", logits.data_ptr(), ldt, _row_stride(logits), T, E, k, _ptr(bias),
+             row_slots.data_ptr(), 1 if row_slots.dtype == torch.int64 else 0, padding_start,
+             ids.data_ptr(), w.data_ptr(), wdt_tag, _stream(logits.device))
+    else:
+        call("d3_route_topk", logits.data_ptr(), ldt, _row_stride(logits), T, E, k, _ptr(bias),
+             ids.data_ptr(), w.data_ptr(), wdt_tag, _stream(logits.device))
     return w, ids
 
 
@@ -328,36 +349,70 @@ def moe_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
     return routed, shared_out
 
 
+def _row_map(t, name, device):
+    if t is None:
+        return None
+    if t.dtype != torch.int64 or t.dim() != 1 or t.stride(0) != 1 or t.device != device:
+        raise ValueError(f"{name} must be a contiguous int64 vector on the layer's device")
+    return t
+
+
 def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, experts, shared, k: int = 8,
               router_bias: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
               out: torch.Tensor | None = None, return_routing: bool = False,
               status: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-              norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6):
+              norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
+              keep: torch.Tensor | None = None, inverse: torch.Tensor | None = None,
+              row_slots: torch.Tensor | None = None, padding_start: int | None = None):
     """Whole MoE layer: out = routed + bf16(shared * bf16(sigmoid(gate))).
     With `residual` and `norm_weight` the layer exit is fused in: residual is
     updated in place with the bf16-fma combine (combine_experts_add_norm) and
-    out = RMSNorm(residual) * (1 + norm_weight)."""
+    out = RMSNorm(residual) * (1 + norm_weight).
+
+    Row maps of the mixed decode + packed-prefill call
+    (src/drama3/mixed_model.py:193-246): `keep` (int64 [T]) runs the MoE over
+    x[keep] without materialising it (T = len(keep)); `inverse` (int64
+    [T_out], fused exit only) makes residual row t take MoE row inverse[t];
+    `row_slots` (int32/int64 [T]) with `padding_start` routes rows whose slot
+    is >= padding_start with row 0's logits (src/drama3/moe_input.py:32-36)."""
     _require_cuda(x, router_weight, router_bias)
     ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
     sv = shared if isinstance(shared, ExpertView) else ExpertView(shared)
-    T, H = x.shape
+    H = x.shape[1]
+    keep = _row_map(keep, "keep", x.device)
+    inverse = _row_map(inverse, "inverse", x.device)
+    T = len(keep) if keep is not None else x.shape[0]
+    _check_row_slots(row_slots, padding_start, T, x.device)
+    if inverse is not None and residual is None:
+        raise ValueError("an inverse row map needs the fused exit (residual and norm_weight)")
+    T_out = len(inverse) if inverse is not None else T
     if router_weight.shape != (ev.E + 1, H) or router_weight.dtype != torch.bfloat16:
         raise ValueError("router_weight must be bf16 [E+1, H] (router rows + shared-gate row)")
     if out is None:
-        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        out = torch.empty((T_out, H), dtype=torch.bfloat16, device=x.device)
     if workspace is None:
         workspace = moe_workspace(T, k, ev.E, ev.I, ev.H, True, x.device)
     ids = torch.empty((T, k), dtype=torch.int64, device=x.device) if return_routing else None
     wts = torch.empty((T, k), dtype=torch.bfloat16, device=x.device) if return_routing else None
     if router_bias is not None:
         router_bias = router_bias.to(torch.float32).contiguous()
+    nw = None
     if residual is not None:
         if norm_weight is None:
             raise ValueError("the fused layer exit needs norm_weight with residual")
         _require_cuda(residual, norm_weight)
         nw = _norm_args(residual, norm_weight)
-        if residual.shape != (T, H):
-            raise ValueError("residual must be [T, H]")
+        if residual.shape != (T_out, H):
+            raise ValueError(f"residual must be [{T_out}, H]")
+    if keep is not None or inverse is not None or row_slots is not None:
+        rows = D3Rows(_ptr(keep), x.shape[0], _ptr(inverse), T_out, _ptr(row_slots),
+                      1 if row_slots is not None and row_slots.dtype == torch.int64 else 0,
+                      padding_start or 0)
+        call("d3_moe_layer_rows", x.data_ptr(), _row_stride(x), router_weight.data_ptr(),
+             _ptr(router_bias), T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct),
+             ctypes.byref(rows), _ptr(residual), _ptr(nw), float(norm_eps), out.data_ptr(), _ptr(ids),
+             _ptr(wts), workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(x.device))
+    elif residual is not None:
         call("d3_moe_layer_add_norm", x.data_ptr(), _row_stride(x), router_weight.data_ptr(),
              _ptr(router_bias), T, k, ctypes.byref(ev.struct), ctypes.byref(sv.struct),
              residual.data_ptr(), nw.data_ptr(), float(norm_eps), out.data_ptr(), _ptr(ids), _ptr(wts),

@@ -53,6 +53,7 @@ typedef struct CUstream_st* d3_stream_t; /* == cudaStream_t */
 /* Device status word values written by kernels that wait on barriers. */
 #define D3_STATUS_OK 0
 #define D3_STATUS_WAIT_TIMEOUT 1
+#define D3_STATUS_BAD_ROW 2 /* a row map named a row outside its tensor; row 0 was read instead */
 
 D3_API int d3_version(void);
 D3_API const char* d3_last_error_string(void);
@@ -100,6 +101,15 @@ D3_API int d3_router_logits(const void* x, int64_t x_stride, const void* w, int 
 D3_API int d3_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
                   const float* bias, int64_t* ids, void* weights, int weights_dtype,
                   d3_stream_t stream);
+
+/* d3_route_topk with reserved padding rows: with row_slots (int32, or int64
+ * when row_slots_int64 = 1) and padding_start > 0, a row whose slot is >=
+ * padding_start routes with row 0's logits; its ids and weights still go to
+ * its own row (src/drama3/moe_input.py:32-36, model.py:546-553). */
+D3_API int d3_route_topk_rows(const void* logits, int logits_dtype, int64_t stride, int T, int E,
+                              int k, const float* bias, const void* row_slots, int row_slots_int64,
+                              int64_t padding_start, int64_t* ids, void* weights, int weights_dtype,
+                              d3_stream_t stream);
 
 /* ---------------------------------------------------------- (a4) permute --
  * Token->expert bucketing with the reference's device layout
@@ -259,6 +269,39 @@ D3_API int d3_moe_layer_add_norm(const void* x, int64_t x_stride, const void* ro
                           float eps, void* out, int64_t* ids_out, void* weights_out,
                           void* workspace, size_t workspace_bytes, int32_t* status,
                           d3_stream_t stream);
+
+/* Row maps of the mixed decode + packed-prefill MoE call (decode rows first,
+ * then packed prompt rows and their padding; src/drama3/mixed_model.py:193-246):
+ *   keep        int64 [T]: MoE row t reads x row keep[t] (NULL: row t); x has
+ *               x_rows rows. Replaces normalized.index_select(0, keep).
+ *   inverse     int64 [T_out]: residual/output row t takes MoE row inverse[t]
+ *               (NULL: row t, T_out = T). Replaces the inverse gather of
+ *               combine_experts_add_norm_inverse (src/drama3/kernels.py:502-556);
+ *               needs the fused exit (residual != NULL).
+ *   row_slots   int32 or int64 [T] (row_slots_int64 = 1 for int64), with
+ *               padding_start > 0: MoE rows whose slot >= padding_start route
+ *               with row 0's logits (src/drama3/moe_input.py:32-36).
+ * A keep or inverse value outside its tensor sets D3_STATUS_BAD_ROW in the
+ * status word and reads row 0 in its place. */
+typedef struct d3_rows {
+  const int64_t* keep;
+  int64_t x_rows;
+  const int64_t* inverse;
+  int T_out;
+  const void* row_slots;
+  int row_slots_int64;
+  int64_t padding_start;
+} d3_rows_t;
+
+/* d3_moe_layer (residual == NULL: out bf16 [T,H]) or d3_moe_layer_add_norm
+ * (residual, out bf16 [T_out,H]) over the row maps `rows` (may be NULL). The
+ * workspace is sized for the T MoE rows. */
+D3_API int d3_moe_layer_rows(const void* x, int64_t x_stride, const void* router_w,
+                             const float* router_bias, int T, int k, const d3_experts_t* experts,
+                             const d3_experts_t* shared, const d3_rows_t* rows, void* residual,
+                             const void* norm_weight, float eps, void* out, int64_t* ids_out,
+                             void* weights_out, void* workspace, size_t workspace_bytes,
+                             int32_t* status, d3_stream_t stream);
 
 /* ---------------------------------------------- (e) expert parallelism --
  * The reference runs on one GPU and has no expert parallelism; these entry

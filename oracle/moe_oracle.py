@@ -167,12 +167,16 @@ def route_keys(v: np.ndarray) -> np.ndarray:
     return (ordered.astype(np.uint64) << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - cols)
 
 
-def route(logits, k: int = 8, bias=None):
+def route(logits, k: int = 8, bias=None, row_slots=None, padding_start=None):
     """src/drama3/kernels.py:360-383: fp32 softmax over all experts, top-k by
     logit (ties to the lower expert id), weights renormalised over the picks.
+    With row_slots/padding_start, rows whose slot is >= padding_start take
+    row 0's logits (src/drama3/moe_input.py:32-36).
     Returns (weights f32 [T,k], ids int64 [T,k]); callers round weights to the
     logits dtype (bf16 in the reference)."""
     v = np.asarray(logits, dtype=np.float32)
+    if row_slots is not None and padding_start:
+        v = np.where((np.asarray(row_slots) >= padding_start)[:, None], v[0:1], v)
     if bias is not None:
         v = (v + np.asarray(bias, dtype=np.float32)[None, :]).astype(np.float32)
     keys = route_keys(v)  # unique per row (the column is part of the key)
@@ -420,6 +424,25 @@ def moe_layer(x, router_w, ex: Experts, shared: Experts, k: int = 8, bias=None):
     routed, sh = moe_experts(x, ids, w, ex, shared)
     out = combine_experts(routed, sh, logits[:, E])
     return out, ids, w
+
+
+def moe_layer_rows(x, router_w, ex: Experts, shared: Experts, residual, norm_weight, eps=1e-6,
+                   k: int = 8, keep=None, inverse=None, row_slots=None, padding_start=None):
+    """The mixed decode + packed-prefill layer step (src/drama3/mixed_model.py:
+    193-246): moe_parts over x[keep] (model.py:490-518) with the padding-router
+    rule on row_slots (moe_input.py:32-36), then combine_experts_add_norm or its
+    _inverse form (kernels.py:448-556). Returns (out, residual_out, ids,
+    weights) in float32 holding bf16 values."""
+    x = np.asarray(x, dtype=np.float32)
+    xk = x if keep is None else x[np.asarray(keep)]
+    E = router_w.shape[0] - 1
+    logits = router_logits(xk, router_w)
+    w, ids = route(logits[:, :E], k, row_slots=row_slots, padding_start=padding_start)
+    w = bf16_round(w)
+    routed, sh = moe_experts(xk, ids, w, ex, shared)
+    out, res = combine_experts_add_norm(routed, sh, logits[:, E:E + 1], residual, norm_weight, eps,
+                                        inverse=inverse)
+    return out, res, ids, w
 
 
 # --------------------------------------------------------- synthetic data --
