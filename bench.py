@@ -716,6 +716,95 @@ def run_mixed(args, dev) -> None:
     print(json.dumps(line), flush=True)
 
 
+DENSE_SHAPES = ((9216, 2048, "QKV"), (12352, 2048, "GDN in"), (2048, 4096, "out / o_proj"),
+                (4096, 2048, "bench QKV"), (2048, 2048, "bench o_proj"))
+
+
+def run_dense(args, dev) -> None:
+    """The weight-only FP8 GEMV at the reference model's real projection shapes
+    (src/drama3/model.py:210-225) and the benchmark's, T in {1, 8, 16, 32, 64}.
+    Each shape rotates enough weight copies that every call streams its weight
+    from HBM (> 2x the 126 MB L2 per rotation). Roofline: weight + activation
+    bytes per call over HBM copy bandwidth."""
+    import torch
+
+    from d3moe import _lib, ops
+
+    lib = _lib.load()
+    pk = peaks()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    rows = []
+    total_bytes, total_ms = 0.0, 0.0
+    launches = 0
+    for N, K, name in DENSE_SHAPES:
+        wbytes = N * K + (N // 128) * (K // 128) * 4
+        sets = max(2, -(-260_000_000 // wbytes))
+        g = torch.Generator(device=dev)
+        g.manual_seed(N + K)
+        ws_q, ws_s = [], []
+        for _ in range(sets):
+            # N need not be a multiple of 128 (GDN in: 12352): the registered
+            # copy pads the last row block, the GEMV writes N columns
+            q, sc = ops.fp8_quantize_weight((torch.randn((N, K), generator=g, device=dev) * 0.02)
+                                            .to(torch.bfloat16))
+            ws_q.append(q)
+            ws_s.append(sc)
+        for T in (1, 8, 16, 32, 64):
+            x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+            nb = ctypes.c_size_t()
+            lib.d3_fp8_gemv_workspace_size(T, N, K, ctypes.byref(nb))
+            ws = torch.empty(nb.value, dtype=torch.uint8, device=dev)
+
+            def call(i):
+                _lib.call("d3_fp8_gemv", x.data_ptr(), K, ws_q[i % sets].data_ptr(), ws_s[i % sets].data_ptr(),
+                          T, N, K, y.data_ptr(), N, ws.data_ptr(), nb.value, None, sptr)
+
+            for i in range(max(args.warmup, sets)):
+                call(i)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(args.steps):
+                call(i)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / args.steps
+            nbytes = wbytes + T * K * 2 + T * N * 2
+            total_bytes += nbytes * args.steps
+            total_ms += ms * args.steps
+            launches += 2 * args.steps
+            rows.append({"shape": f"{N}x{K} ({name})", "T": T, "us": round(ms * 1e3, 2),
+                         "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                         "frac": round(nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)})
+        del ws_q, ws_s
+        torch.cuda.empty_cache()
+    achieved = total_bytes / (total_ms * 1e-3) / 1e9
+    line = {
+        "metric": "fp8_dense_gemv_bytes_per_s",
+        "value": achieved,
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / (args.steps * len(rows)),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 weights x f16 activations -> f32 (mma.sync), bf16 out",
+        "data": "synthetic",
+        "config": {"workload": "weight-only FP8 GEMV, real Drama-3 projection shapes and the benchmark's, "
+                               "T in {1,8,16,32,64}, weights rotated over > 260 MB per shape",
+                   "per_shape": rows},
+        "roofline": {"bound": "hbm", "kernel": "expert_gemv_kernel<EPI_DENSE> (+ dense_act_prep)",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"], "traffic": None},
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def cpu_prefill_baseline(layer, seconds: float) -> dict:
     """Oracle port on the host cores over a bounded slice of the prefill batch
     (the first prompts, 512 tokens), repeated until `seconds` have passed."""
@@ -756,9 +845,10 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=4, help="weight sets rotated across steps")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "dense"],
                     help="decode: the default 64-token step; prefill: ~8k ragged tokens, one GPU; "
-                         "mixed: 64 decode + 1280 packed prompt rows in one call, one GPU")
+                         "mixed: 64 decode + 1280 packed prompt rows in one call, one GPU; "
+                         "dense: the FP8 GEMV at the real projection shapes, one GPU")
     ap.add_argument("--row-reuse", action="store_true", help="mixed: run the MoE on the row-reuse bucket")
     ap.add_argument("--experts", type=int, default=E, help="mixed: routed experts")
     ap.add_argument("--inter", type=int, default=I, help="mixed: expert intermediate size")
@@ -783,6 +873,11 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.workload == "dense":
+        if world > 1:
+            raise SystemExit("--workload dense runs on one GPU")
+        run_dense(args, dev)
+        return
     if args.workload in ("prefill", "mixed"):
         if world > 1:
             raise SystemExit(f"--workload {args.workload} runs on one GPU")

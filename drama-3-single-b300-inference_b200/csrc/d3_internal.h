@@ -35,11 +35,23 @@ void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           cudaStream_t s, int32_t* zero = nullptr, int nzero = 0,
                           const RowGather& rg = RowGather{});
 
+// Already-quantised activations (q e4m3 [T,H], scales [H/128,T] when
+// transposed, else [T,H/128]) copied into expert order like
+// launch_quant_scatter (routed rows only).
+void launch_prequant_scatter(const uint8_t* q, int64_t q_stride, const float* qs, int transposed,
+                             int T, int H, int k, const int32_t* inv_rows, uint8_t* xq, float* sx,
+                             cudaStream_t s, int32_t* zero, int nzero);
+
 // Weight-only GEMV activation prep: x bf16 [T,K] -> f16 [T,K] scaled by a
 // power of two per 1x128 group (exact), inv f32 [T,K/128] = the inverse factor.
 // The first CTA also zeroes zero[0..nzero) (split-K tile counters, status).
+// With a gate (bf16 [T,K], row stride gate_stride) x is first replaced by
+// bf16(x * bf16(act(gate))), act = silu (GATE_SWIGLU) or sigmoid (GATE_SIGMOID).
+enum GateMode { GATE_NONE = 0, GATE_SWIGLU = 1, GATE_SIGMOID = 2 };
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
-                           cudaStream_t s, int32_t* zero = nullptr, int nzero = 0);
+                           cudaStream_t s, int32_t* zero = nullptr, int nzero = 0,
+                           const void* gate = nullptr, int64_t gate_stride = 0,
+                           int mode = GATE_NONE);
 
 // Final combine of the expert rows (see d3_moe_experts / d3_moe_layer).
 //   routed[t] = bf16(sum_r w[t,r] * d[inv_rows[t*k+r]])

@@ -146,13 +146,52 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
   }
 }
 
+// Already-quantised activations into expert order (the FlashInfer calling
+// convention): q e4m3 [T, H] rows are copied unchanged to rows inv_rows[t*k + j]
+// (negative = skipped) and their group scales, read from [H/128, T]
+// (transposed) or [T, H/128], to sx [rows, H/128]. One thread per 16 bytes.
+__global__ void prequant_scatter_kernel(const uint8_t* __restrict__ q, int64_t q_stride,
+                                        const float* __restrict__ qs, int transposed, int T, int H,
+                                        int k, const int32_t* __restrict__ inv_rows,
+                                        uint8_t* __restrict__ xq, float* __restrict__ sx,
+                                        int32_t* __restrict__ zero, int nzero) {
+  pdl_wait();
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
+  const int chunks = H / 16, G = H / 128;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(T) * chunks) return;
+  const int t = static_cast<int>(idx / chunks), c = static_cast<int>(idx - static_cast<int64_t>(t) * chunks);
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(q + static_cast<int64_t>(t) * q_stride) + c);
+  const bool scale_lane = (c & 7) == 0;
+  const int g = c >> 3;
+  float sc = 0.f;
+  if (scale_lane) sc = __ldg(qs + (transposed ? static_cast<int64_t>(g) * T + t : static_cast<int64_t>(t) * G + g));
+  for (int j = 0; j < k; ++j) {
+    const int d = __ldg(inv_rows + static_cast<int64_t>(t) * k + j);
+    if (d < 0) continue;
+    reinterpret_cast<uint4*>(xq + static_cast<int64_t>(d) * H)[c] = v;
+    if (scale_lane) sx[static_cast<int64_t>(d) * G + g] = sc;
+  }
+}
+
 // Exact bf16 -> f16 transfer: each 128-group is multiplied by 2^s with s chosen
 // so that the group amax lands in [2^14, 2^15); the GEMV multiplies by 2^-s.
 // Within each 128-element block, element k is stored at dense_act_position(k)
 // (expert_gemv.cuh).
+// Gated projection input (src/drama3/fused_projection.py:22-29): with a gate,
+// x becomes bf16(x * a) where a = bf16(silu(g)) (GATE_SWIGLU) or
+// bf16(sigmoid(g)) (GATE_SIGMOID), sigmoid(g) = 1 / (1 + exp(-g)) in fp32.
+__device__ __forceinline__ float gate_activation(float g, int mode) {
+  const float sg = 1.0f / (1.0f + expf(-g));
+  return bf16_round(mode == GATE_SWIGLU ? g * sg : sg);
+}
+
 __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                       int K, __half* __restrict__ xh, float* __restrict__ inv,
-                                      int32_t* __restrict__ zero, int nzero) {
+                                      int32_t* __restrict__ zero, int nzero,
+                                      const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
+                                      int mode) {
   pdl_wait();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
@@ -167,6 +206,14 @@ __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64
   if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + row * x_stride + g * 128 + hl * 8));
   float f[8];
   unpack_bf16x8(v, f);
+  if (mode != GATE_NONE) {
+    uint4 gv = make_uint4(0, 0, 0, 0);
+    if (valid) gv = __ldg(reinterpret_cast<const uint4*>(gate + row * gate_stride + g * 128 + hl * 8));
+    float gf[8];
+    unpack_bf16x8(gv, gf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = bf16_round(f[i] * gate_activation(gf[i], mode));
+  }
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
@@ -490,11 +537,22 @@ void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                 sx, zero, nzero, rg);
 }
 
+void launch_prequant_scatter(const uint8_t* q, int64_t q_stride, const float* qs, int transposed,
+                             int T, int H, int k, const int32_t* inv_rows, uint8_t* xq, float* sx,
+                             cudaStream_t s, int32_t* zero, int nzero) {
+  if (T <= 0) return;
+  const int64_t n = static_cast<int64_t>(T) * (H / 16);
+  launch_kernel(prequant_scatter_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+                q, q_stride, qs, transposed, T, H, k, inv_rows, xq, sx, zero, nzero);
+}
+
 void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half* xh, float* inv,
-                           cudaStream_t s, int32_t* zero, int nzero) {
+                           cudaStream_t s, int32_t* zero, int nzero, const void* gate,
+                           int64_t gate_stride, int mode) {
   if (T <= 0) return;
   launch_kernel(dense_act_prep_kernel, dim3(pair_blocks(T, K)), dim3(256), 0, s,
-                static_cast<const __nv_bfloat16*>(x), x_stride, T, K, xh, inv, zero, nzero);
+                static_cast<const __nv_bfloat16*>(x), x_stride, T, K, xh, inv, zero, nzero,
+                static_cast<const __nv_bfloat16*>(gate), gate_stride, gate ? mode : GATE_NONE);
 }
 
 void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,

@@ -191,12 +191,19 @@ int tc_grid(int R, int groups, int ntiles, int sms) {
   return static_cast<int>(tiles < sms ? tiles : sms);
 }
 
+// Row layout of w13 within an expert: [gate | up] (D3_GATE_UP, the checkpoint
+// order) or [up | gate] (D3_UP_GATE, FlashInfer's SwiGLU order).
+int gate_first_row(const d3_experts_t* e) { return e->gate_up_order == D3_UP_GATE ? e->I : 0; }
+int up_minus_gate(const d3_experts_t* e) { return e->gate_up_order == D3_UP_GATE ? -e->I : e->I; }
+
 int check_experts(const d3_experts_t* e, const char* what) {
   D3_REQUIRE(e != nullptr, "%s: expert weights missing", what);
   D3_REQUIRE(e->w13 && e->s13 && e->w2 && e->s2, "%s: null weight pointer", what);
   D3_REQUIRE(e->E > 0 && e->I > 0 && e->H > 0, "%s: bad expert shape", what);
   D3_REQUIRE(e->I % 128 == 0 && e->H % 128 == 0, "%s: H=%d and I=%d must be multiples of 128", what, e->H, e->I);
   D3_REQUIRE(aligned(e->w13, 16) && aligned(e->w2, 16), "%s: weights must be 16-byte aligned", what);
+  D3_REQUIRE(e->gate_up_order == D3_GATE_UP || e->gate_up_order == D3_UP_GATE,
+             "%s: gate_up_order must be D3_GATE_UP or D3_UP_GATE", what);
   return D3_OK;
 }
 
@@ -225,11 +232,20 @@ int finish_layer(const MoeBuffers& b, int H, const void* weights, int T, int k, 
   return check_launch("combine_rows");
 }
 
+// Already-quantised input of d3_moe_experts_fp8 (replaces the bf16 x).
+struct PreQuant {
+  const uint8_t* q = nullptr;
+  int64_t q_stride = 0;
+  const float* scales = nullptr;
+  int transposed = 0;
+};
+
 int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
                 int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
                 int64_t gate_stride, void* routed_out, void* shared_out, void* out,
                 const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted,
-                const AddNorm& an = AddNorm{}, const RowGather& rg = RowGather{}) {
+                const AddNorm& an = AddNorm{}, const RowGather& rg = RowGather{},
+                const PreQuant& pq = PreQuant{}) {
   const int E = ex->E, I = ex->I, H = ex->H;
   const int P = T * k;
   const int has_shared = sh ? 1 : 0;
@@ -242,7 +258,11 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
                         b.inv, b.active, b.n_active, s, b.permute_scratch);
     if (rc) return rc;
   }
-  launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2, rg);
+  if (pq.q)
+    launch_prequant_scatter(pq.q, pq.q_stride, pq.scales, pq.transposed, T, H, k, b.inv, b.xq, b.sx,
+                            s, b.work, 2);
+  else
+    launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2, rg);
   if ((rc = check_launch("quant_scatter"))) return rc;
 
   const int sms = sm_count();
@@ -268,7 +288,10 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
       a.ntiles = I / 128;
       a.KB = H / 128;
       a.rows_per_expert = 2 * I;
-      a.second_box = I;
+      a.first_off[0] = gate_first_row(ex);
+      a.first_off[1] = has_shared ? gate_first_row(sh) : 0;
+      a.second_box[0] = up_minus_gate(ex);
+      a.second_box[1] = has_shared ? up_minus_gate(sh) : I;
       a.nt_stride = 128;
       a.wscale = ex->s13;
       a.wscale_sh = has_shared ? sh->s13 : ex->s13;
@@ -287,7 +310,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
       a.ntiles = H / 256;
       a.KB = I / 128;
       a.rows_per_expert = H;
-      a.second_box = 128;
+      a.first_off[0] = a.first_off[1] = 0;
+      a.second_box[0] = a.second_box[1] = 128;
       a.nt_stride = 256;
       a.wscale = ex->s2;
       a.wscale_sh = has_shared ? sh->s2 : ex->s2;
@@ -330,7 +354,10 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.ksplit = 1;
     a.kb_per_split = a.KB;
     a.rows_per_expert = 2 * I;
-    a.up_offset = I;
+    a.first_off[0] = gate_first_row(ex);
+    a.first_off[1] = has_shared ? gate_first_row(sh) : 0;
+    a.up_offset[0] = up_minus_gate(ex);
+    a.up_offset[1] = has_shared ? up_minus_gate(sh) : I;
     a.wscale = ex->s13;
     a.wscale_sh = has_shared ? sh->s13 : ex->s13;
     a.act_scale = b.sx;
@@ -367,7 +394,6 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.ksplit = 1;
     a.kb_per_split = a.KB;
     a.rows_per_expert = H;
-    a.up_offset = 0;
     a.wscale = ex->s2;
     a.wscale_sh = has_shared ? sh->s2 : ex->s2;
     a.act_scale = b.sa;
@@ -451,6 +477,31 @@ extern "C" int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* id
   stage_mark(0, s);
   return run_experts(x, x_stride, ids, weights, T, k, experts, shared, nullptr, 0, routed_out,
                      shared_out, nullptr, b, status ? status : b.status, s, false);
+}
+
+extern "C" int d3_moe_experts_fp8(const uint8_t* q, int64_t q_stride, const float* q_scales,
+                                  int scales_transposed, const int64_t* ids, const void* weights,
+                                  int T, int k, const d3_experts_t* experts, void* routed_out,
+                                  void* workspace, size_t workspace_bytes, int32_t* status,
+                                  d3_stream_t stream) {
+  int rc = check_common(q, q_stride, T, k, experts, nullptr, workspace, workspace_bytes,
+                        "moe_experts_fp8");
+  if (rc) return rc;
+  D3_REQUIRE(q_stride % 16 == 0, "moe_experts_fp8: q row stride must be a multiple of 16 bytes");
+  D3_REQUIRE(q_scales && ids && weights && routed_out && aligned(routed_out, 16),
+             "moe_experts_fp8: null or misaligned scales / ids / weights / output");
+  if (T == 0) return D3_OK;
+  auto b = carve_moe(workspace, T, k, experts->E, experts->I, experts->H, 0, 1);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  PreQuant pq;
+  pq.q = q;
+  pq.q_stride = q_stride;
+  pq.scales = q_scales;
+  pq.transposed = scales_transposed ? 1 : 0;
+  stage_mark(0, s);
+  return run_experts(nullptr, 0, ids, weights, T, k, experts, nullptr, nullptr, 0, routed_out,
+                     nullptr, nullptr, b, status ? status : b.status, s, false, AddNorm{},
+                     RowGather{}, pq);
 }
 
 static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
@@ -588,9 +639,10 @@ extern "C" int d3_fp8_gemv_workspace_size(int T, int N, int K, size_t* bytes) {
   return D3_OK;
 }
 
-extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const float* s,
-                           int T, int N, int K, void* y, int64_t y_stride, void* workspace,
-                           size_t workspace_bytes, int32_t* status, d3_stream_t stream) {
+static int fp8_gemv_impl(const void* x, int64_t x_stride, const void* gate, int64_t gate_stride,
+                         int mode, const uint8_t* wq, const float* s, int T, int N, int K, void* y,
+                         int64_t y_stride, void* workspace, size_t workspace_bytes, int32_t* status,
+                         d3_stream_t stream) {
   D3_REQUIRE(T >= 0 && N > 0 && K > 0 && K % 128 == 0, "fp8_gemv: bad shape T=%d N=%d K=%d", T, N, K);
   D3_REQUIRE(x_stride >= K && x_stride % 8 == 0, "fp8_gemv: x row stride must be >= K and a multiple of 8");
   D3_REQUIRE(y_stride >= N, "fp8_gemv: y row stride must be >= N");
@@ -612,7 +664,8 @@ extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, c
   split = (KB + kbps - 1) / kbps;
   const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
   // the split-K tile counters are zeroed by the activation prep kernel
-  launch_dense_act_prep(x, x_stride, T, K, b.xh, b.inv, st, b.counters, split > 1 ? tiles * groups : 0);
+  launch_dense_act_prep(x, x_stride, T, K, b.xh, b.inv, st, b.counters, split > 1 ? tiles * groups : 0,
+                        gate, gate_stride, mode);
   int rc = check_launch("dense_act_prep");
   if (rc) return rc;
   CUtensorMap tw, ta;
@@ -638,6 +691,25 @@ extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, c
   const int items = tiles * split;
   const int grid = items < sms ? items : sms;
   return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
+}
+
+extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const float* s,
+                           int T, int N, int K, void* y, int64_t y_stride, void* workspace,
+                           size_t workspace_bytes, int32_t* status, d3_stream_t stream) {
+  return fp8_gemv_impl(x, x_stride, nullptr, 0, GATE_NONE, wq, s, T, N, K, y, y_stride, workspace,
+                       workspace_bytes, status, stream);
+}
+
+extern "C" int d3_fp8_gated_gemv(const void* x, int64_t x_stride, const void* gate,
+                                 int64_t gate_stride, int mode, const uint8_t* wq, const float* s,
+                                 int T, int N, int K, void* y, int64_t y_stride, void* workspace,
+                                 size_t workspace_bytes, int32_t* status, d3_stream_t stream) {
+  D3_REQUIRE(mode == D3_GATE_SWIGLU || mode == D3_GATE_SIGMOID,
+             "fp8_gated_gemv: mode must be D3_GATE_SWIGLU or D3_GATE_SIGMOID");
+  D3_REQUIRE(gate && aligned(gate, 16) && gate_stride >= K && gate_stride % 8 == 0,
+             "fp8_gated_gemv: null or misaligned gate, or gate row stride < K / not a multiple of 8");
+  return fp8_gemv_impl(x, x_stride, gate, gate_stride, mode == D3_GATE_SWIGLU ? GATE_SWIGLU : GATE_SIGMOID,
+                       wq, s, T, N, K, y, y_stride, workspace, workspace_bytes, status, stream);
 }
 
 // --------------------------------------------------------------------------

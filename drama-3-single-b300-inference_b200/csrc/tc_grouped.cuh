@@ -50,7 +50,10 @@ struct TcArgs {
   int ntiles;             // 256-column tiles per group (gate_up: I/128, down: H/256)
   int KB;                 // K / 128
   int rows_per_expert;    // weight rows per routed expert (2I or H)
-  int second_box;         // row offset of the second 128-row B box (gate_up: I, down: 128)
+  int first_off[2];       // row offset of the first 128-row B box in an expert [routed, shared]
+                          // (gate_up: where the gate half starts, 0 or I; down: 0)
+  int second_box[2];      // offset of the second B box from the first (gate_up: up - gate,
+                          // +I or -I; down: 128)
   int nt_stride;          // weight rows per n tile (gate_up: 128, down: 256)
   int act_rows;           // rows of the activation buffer (for scale loads)
   const float* wscale;    // routed weight scales [E, rows/128, KB]
@@ -127,7 +130,7 @@ __device__ __forceinline__ TcTile tc_tile(const TcArgs& a, const int* prefix, in
   }
   t.row0 = gstart + 128 * t.mt;
   t.mvalid = min(128, gcount - 128 * t.mt);
-  t.wrow = e * a.rows_per_expert + t.nt * a.nt_stride;
+  t.wrow = e * a.rows_per_expert + t.nt * a.nt_stride + a.first_off[t.shared];
   return t;
 }
 
@@ -251,7 +254,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               if (q == s) last_parity[q] = static_cast<int>(ph);
             tma_load_2d(st, &tm_act, kb * 128, t.row0, &full[s]);
             tma_load_2d(st + kTcABytes, wmap, kb * 128, t.wrow, &full[s]);
-            tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box, &full[s]);
+            tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box[t.shared], &full[s]);
           }
         }
         pdl_trigger();  // every load of this CTA is issued
@@ -349,7 +352,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto load_scales = [&](const TcTile& t, int kb, float& sa, float& w0, float& w1) {
       const float* wscale = t.shared ? args.wscale_sh : args.wscale;
       const int sb0 = KIND == TC_GATE_UP ? t.wrow / 128 : (t.wrow + 128 * wg) / 128;
-      const int sb1 = KIND == TC_GATE_UP ? (t.wrow + args.second_box) / 128 : sb0;
+      const int sb1 = KIND == TC_GATE_UP ? (t.wrow + args.second_box[t.shared]) / 128 : sb0;
       const int grow = t.row0 + row;
       sa = grow < args.act_rows ? __ldg(args.act_scale + static_cast<int64_t>(grow) * KB + kb) : 0.f;
       w0 = __ldg(wscale + sb0 * KB + kb);

@@ -22,6 +22,11 @@ D3_DTYPE_BF16 = 0
 D3_DTYPE_F32 = 1
 D3_STATUS_OK = 0
 D3_STATUS_WAIT_TIMEOUT = 1
+D3_STATUS_BAD_ROW = 2
+D3_GATE_UP = 0
+D3_UP_GATE = 1
+D3_GATE_SWIGLU = 1
+D3_GATE_SIGMOID = 2
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int
@@ -40,6 +45,7 @@ class D3Experts(ctypes.Structure):
         ("E", _i32),
         ("I", _i32),
         ("H", _i32),
+        ("gate_up_order", _i32),
     ]
 
 
@@ -126,6 +132,16 @@ SIGNATURES: dict[str, tuple] = {
     "d3_combine_pairs": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p],
+    ),
+    "d3_fp8_gated_gemv": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p,
+         _i64, _c_void_p, _size_t, _c_void_p, _c_void_p],
+    ),
+    "d3_moe_experts_fp8": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i32,
+         ctypes.POINTER(D3Experts), _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
     "d3_moe_layer": (
         _i32,

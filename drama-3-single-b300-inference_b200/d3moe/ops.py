@@ -46,11 +46,18 @@ class ExpertView:
     `experts` is any object exposing w13_weight [E,2I,H] e4m3, w13_scale_inv
     [E,2I/128,H/128] f32, w2_weight [E,H,I] e4m3 and w2_scale_inv
     [E,H/128,I/128] f32 (the reference's container, src/drama3/kernels.py:
-    336-350)."""
+    336-350). gate_up_order: "gate_up" (w13 rows [gate | up], the checkpoint
+    order) or "up_gate" ([up | gate], FlashInfer's order, model.py:196-201). `tensors`
+    = (w13, s13, w2, s2) replaces the container."""
 
-    def __init__(self, experts):
-        w13, s13 = experts.w13_weight, experts.w13_scale_inv
-        w2, s2 = experts.w2_weight, experts.w2_scale_inv
+    def __init__(self, experts=None, gate_up_order: str = "gate_up", *, tensors=None):
+        if tensors is not None:
+            w13, s13, w2, s2 = tensors
+        else:
+            w13, s13 = experts.w13_weight, experts.w13_scale_inv
+            w2, s2 = experts.w2_weight, experts.w2_scale_inv
+        if gate_up_order not in ("gate_up", "up_gate"):
+            raise ValueError("gate_up_order must be 'gate_up' or 'up_gate'")
         if w13.dim() == 2:  # a single (shared) expert stored without the E axis
             w13, s13, w2, s2 = w13[None], s13[None], w2[None], s2[None]
         E, I2, H = w13.shape
@@ -69,7 +76,9 @@ class ExpertView:
         _require_cuda(w13, s13, w2, s2)
         self.tensors = (w13, s13, w2, s2)
         self.E, self.I, self.H = E, I, H
-        self.struct = D3Experts(w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(), E, I, H)
+        self.gate_up_order = gate_up_order
+        self.struct = D3Experts(w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(), E, I, H,
+                                _lib.D3_UP_GATE if gate_up_order == "up_gate" else _lib.D3_GATE_UP)
 
 
 def quant_act_fp8(x: torch.Tensor, transposed: bool = False):
@@ -293,6 +302,33 @@ def fp8_gemv(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, n: int | N
     return out
 
 
+def fp8_gated_gemv(x: torch.Tensor, gate: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
+                   mode: str, n: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y bf16 [T,N] = bf16(x * bf16(act(gate))) . dequant(wq, scales)^T with
+    act = silu (mode "swiglu") or sigmoid (mode "sigmoid")."""
+    _require_cuda(x, gate, wq, scales)
+    if x.dtype != torch.bfloat16 or gate.dtype != torch.bfloat16:
+        raise ValueError("x and gate must be bfloat16")
+    if mode not in ("swiglu", "sigmoid"):
+        raise ValueError("Expected swiglu or sigmoid")
+    T, K = x.shape
+    if tuple(gate.shape) != (T, K):
+        raise ValueError("gate must have the shape of x")
+    N = wq.shape[0] if n is None else n
+    if wq.shape[1] != K or not wq.is_contiguous() or wq.dtype != FP8:
+        raise ValueError("wq must be contiguous float8_e4m3fn [>=N, K]")
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
+    nbytes = ctypes.c_size_t()
+    call("d3_fp8_gemv_workspace_size", T, N, K, ctypes.byref(nbytes))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+    call("d3_fp8_gated_gemv", x.data_ptr(), _row_stride(x), gate.data_ptr(), _row_stride(gate),
+         _lib.D3_GATE_SWIGLU if mode == "swiglu" else _lib.D3_GATE_SIGMOID, wq.data_ptr(),
+         scales.data_ptr(), T, N, K, out.data_ptr(), out.stride(0), ws.data_ptr(), nbytes.value, None,
+         _stream(x.device))
+    return out
+
+
 def set_prefill_min_tokens(t: int) -> int:
     """Token count from which the expert GEMMs run on the tcgen05 prefill
     kernel (t <= 0 restores the default); returns the previous value."""
@@ -347,6 +383,36 @@ def moe_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
          routed.data_ptr(), _ptr(shared_out), workspace.data_ptr(), workspace.numel(),
          _ptr(status), _stream(x.device))
     return routed, shared_out
+
+
+def moe_experts_fp8(q: torch.Tensor, scales: torch.Tensor, topk_ids: torch.Tensor,
+                    topk_weights: torch.Tensor, experts, transposed: bool = True,
+                    workspace: torch.Tensor | None = None, status: torch.Tensor | None = None):
+    """Routed expert output bf16 [T,H] for already-quantised activations q e4m3
+    [T,H] with group scales f32 [H/128,T] (transposed, FlashInfer's layout) or
+    [T,H/128]. ids outside [0,E) contribute nothing."""
+    _require_cuda(q, scales, topk_ids, topk_weights)
+    if q.dtype != FP8 or q.dim() != 2 or q.stride(1) != 1:
+        raise ValueError("hidden states must be float8_e4m3fn [T, H] with contiguous channels")
+    if scales.dtype != torch.float32 or not scales.is_contiguous():
+        raise ValueError("hidden-state scales must be contiguous float32")
+    ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
+    T, H = q.shape
+    if H != ev.H:
+        raise ValueError(f"hidden size {H} != expert H {ev.H}")
+    if tuple(scales.shape) != ((H // 128, T) if transposed else (T, H // 128)):
+        raise ValueError(f"hidden-state scales shape {tuple(scales.shape)} does not match T={T}, H={H}")
+    if topk_ids.dtype != torch.int64 or not topk_ids.is_contiguous() or topk_ids.shape[0] != T:
+        raise ValueError("topk_ids must be contiguous int64 [T, k]")
+    k = topk_ids.shape[1]
+    topk_weights = topk_weights.to(torch.bfloat16).contiguous()
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=q.device)
+    if workspace is None:
+        workspace = moe_workspace(T, k, ev.E, ev.I, ev.H, False, q.device)
+    call("d3_moe_experts_fp8", q.data_ptr(), q.stride(0), scales.data_ptr(), int(transposed),
+         topk_ids.data_ptr(), topk_weights.data_ptr(), T, k, ctypes.byref(ev.struct), out.data_ptr(),
+         workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(q.device))
+    return out
 
 
 def _row_map(t, name, device):

@@ -197,6 +197,18 @@ D3_API int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const
                 int K, void* y, int64_t y_stride, void* workspace, size_t workspace_bytes,
                 int32_t* status, d3_stream_t stream);
 
+/* Gated projection (replaces gated_gemv, src/drama3/fused_projection.py:9-60,
+ * with FP8 weights): x is first replaced by bf16(x * a), a = bf16(silu(gate))
+ * (D3_GATE_SWIGLU) or bf16(sigmoid(gate)) (D3_GATE_SIGMOID), gate bf16 [T,K]
+ * with row stride gate_stride; then y = d3_fp8_gemv of that. Any T (the
+ * reference takes one row). Workspace: d3_fp8_gemv_workspace_size. */
+#define D3_GATE_SWIGLU 1
+#define D3_GATE_SIGMOID 2
+D3_API int d3_fp8_gated_gemv(const void* x, int64_t x_stride, const void* gate, int64_t gate_stride,
+                             int mode, const uint8_t* wq, const float* s, int T, int N, int K, void* y,
+                             int64_t y_stride, void* workspace, size_t workspace_bytes,
+                             int32_t* status, d3_stream_t stream);
+
 /* The same weight-only FP8 GEMV for callers that cannot allocate device
  * memory, and so cannot pass a workspace: for example a host runtime that
  * hands a plugin only its inputs, outputs and a stream and does not let it
@@ -228,7 +240,13 @@ typedef struct d3_experts {
   int E;
   int I;
   int H;
+  int gate_up_order; /* D3_GATE_UP (0): w13 rows [gate | up], the checkpoint order;
+                        D3_UP_GATE (1): [up | gate], FlashInfer's SwiGLU order
+                        (src/drama3/model.py:196-201); s13 row blocks follow w13 */
 } d3_experts_t;
+
+#define D3_GATE_UP 0
+#define D3_UP_GATE 1
 
 /* Workspace for d3_moe_experts / d3_moe_layer at T tokens, top-k. */
 D3_API int d3_moe_workspace_size(int T, int k, int E, int I, int H, int has_shared, size_t* bytes);
@@ -246,6 +264,18 @@ D3_API int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* ids, c
                    int T, int k, const d3_experts_t* experts, const d3_experts_t* shared,
                    void* routed_out, void* shared_out, void* workspace, size_t workspace_bytes,
                    int32_t* status, d3_stream_t stream);
+
+/* Routed experts over already-quantised activations, the calling convention
+ * of FlashInfer's trtllm_fp8_block_scale_moe (src/drama3/model.py:544-580):
+ * q e4m3 [T,H] (row stride q_stride bytes, a multiple of 16), q_scales f32
+ * [H/128, T] (scales_transposed = 1, the layout prepare_moe_input writes) or
+ * [T, H/128]. ids int64 [T,k] (ids outside [0,E) contribute nothing), weights
+ * bf16 [T,k]; routed_out bf16 [T,H] as d3_moe_experts. experts may use either
+ * gate_up_order. Workspace: d3_moe_workspace_size(T, k, E, I, H, 0). */
+D3_API int d3_moe_experts_fp8(const uint8_t* q, int64_t q_stride, const float* q_scales,
+                              int scales_transposed, const int64_t* ids, const void* weights, int T,
+                              int k, const d3_experts_t* experts, void* routed_out, void* workspace,
+                              size_t workspace_bytes, int32_t* status, d3_stream_t stream);
 
 /* One whole MoE layer: router projection over [E+1, H] bf16 (rows 0..E-1 the
  * router, row E the shared-expert gate; src/drama3/model.py:236-245), top-k

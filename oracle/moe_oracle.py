@@ -302,16 +302,18 @@ def expert_down_rows(a, sa, w2, s2, ids):
     return out
 
 
-def expert_down_combine(a, sa, w2, s2, ids, weights):
+def expert_down_combine(a, sa, w2, s2, ids, weights, skip=None):
     """src/drama3/kernels.py:304-322: y[t] = bf16(sum_r w[t,r] * down_r) with
-    fp32 accumulation (rank order r = 0..k-1)."""
+    fp32 accumulation (rank order r = 0..k-1); pairs marked in `skip` [T,k]
+    are left out of the sum."""
     ids = np.asarray(ids, dtype=np.int64)
     T, k = ids.shape
     d = expert_down_rows(a, sa, w2, s2, ids).reshape(T, k, -1)
     w = np.asarray(weights, dtype=np.float32)
     acc = np.zeros((T, d.shape[2]), dtype=np.float32)
     for r in range(k):
-        acc = (acc + d[:, r] * w[:, r: r + 1]).astype(np.float32)
+        term = (acc + d[:, r] * w[:, r: r + 1]).astype(np.float32)
+        acc = term if skip is None else np.where(skip[:, r: r + 1], acc, term)
     return bf16_round(acc)
 
 
@@ -367,6 +369,16 @@ def combine_experts_add_norm(routed, shared, gate, residual, weight, eps, invers
     return _rms_scale(value, weight, eps), value
 
 
+def gated_input(x, gate, mode):
+    """src/drama3/fused_projection.py:22-29: a = bf16(silu(g)) ("swiglu") or
+    bf16(sigmoid(g)) ("sigmoid"), sigmoid(g) = 1 / (1 + exp(-g)) in fp32;
+    returns bf16(x * a), the input the projection multiplies."""
+    g = np.asarray(gate, dtype=np.float32)
+    sg = (F32(1.0) / (F32(1.0) + np.exp(-g))).astype(np.float32)
+    a = bf16_round((g * sg).astype(np.float32) if mode == "swiglu" else sg)
+    return bf16_round((np.asarray(x, np.float32) * a).astype(np.float32))
+
+
 def fp8_gemv(x, wq, scales, n=None):
     """src/drama3/experimental_fp8.py:21-29 (_gemv): y = sum_k w*scale*x with
     bf16 activations (no activation quantisation), stored bf16. The sum is
@@ -410,6 +422,22 @@ def moe_experts(x, ids, weights, ex: Experts, shared: Experts | None = None):
         a2, sa2 = silu_mul_quant(gus)
         sh = bf16_round(expert_down_rows(a2, sa2, shared.w2, shared.s2, sid))
     return routed, sh
+
+
+def moe_experts_q(q, sx, ids, weights, ex: Experts):
+    """Routed experts over already-quantised activations (q e4m3 bytes [T,H],
+    sx f32 [T,H/128]): the expert arithmetic of moe_experts after its input
+    quantisation, the operands FlashInfer's trtllm_fp8_block_scale_moe gets
+    (src/drama3/model.py:544-580). Pairs whose id is outside [0, E) contribute
+    nothing. Returns routed bf16 [T,H]."""
+    ids = np.asarray(ids, dtype=np.int64)
+    E = len(ex.w13)
+    valid = (ids >= 0) & (ids < E)
+    w = np.where(valid, np.asarray(weights, np.float32), F32(0.0)).astype(np.float32)
+    safe = np.where(valid, ids, 0)
+    gu = expert_gate_up(np.asarray(q), np.asarray(sx, np.float32), ex.w13, ex.s13, safe)
+    a, sa = silu_mul_quant(gu)
+    return expert_down_combine(a, sa, ex.w2, ex.s2, safe, w, skip=~valid)
 
 
 def moe_layer(x, router_w, ex: Experts, shared: Experts, k: int = 8, bias=None):

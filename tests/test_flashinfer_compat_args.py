@@ -1,0 +1,57 @@
+"""Host-side argument contract of the FlashInfer-compatible entry: arguments
+outside what the reference passes (src/drama3/model.py:556-580) raise before any
+device work instead of running a different algorithm."""
+
+from __future__ import annotations
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from d3moe.flashinfer_compat import RoutingMethodType, WeightLayout, trtllm_fp8_block_scale_moe  # noqa: E402
+
+E, I, H, T = 8, 128, 256, 4
+
+
+def args(**over):
+    a = dict(
+        routing_logits=torch.zeros(T, E), routing_bias=None,
+        hidden_states=torch.zeros(T, H, dtype=torch.float8_e4m3fn),
+        hidden_states_scale=torch.ones(H // 128, T),
+        gemm1_weights=torch.zeros(E, 2 * I, H, dtype=torch.float8_e4m3fn),
+        gemm1_weights_scale=torch.ones(E, 2 * I // 128, H // 128),
+        gemm2_weights=torch.zeros(E, H, I, dtype=torch.float8_e4m3fn),
+        gemm2_weights_scale=torch.ones(E, H // 128, I // 128),
+        num_experts=E, top_k=2, n_group=None, topk_group=None, intermediate_size=I,
+        local_expert_offset=0, local_num_experts=E, routed_scaling_factor=1.0,
+        routing_method_type=RoutingMethodType.RenormalizeNaive, use_shuffled_weight=False,
+        weight_layout=WeightLayout.MajorK)
+    a.update(over)
+    return a
+
+
+@pytest.mark.parametrize("over", [
+    dict(routing_method_type=RoutingMethodType.DeepSeekV3),
+    dict(routing_method_type=RoutingMethodType.Renormalize),
+    dict(n_group=4, topk_group=2),
+    dict(use_shuffled_weight=True),
+    dict(weight_layout=WeightLayout.BlockMajorK),
+    dict(routed_scaling_factor=2.5),
+    dict(do_finalize=False),
+    dict(activation_type=4),
+])
+def test_unsupported_arguments_raise(over):
+    with pytest.raises(NotImplementedError):
+        trtllm_fp8_block_scale_moe(**args(**over))
+
+
+@pytest.mark.parametrize("over", [
+    dict(num_experts=16),
+    dict(intermediate_size=256),
+    dict(local_num_experts=4),
+    dict(local_expert_offset=1),
+    dict(hidden_states=torch.zeros(T + 1, H, dtype=torch.float8_e4m3fn)),
+])
+def test_inconsistent_shapes_raise(over):
+    with pytest.raises(ValueError):
+        trtllm_fp8_block_scale_moe(**args(**over))

@@ -187,7 +187,11 @@ def test_dense_fp8_golden(d3, golden):
 
 
 @pytest.mark.parametrize("T", [1, 8, 16, 32, 64, 100])
-@pytest.mark.parametrize("N,K", [(4096, 2048), (2048, 2048), (300, 384)])
+# the benchmark's QKV and o_proj, an odd size, and the reference model's real
+# projections: QKV 9216x2048, GDN in 12352x2048, out / o_proj 2048x4096
+# (src/drama3/model.py:210-225)
+@pytest.mark.parametrize("N,K", [(4096, 2048), (2048, 2048), (300, 384), (9216, 2048), (12352, 2048),
+                                 (2048, 4096)])
 def test_dense_fp8_gemv_matches_oracle(d3, T, N, K):
     rng = np.random.default_rng(T * 7 + N)
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
