@@ -75,8 +75,8 @@ struct EngineArgs {
   int tiles;                // 128-row weight tiles per group
   int KB;                   // K / 128
   int rows_per_expert;      // weight rows per routed expert in the map (2I or H)
-  int first_off[2];         // row offset of the gate half (EPI_GATE_UP: 0 or I) [routed, shared]
-  int up_offset[2];         // EPI_GATE_UP: up-half rows relative to the gate half (+I or -I)
+  int first_off;            // row offset of the gate half (EPI_GATE_UP: 0 or I)
+  int up_offset;            // EPI_GATE_UP: up-half rows relative to the gate half (+I or -I)
   const float* wscale;      // routed weight scales [E, rows/128, KB]
   const float* wscale_sh;   // shared weight scales [rows/128, KB]
   const float* act_scale;   // [rows, KB]: fp8 act scales, or 2^-s for EPI_DENSE
@@ -145,8 +145,8 @@ __device__ __forceinline__ WorkItem engine_item(const EngineArgs& a, const int* 
     w.row0 = a.starts ? sm_starts[e] : 0;
     w.m = a.counts ? sm_counts[e] : a.dense_count;
   }
-  w.wrow = e * a.rows_per_expert + w.tile * 128 + a.first_off[w.shared];
-  w.wrow_up = w.wrow + a.up_offset[w.shared];
+  w.wrow = e * a.rows_per_expert + w.tile * 128 + a.first_off;
+  w.wrow_up = w.wrow + a.up_offset;
   return w;
 }
 

@@ -109,6 +109,9 @@ int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUt
   constexpr int kGroup = NCH * 8 < kTokensPerGroup ? NCH * 8 : kTokensPerGroup;
   constexpr int kActRows = kGroup < 16 ? 16 : kGroup;
   const size_t smem = EngineSmem<EPI, ACT_F16, STAGES, kActRows>::bytes(args.KB, args.num_experts);
+  if (smem > 227 * 1024)
+    return set_error(D3_EUNSUPPORTED, "engine: %zu bytes of shared memory needed (K=%d too large)",
+                     smem, args.KB * 128);
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -288,17 +291,16 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
       a.ntiles = I / 128;
       a.KB = H / 128;
       a.rows_per_expert = 2 * I;
-      a.first_off[0] = gate_first_row(ex);
-      a.first_off[1] = has_shared ? gate_first_row(sh) : 0;
-      a.second_box[0] = up_minus_gate(ex);
-      a.second_box[1] = has_shared ? up_minus_gate(sh) : I;
+      a.second_box = up_minus_gate(ex);  // the gate half's offset is I (TC_UP_GATE)
       a.nt_stride = 128;
       a.wscale = ex->s13;
       a.wscale_sh = has_shared ? sh->s13 : ex->s13;
       a.act_scale = b.sx;
       a.out_q = b.a;
       a.out_qs = b.sa;
-      rc = launch_tc<TC_GATE_UP>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s);
+      rc = ex->gate_up_order == D3_UP_GATE
+               ? launch_tc<TC_UP_GATE>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s)
+               : launch_tc<TC_GATE_UP>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s);
       if (rc) return rc;
     }
     stage_mark(2, s);
@@ -310,8 +312,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
       a.ntiles = H / 256;
       a.KB = I / 128;
       a.rows_per_expert = H;
-      a.first_off[0] = a.first_off[1] = 0;
-      a.second_box[0] = a.second_box[1] = 128;
+      a.second_box = 128;
       a.nt_stride = 256;
       a.wscale = ex->s2;
       a.wscale_sh = has_shared ? sh->s2 : ex->s2;
@@ -354,10 +355,8 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.ksplit = 1;
     a.kb_per_split = a.KB;
     a.rows_per_expert = 2 * I;
-    a.first_off[0] = gate_first_row(ex);
-    a.first_off[1] = has_shared ? gate_first_row(sh) : 0;
-    a.up_offset[0] = up_minus_gate(ex);
-    a.up_offset[1] = has_shared ? up_minus_gate(sh) : I;
+    a.first_off = gate_first_row(ex);
+    a.up_offset = up_minus_gate(ex);
     a.wscale = ex->s13;
     a.wscale_sh = has_shared ? sh->s13 : ex->s13;
     a.act_scale = b.sx;
@@ -447,6 +446,8 @@ static int check_common(const void* x, int64_t x_stride, int T, int k, const d3_
     if ((rc = check_experts(sh, what))) return rc;
     D3_REQUIRE(sh->E == 1 && sh->I == ex->I && sh->H == ex->H,
                "%s: the shared expert must have E=1 and the routed I/H", what);
+    D3_REQUIRE(sh->gate_up_order == ex->gate_up_order,
+               "%s: routed and shared experts must use the same gate_up_order", what);
   }
   D3_REQUIRE(T >= 0 && k > 0 && k <= 32 && k <= ex->E, "%s: bad top-k %d", what, k);
   D3_REQUIRE(ex->E <= 1024, "%s: E=%d above 1024", what, ex->E);

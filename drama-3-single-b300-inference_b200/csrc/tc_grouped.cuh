@@ -38,7 +38,9 @@
 
 namespace d3 {
 
-enum TcKind { TC_GATE_UP = 0, TC_DOWN = 1 };
+// TC_UP_GATE is gate_up over w13 rows stored [up | gate] (the gate half
+// starts I rows into each expert); TC_GATE_UP reads [gate | up].
+enum TcKind { TC_GATE_UP = 0, TC_DOWN = 1, TC_UP_GATE = 2 };
 
 struct TcArgs {
   const int32_t* counts;  // [E] tokens per routed expert
@@ -50,9 +52,7 @@ struct TcArgs {
   int ntiles;             // 256-column tiles per group (gate_up: I/128, down: H/256)
   int KB;                 // K / 128
   int rows_per_expert;    // weight rows per routed expert (2I or H)
-  int first_off[2];       // row offset of the first 128-row B box in an expert [routed, shared]
-                          // (gate_up: where the gate half starts, 0 or I; down: 0)
-  int second_box[2];      // offset of the second B box from the first (gate_up: up - gate,
+  int second_box;         // offset of the second B box from the first (gate_up: up - gate,
                           // +I or -I; down: 128)
   int nt_stride;          // weight rows per n tile (gate_up: 128, down: 256)
   int act_rows;           // rows of the activation buffer (for scale loads)
@@ -79,7 +79,7 @@ constexpr int kTcMaxGroups = 1025;
 
 template <int KIND>
 struct TcSmem {
-  static constexpr int kStages = KIND == TC_GATE_UP ? 3 : 4;
+  static constexpr int kStages = KIND != TC_DOWN ? 3 : 4;
   static constexpr int kRing = kStages * kTcStageBytes;
   // full[S], empty[S], tfull[2], tempty[2], hfull, hempty
   static constexpr int kBars = kRing;
@@ -89,7 +89,7 @@ struct TcSmem {
   // gate_up: handoff tile [128 rows][32 chunks of 4 fp32] + row amax [2][128]
   // down:    staging tiles [8 warps][32 rows][4 chunks of 4 floats]
   static constexpr int kAux = (kPrefix + (kTcMaxGroups + 1) * 4 + 1023) / 1024 * 1024;
-  static constexpr int kAuxBytes = KIND == TC_GATE_UP ? 128 * 128 * 4 + 2 * 128 * 4 : 8 * 32 * 16 * 4;
+  static constexpr int kAuxBytes = KIND != TC_DOWN ? 128 * 128 * 4 + 2 * 128 * 4 : 8 * 32 * 16 * 4;
   static constexpr size_t bytes() { return 1024 + kAux + kAuxBytes; }
 };
 static_assert(TcSmem<TC_GATE_UP>::bytes() <= 227 * 1024, "gate_up shared memory");
@@ -130,7 +130,15 @@ __device__ __forceinline__ TcTile tc_tile(const TcArgs& a, const int* prefix, in
   }
   t.row0 = gstart + 128 * t.mt;
   t.mvalid = min(128, gcount - 128 * t.mt);
-  t.wrow = e * a.rows_per_expert + t.nt * a.nt_stride + a.first_off[t.shared];
+  t.wrow = e * a.rows_per_expert + t.nt * a.nt_stride;
+  return t;
+}
+
+// TC_UP_GATE tiles start their first (gate) box I rows into the expert.
+template <int KIND>
+__device__ __forceinline__ TcTile tc_tile_k(const TcArgs& a, const int* prefix, int ngroups, int i) {
+  TcTile t = tc_tile(a, prefix, ngroups, i);
+  if constexpr (KIND == TC_UP_GATE) t.wrow += a.I;
   return t;
 }
 
@@ -238,7 +246,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int s = 0; s < S; ++s) last_parity[s] = -1;
         bool ok = true;
         for (int i = blockIdx.x; i < total_tiles && ok; i += gridDim.x) {
-          const TcTile t = tc_tile(args, prefix, ngroups, i);
+          const TcTile t = tc_tile_k<KIND>(args, prefix, ngroups, i);
           const CUtensorMap* wmap = t.shared ? &tm_w_sh : &tm_w;
           for (int kb = 0; kb < args.KB; ++kb, ++it) {
             const int s = it % S;
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               if (q == s) last_parity[q] = static_cast<int>(ph);
             tma_load_2d(st, &tm_act, kb * 128, t.row0, &full[s]);
             tma_load_2d(st + kTcABytes, wmap, kb * 128, t.wrow, &full[s]);
-            tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box[t.shared], &full[s]);
+            tma_load_2d(st + kTcABytes + 16384, wmap, kb * 128, t.wrow + args.second_box, &full[s]);
           }
         }
         pdl_trigger();  // every load of this CTA is issued
@@ -295,7 +303,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (last_tfull[0] >= 0) mbar_wait(&tfull[0], static_cast<uint32_t>(last_tfull[0]));
         if (last_tfull[1] >= 0) mbar_wait(&tfull[1], static_cast<uint32_t>(last_tfull[1]));
       }
-    } else if constexpr (KIND == TC_GATE_UP) {
+    } else if constexpr (KIND != TC_DOWN) {
       // ------------------------------------------------------- activation --
       // Thread t (0..63) of the two activation warps owns rows t and t + 64 of
       // each handed-over tile: scale = max(row amax halves) / 448, then the
@@ -305,7 +313,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const float* hamax = reinterpret_cast<const float*>(aux + 128 * 128 * 4);
       uint32_t n = 0;
       for (int i = blockIdx.x; i < total_tiles; i += gridDim.x, ++n) {
-        const TcTile t = tc_tile(args, prefix, ngroups, i);
+        const TcTile t = tc_tile_k<KIND>(args, prefix, ngroups, i);
         tc_wait(hfull, n & 1, abort_flag, args.status);
         __syncwarp();
 #pragma unroll 1
@@ -346,13 +354,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int KB = args.KB;
     // columns of this thread: gate_up -> [64wg, 64wg+64) gate and [128+64wg, ...) up;
     // down -> [128wg, 128wg+128) as two runs of 64
-    const uint32_t c0 = KIND == TC_GATE_UP ? 64 * wg : 128 * wg;
-    const uint32_t c1 = KIND == TC_GATE_UP ? 128 + 64 * wg : 128 * wg + 64;
+    const uint32_t c0 = KIND != TC_DOWN ? 64 * wg : 128 * wg;
+    const uint32_t c1 = KIND != TC_DOWN ? 128 + 64 * wg : 128 * wg + 64;
     // scale of (row, kb) and the two weight blocks of this thread's columns
     auto load_scales = [&](const TcTile& t, int kb, float& sa, float& w0, float& w1) {
       const float* wscale = t.shared ? args.wscale_sh : args.wscale;
-      const int sb0 = KIND == TC_GATE_UP ? t.wrow / 128 : (t.wrow + 128 * wg) / 128;
-      const int sb1 = KIND == TC_GATE_UP ? (t.wrow + args.second_box[t.shared]) / 128 : sb0;
+      const int sb0 = KIND != TC_DOWN ? t.wrow / 128 : (t.wrow + 128 * wg) / 128;
+      const int sb1 = KIND != TC_DOWN ? (t.wrow + args.second_box) / 128 : sb0;
       const int grow = t.row0 + row;
       sa = grow < args.act_rows ? __ldg(args.act_scale + static_cast<int64_t>(grow) * KB + kb) : 0.f;
       w0 = __ldg(wscale + sb0 * KB + kb);
@@ -363,13 +371,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     TcTile t{};
     float p_sa = 0.f, p_w0 = 0.f, p_w1 = 0.f;
     if (i < total_tiles) {
-      t = tc_tile(args, prefix, ngroups, i);
+      t = tc_tile_k<KIND>(args, prefix, ngroups, i);
       load_scales(t, 0, p_sa, p_w0, p_w1);
     }
     for (; i < total_tiles; i += gridDim.x, ++n) {
       const int inext = i + gridDim.x;
       TcTile tn{};
-      if (inext < total_tiles) tn = tc_tile(args, prefix, ngroups, inext);
+      if (inext < total_tiles) tn = tc_tile_k<KIND>(args, prefix, ngroups, inext);
       float acc0[64], acc1[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc0[j] = acc1[j] = 0.f;
@@ -407,7 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
       // ------------------------------------------------------ tile epilogue --
-      if constexpr (KIND == TC_GATE_UP) {
+      if constexpr (KIND != TC_DOWN) {
         // a = bf16(silu(g)) * u with g, u the bf16-rounded gate and up and
         // silu(g) = g / (1 + exp(-g)) on the fast exponential and divide; a goes
         // to the activation warps as fp32 (16-byte chunk c of row r at chunk
