@@ -40,7 +40,14 @@
 
 namespace d3 {
 
-enum EpilogueKind { EPI_GATE_UP = 0, EPI_DOWN = 1, EPI_DENSE = 2 };
+// EPI_DOWN2: down over pairs of 128-row weight tiles (256 output columns per
+// work item, two accumulator sets like gate/up), so an item streams twice the
+// weight bytes of EPI_DOWN for the same per-item overhead.
+enum EpilogueKind { EPI_GATE_UP = 0, EPI_DOWN = 1, EPI_DENSE = 2, EPI_DOWN2 = 3 };
+
+// Two 128-row weight boxes (and two accumulator sets) per stage.
+template <int EPI>
+constexpr bool kTwoBoxes = EPI == EPI_GATE_UP || EPI == EPI_DOWN2;
 
 constexpr int kEngineConsumerWarps = 8;
 constexpr int kEngineConsumerThreads = kEngineConsumerWarps * 32;
@@ -121,6 +128,7 @@ struct GroupHeader {
 };
 static_assert(sizeof(GroupHeader) == 64, "slab header is 16 words");
 
+template <int EPI>
 __device__ __forceinline__ WorkItem engine_item(const EngineArgs& a, const int* sm_active,
                                                 const int* sm_counts, const int* sm_starts,
                                                 int i) {
@@ -145,15 +153,16 @@ __device__ __forceinline__ WorkItem engine_item(const EngineArgs& a, const int* 
     w.row0 = a.starts ? sm_starts[e] : 0;
     w.m = a.counts ? sm_counts[e] : a.dense_count;
   }
-  w.wrow = e * a.rows_per_expert + w.tile * 128 + a.first_off;
-  w.wrow_up = w.wrow + a.up_offset;
+  // EPI_DOWN2 tiles are 256 rows: rows [256 tile, +128) and [+128, +256)
+  w.wrow = e * a.rows_per_expert + w.tile * (EPI == EPI_DOWN2 ? 256 : 128) + a.first_off;
+  w.wrow_up = w.wrow + (EPI == EPI_DOWN2 ? 128 : a.up_offset);
   return w;
 }
 
 // ACT_ROWS: activation rows per stage = tokens per group rounded up to 16.
 template <int EPI, bool ACT_F16, int STAGES, int ACT_ROWS>
 struct EngineSmem {
-  static constexpr int kWBytes = (EPI == EPI_GATE_UP ? 2 : 1) * 128 * 128;
+  static constexpr int kWBytes = (kTwoBoxes<EPI> ? 2 : 1) * 128 * 128;
   static constexpr int kActHalf = ACT_ROWS * 128;  // one 128-byte column block of act rows
   static constexpr int kActBytes = (ACT_F16 ? 2 : 1) * kActHalf;
   static constexpr int kStageBytes = kWBytes + kActBytes;
@@ -200,7 +209,7 @@ template <int EPI, bool ACT_F16, int STAGES, int ACT_ROWS, int NC>
 __device__ __forceinline__ void consume_group(const EngineArgs& args, const ConsumerCtx& cx,
                                               const GroupHeader& w, uint32_t& it) {
   using L = EngineSmem<EPI, ACT_F16, STAGES, ACT_ROWS>;
-  constexpr int NACC = (EPI == EPI_GATE_UP) ? 2 : 1;
+  constexpr int NACC = kTwoBoxes<EPI> ? 2 : 1;
   const int warp = cx.warp, lane = cx.lane;
   const int g = lane >> 2, tq = lane & 3;
   const int KB = args.KB;
@@ -283,7 +292,7 @@ __device__ __forceinline__ void consume_group(const EngineArgs& args, const Cons
     if (lane == 0) mbar_arrive(&cx.empty[s]);
     // block-scale promotion
     const float ws_g = cx.wsl[kb];
-    const float ws_u = (EPI == EPI_GATE_UP) ? cx.wsl[KB + kb] : 0.f;
+    const float ws_u = kTwoBoxes<EPI> ? cx.wsl[KB + kb] : 0.f;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int t0 = c * 8 + 2 * tq;
@@ -348,7 +357,9 @@ __device__ __forceinline__ void consume_group(const EngineArgs& args, const Cons
       }
     }
     named_bar_sync(1, kEngineConsumerThreads);  // amax_sm is reused by the next group
-  } else if constexpr (EPI == EPI_DOWN) {
+  } else if constexpr (EPI == EPI_DOWN || EPI == EPI_DOWN2) {
+    // EPI_DOWN2: the item's columns start at 256 * tile; set h adds 128
+    const int cbase = EPI == EPI_DOWN2 ? w.tile * 256 + 16 * warp + g : col0;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
 #pragma unroll
@@ -356,8 +367,11 @@ __device__ __forceinline__ void consume_group(const EngineArgs& args, const Cons
         const int t = c * 8 + 2 * tq + u;
         if (t < mg) {
           float* orow = args.out_rows + static_cast<int64_t>(out_row0 + t) * args.out_ld;
-          orow[col0] = acc[0][c][u];
-          orow[col0 + 8] = acc[0][c][u + 2];
+#pragma unroll
+          for (int h = 0; h < NACC; ++h) {
+            orow[cbase + 128 * h] = acc[h][c][u];
+            orow[cbase + 128 * h + 8] = acc[h][c][u + 2];
+          }
         }
       }
     }
@@ -511,7 +525,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
       int next = i + gridDim.x;
       if (have && args.work_counter && leader) next = gridDim.x + atomicAdd(args.work_counter, 1);
       WorkItem w{};
-      if (have) w = engine_item(args, sm_active, sm_counts, sm_starts, i);
+      if (have) w = engine_item<EPI>(args, sm_active, sm_counts, sm_starts, i);
       const CUtensorMap* wmap = w.shared ? &tm_w_sh : &tm_w;
       const float* wscale = w.shared ? args.wscale_sh : args.wscale;
       // one slab per token group; one final slab marks the end of the work
@@ -528,7 +542,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         if (have) {
           for (int idx = lane; idx < KB; idx += 32) {
             cp_async_4(slab + 16 + idx, wscale + (w.wrow / 128) * KB + idx);
-            if (EPI == EPI_GATE_UP)
+            if (kTwoBoxes<EPI>)
               cp_async_4(slab + 16 + KB + idx, wscale + (w.wrow_up / 128) * KB + idx);
           }
           const float* src = args.act_scale + static_cast<int64_t>(w.row0 + g0) * KB;
@@ -563,7 +577,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
               mbar_arrive_expect_tx(&full[s], bytes);
               last_parity[s] = static_cast<int>(ph);
               tma_load_2d_hint(st, wmap, kb * 128, w.wrow, &full[s], pol_w);
-              if (EPI == EPI_GATE_UP)
+              if (kTwoBoxes<EPI>)
                 tma_load_2d_hint(st + 128 * 128, wmap, kb * 128, w.wrow_up, &full[s], pol_w);
               uint8_t* act = st + L::kWBytes;
               for (int b = 0; b < nbox; ++b) {

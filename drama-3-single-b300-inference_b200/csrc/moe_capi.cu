@@ -128,7 +128,8 @@ int launch_engine_inst(const CUtensorMap& tw, const CUtensorMap& twsh, const CUt
 template <int EPI, bool ACT_F16, int STAGES>
 int launch_engine(int nch, const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& ta,
                   const EngineArgs& args, int grid, cudaStream_t s) {
-  constexpr int kMax = (EPI == EPI_GATE_UP) ? 4 : 8;  // gate_up holds two accumulator sets
+  // gate_up and paired-tile down hold two accumulator sets
+  constexpr int kMax = kTwoBoxes<EPI> ? 4 : 8;
   switch (nch) {
     case 1: return launch_engine_inst<EPI, ACT_F16, 1, STAGES>(tw, twsh, ta, args, grid, s);
     case 2: return launch_engine_inst<EPI, ACT_F16, 2, STAGES>(tw, twsh, ta, args, grid, s);
@@ -383,12 +384,15 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.active = b.active;
     a.n_active = b.n_active;
     a.num_experts = E;
-    const int nch = nch_for(T);
+    // pairs of 128-row tiles per item when H allows (two accumulator sets:
+    // at most 4 token chunks per group, like gate_up)
+    const bool pair = H % 256 == 0;
+    const int nch = pair ? (nch_for(T) < 4 ? nch_for(T) : 4) : nch_for(T);
     a.shared_chunk = nch * 8;
     a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
     a.shared_row0 = P;
     a.shared_count = T;
-    a.tiles = H / 128;
+    a.tiles = pair ? H / 256 : H / 128;
     a.KB = I / 128;
     a.ksplit = 1;
     a.kb_per_split = a.KB;
@@ -400,9 +404,10 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     a.out_ld = H;
     a.status = status;
     a.work_counter = b.work + 1;
-    const int max_items = (E + a.shared_groups) * (H / 128);
+    const int max_items = (E + a.shared_groups) * a.tiles;
     const int grid = max_items < sms ? max_items : sms;
-    rc = launch_engine<EPI_DOWN, false, kStagesDown>(nch, tw, twsh, ta, a, grid, s);
+    rc = pair ? launch_engine<EPI_DOWN2, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s)
+              : launch_engine<EPI_DOWN, false, kStagesDown>(nch, tw, twsh, ta, a, grid, s);
     if (rc) return rc;
   }
   stage_mark(3, s);
