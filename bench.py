@@ -260,7 +260,7 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     def gemv(x, wq, sq, n, out):
         _lib.call("d3_fp8_gemv", x.data_ptr(), x.stride(0), wq.data_ptr(), sq.data_ptr(), T, n, H,
                   out.data_ptr(), out.stride(0), ws_dense.data_ptr(), ws_dense.numel(),
-                  status.data_ptr(), sptr)
+                  status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
 
     ids_seen = []
 
@@ -279,6 +279,58 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     torch.cuda.synchronize(dev)
     dist.barrier()
     torch.cuda.synchronize(dev)
+
+    # The decode step captured in one CUDA graph per weight set, like the
+    # reference's captured decode step (src/drama3/engine.py:84-92): the NCCL
+    # exchanges and every kernel replay without host launch overhead. The
+    # input is copied into the graph's static buffer before each replay.
+    graphs, x_static, y_static = [], [], []
+    graph_ms = None
+    if not args.eager:
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            for li in range(args.layers):
+                xb = xs[li % len(xs)].clone()
+                step(li, xb)  # warm the capture stream's allocations
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    yb = step(li, xb)
+                graphs.append(g)
+                x_static.append(xb)
+                y_static.append(yb)
+        stream.wait_stream(cap)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        # the replay must reproduce the eager step bit for bit
+        y_eager = step(0, x_static[0]).clone()
+        y_static[0].zero_()
+        graphs[0].replay()
+        torch.cuda.synchronize(dev)
+        if not torch.equal(y_static[0], y_eager):
+            raise RuntimeError("CUDA graph replay differs from the eager step")
+        dist.barrier()
+        for i in range(args.warmup):
+            li = i % args.layers
+            x_static[li].copy_(xs[i % len(xs)])
+            graphs[li].replay()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        gstart, gend = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gstart.record(stream)
+        for i in range(args.steps):
+            li = i % args.layers
+            x_static[li].copy_(xs[(args.warmup + i) % len(xs)])
+            graphs[li].replay()
+        gend.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        graph_ms = gstart.elapsed_time(gend) / args.steps
+        t = torch.tensor([graph_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        graph_ms = float(t.item())
+
     stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     for evs in stage_events:
         for e in evs:
@@ -299,7 +351,8 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     down_avg = statistics.mean(evs[2].elapsed_time(evs[3]) for evs in stage_events)
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    eager_ms = float(t.item())
+    ms = eager_ms if graph_ms is None else graph_ms
     # experts this rank streamed per step: distinct global ids it owns, over all ranks' tokens
     gathered = [torch.empty_like(ids_seen[0]) for _ in range(world)]
     U_local = []
@@ -314,16 +367,25 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     hx = torch.randn((T, H)).to(torch.bfloat16).pin_memory()
     hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
     dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i):
+        if not graphs:
+            dx.copy_(hx, non_blocking=True)
+            hy.copy_(step(i, dx), non_blocking=True)
+        else:
+            li = i % args.layers
+            x_static[li].copy_(hx, non_blocking=True)
+            graphs[li].replay()
+            hy.copy_(y_static[li], non_blocking=True)
+
     for i in range(2):
-        dx.copy_(hx, non_blocking=True)
-        hy.copy_(step(i, dx), non_blocking=True)
+        e2e_step(i)
     torch.cuda.synchronize(dev)
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        dx.copy_(hx, non_blocking=True)
-        hy.copy_(step(i, dx), non_blocking=True)
+        e2e_step(i)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -357,6 +419,8 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
             "parallelism": f"ep{world}",
             "collective": "NCCL all_to_all_single, fixed capacity (token rows + per-rank routing out, "
                           "weighted partial rows back; no host synchronisation)",
+            "launch": "eager" if graph_ms is None else "one CUDA graph per weight set (kernels + NCCL), replayed",
+            "eager_ms_per_step": eager_ms,
         },
         "roofline": {
             "bound": "hbm",
@@ -376,6 +440,9 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    # graphs holding NCCL work are released before the process group goes
+    del graphs, x_static, y_static
+    torch.cuda.synchronize(dev)
 
 
 def prefill_lengths() -> list[int]:
@@ -856,6 +923,8 @@ def main() -> None:
                     help="mixed: MoE rows from which the tcgen05 path runs (0: the library default)")
     ap.add_argument("--prefill-tokens", type=int, default=0,
                     help="prefill: a flat batch of this many tokens instead of the ragged 64-prompt batch")
+    ap.add_argument("--eager", action="store_true",
+                    help="with N > 1: launch the step op by op instead of replaying its CUDA graph")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1: independent full-layer replicas instead of expert parallelism")
     args = ap.parse_args()
@@ -932,7 +1001,7 @@ def main() -> None:
     def gemv(x, x_ld, wq, sq, n, out):
         _lib.call("d3_fp8_gemv", x.data_ptr(), x_ld, wq.data_ptr(), sq.data_ptr(), T, n, H,
                   out.data_ptr(), out.stride(0), ws_dense.data_ptr(), ws_dense.numel(),
-                  status.data_ptr(), sptr)
+                  status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
 
     def step(i: int, x: torch.Tensor, ids_buf, dense_events=None):
         li = i % args.layers
@@ -948,7 +1017,7 @@ def main() -> None:
         _lib.call("d3_moe_layer", o.data_ptr(), o.stride(0), lw.router.data_ptr(), None, T, TOPK,
                   ctypes.byref(ev.struct), ctypes.byref(sv.struct), y.data_ptr(),
                   None if ids_buf is None else ids_buf.data_ptr(), wts.data_ptr(),
-                  ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), sptr)
+                  ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
 
     # (act prep + engine) x 2 GEMVs; router, route, permute, quant_scatter, gate_up, down, combine
     launches_per_step = 2 * 2 + 7
@@ -993,24 +1062,79 @@ def main() -> None:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+    eager_ms = ms
+
+    # ---- the step captured in one CUDA graph per weight set (the reference
+    # captures its decode step, src/drama3/engine.py:84-92); the timed value
+    # replays them. The eager loop above gives the per-kernel stage times.
+    graphs, x_static = [], []
+    if not args.eager:
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            for li in range(args.layers):
+                xb = xs[li % len(xs)].clone()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    step(li, xb, None)
+                graphs.append(g)
+                x_static.append(xb)
+        stream.wait_stream(cap)
+        # the replay must reproduce the eager step bit for bit
+        step(0, x_static[0], None)
+        y_eager = y.clone()
+        y.zero_()
+        graphs[0].replay()
+        torch.cuda.synchronize(dev)
+        if not torch.equal(y, y_eager):
+            raise RuntimeError("CUDA graph replay differs from the eager step")
+        for i in range(args.warmup):
+            graphs[i % args.layers].replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for i in range(args.steps):
+            li = i % args.layers
+            x_static[li].copy_(xs[(args.warmup + i) % len(xs)])
+            graphs[li].replay()
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = g0.elapsed_time(g1) / args.steps
+        if world > 1:
+            torch.distributed.barrier()
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        if int(status.item()) != 0:
+            raise RuntimeError(f"device status word {int(status.item())}: a bounded wait timed out")
 
     # ---- end-to-end through the C ABI with host buffers (pinned H2D + D2H per step)
     hx = torch.randn((T, H)).to(torch.bfloat16).pin_memory()
     hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
     dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    for i in range(3):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx, None)
+
+    def e2e_step(i):
+        if graphs:
+            li = i % args.layers
+            x_static[li].copy_(hx, non_blocking=True)
+            graphs[li].replay()
+        else:
+            dx.copy_(hx, non_blocking=True)
+            step(i, dx, None)
         hy.copy_(y, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx, None)
-        hy.copy_(y, non_blocking=True)
+        e2e_step(i)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -1047,6 +1171,8 @@ def main() -> None:
             "l2": f"inputs larger than L2: {args.layers} weight sets x "
                   f"{layers[0].nbytes() / 1e6:.0f} MB rotated per step",
             "parallelism": "replicas" if world > 1 else "single",
+            "launch": "one CUDA graph per weight set, replayed" if graphs else "eager",
+            "eager_ms_per_step": eager_ms,
         },
         "roofline": {
             "bound": "hbm",
