@@ -518,6 +518,66 @@ __global__ void ep_dispatch_meta_kernel(const int64_t* __restrict__ ids,
   meta_w[idx] = mine ? w[tj] : __float2bfloat16_rn(0.f);
 }
 
+// Packed capacity-mode dispatch: for destination rank d and token t, row
+// (d, t) of `send` holds x[t] (2H bytes), the k owner-local expert ids (int64,
+// -1 where expert e is owned by another rank) and the k bf16 weights (0 there),
+// padded to ep_row_bytes. One 16-byte chunk per thread.
+__global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                               const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
+                               int T, int k, int H, int experts_per_rank, int ranks, int row_bytes,
+                               uint8_t* __restrict__ send) {
+  pdl_wait();
+  const int chunks = row_bytes / 16;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n = static_cast<int64_t>(ranks) * T * chunks;
+  if (idx >= n) return;
+  const int c = static_cast<int>(idx % chunks);
+  const int64_t rt = idx / chunks;
+  const int t = static_cast<int>(rt % T), d = static_cast<int>(rt / T);
+  uint8_t* row = send + rt * row_bytes;
+  const int xchunks = H / 8;
+  if (c < xchunks) {
+    reinterpret_cast<uint4*>(row)[c] = __ldg(reinterpret_cast<const uint4*>(x + t * x_stride) + c);
+    return;
+  }
+  // metadata chunks: k int64 ids, then k bf16 weights, then zero padding
+  uint32_t out[4] = {0u, 0u, 0u, 0u};
+  const int base = 16 * c - 2 * H;  // byte offset inside the metadata
+  for (int b = 0; b < 16; b += 2) {
+    const int off = base + b;
+    uint16_t v = 0;
+    if (off < 8 * k) {
+      const int j = off / 8, part = (off % 8) / 2;
+      const int64_t e = ids[static_cast<int64_t>(t) * k + j];
+      const bool mine = e >= 0 && e / experts_per_rank == d && e < static_cast<int64_t>(experts_per_rank) * ranks;
+      const int64_t local = mine ? e - static_cast<int64_t>(d) * experts_per_rank : -1;
+      v = static_cast<uint16_t>(static_cast<uint64_t>(local) >> (16 * part));
+    } else if (off < 10 * k) {
+      const int j = (off - 8 * k) / 2;
+      const int64_t e = ids[static_cast<int64_t>(t) * k + j];
+      const bool mine = e >= 0 && e / experts_per_rank == d && e < static_cast<int64_t>(experts_per_rank) * ranks;
+      v = mine ? __bfloat16_as_ushort(w[static_cast<int64_t>(t) * k + j]) : 0;
+    }
+    out[b / 4] |= static_cast<uint32_t>(v) << (16 * ((b / 2) & 1));
+  }
+  reinterpret_cast<uint4*>(row)[c] = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// The metadata of received packed rows into contiguous ids [rows, k] int64
+// and weights [rows, k] bf16.
+__global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, int rows, int k, int H,
+                                      int row_bytes, int64_t* __restrict__ ids,
+                                      __nv_bfloat16* __restrict__ w) {
+  pdl_wait();
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * k) return;
+  const int64_t r = idx / k;
+  const int j = static_cast<int>(idx % k);
+  const uint8_t* meta = recv + r * row_bytes + 2 * H;
+  ids[idx] = reinterpret_cast<const int64_t*>(meta)[j];
+  w[idx] = reinterpret_cast<const __nv_bfloat16*>(meta + 8 * k)[j];
+}
+
 inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps); }
 
 // CTAs for one warp per (row, group pair).
@@ -671,6 +731,43 @@ extern "C" int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const
       T, k, static_cast<const __nv_bfloat16*>(shared), static_cast<const __nv_bfloat16*>(gate),
       gate_stride, static_cast<__nv_bfloat16*>(out));
   return check_launch("combine_pairs");
+}
+
+extern "C" int d3_ep_row_bytes(int H, int k, int* bytes) {
+  D3_REQUIRE(bytes && H > 0 && H % 8 == 0 && k > 0, "ep_row_bytes: bad arguments");
+  *bytes = (2 * H + 10 * k + 15) / 16 * 16;
+  return D3_OK;
+}
+
+extern "C" int d3_ep_pack(const void* x, int64_t x_stride, const int64_t* ids, const void* weights,
+                          int T, int k, int H, int experts_per_rank, int ranks, uint8_t* send,
+                          d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && H > 0 && H % 8 == 0 && experts_per_rank > 0 && ranks > 0,
+             "ep_pack: bad shape");
+  D3_REQUIRE(x_stride >= H && x_stride % 8 == 0 && aligned(x, 16) && aligned(send, 16),
+             "ep_pack: x must be 16-byte aligned with a row stride >= H, multiple of 8");
+  D3_REQUIRE(ids && weights, "ep_pack: null ids or weights");
+  const int row_bytes = (2 * H + 10 * k + 15) / 16 * 16;
+  const int64_t n = static_cast<int64_t>(ranks) * T * (row_bytes / 16);
+  if (n == 0) return D3_OK;
+  launch_kernel(ep_pack_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                reinterpret_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x), x_stride,
+                ids, static_cast<const __nv_bfloat16*>(weights), T, k, H, experts_per_rank, ranks,
+                row_bytes, send);
+  return check_launch("ep_pack");
+}
+
+extern "C" int d3_ep_unpack_meta(const uint8_t* recv, int rows, int k, int H, int64_t* ids,
+                                 void* weights, d3_stream_t stream) {
+  D3_REQUIRE(rows >= 0 && k > 0 && H > 0 && H % 8 == 0 && recv && ids && weights,
+             "ep_unpack_meta: bad arguments");
+  const int row_bytes = (2 * H + 10 * k + 15) / 16 * 16;
+  const int64_t n = static_cast<int64_t>(rows) * k;
+  if (n == 0) return D3_OK;
+  launch_kernel(ep_unpack_meta_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                reinterpret_cast<cudaStream_t>(stream), recv, rows, k, H, row_bytes, ids,
+                static_cast<__nv_bfloat16*>(weights));
+  return check_launch("ep_unpack_meta");
 }
 
 extern "C" int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, int k,

@@ -127,6 +127,12 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i32, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p, _i32, _i64, _c_void_p,
          _c_void_p, _i32, _c_void_p],
     ),
+    "d3_ep_row_bytes": (_i32, [_i32, _i32, ctypes.POINTER(_i32)]),
+    "d3_ep_pack": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p],
+    ),
+    "d3_ep_unpack_meta": (_i32, [_c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_ep_dispatch_meta": (_i32, [_c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_gather_rows": (_i32, [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p]),
     "d3_combine_pairs": (

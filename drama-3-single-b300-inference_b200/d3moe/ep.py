@@ -21,16 +21,20 @@ That is mode="exact": it moves only the pairs, but needs a host read of the
 send counts per call. The default, mode="capacity", has no host
 synchronisation (so the layer can be captured into a CUDA graph with its NCCL
 calls): every token row goes once to every rank together with the routing
-restricted to that rank's experts (d3_ep_dispatch_meta: local ids or -1, the
-routing weight or 0), the owner runs its experts on all received rows with
-those k ids and returns one weighted partial row per token, bf16(sum over its
-experts of w * down), and the token's rank adds the N partials in rank order
-plus the gated shared expert (d3_combine_pairs with weight 1 per rank). All
-ranks must then call the layer with the same T. At decode sizes this moves
-T*N rows per rank per direction, the same order as the exact scheme.
+restricted to that rank's experts (local ids or -1, the routing weight or 0),
+packed with the row into one buffer so the dispatch is a single all_to_all
+(d3_ep_pack / d3_ep_unpack_meta); the owner runs its experts on all received
+rows with those k ids and returns one weighted partial row per token,
+bf16(sum over its experts of w * down), and the token's rank adds the N
+partials in rank order plus the gated shared expert (d3_combine_pairs with
+weight 1 per rank). The shared expert runs on a side stream while the
+exchange is in flight. All ranks must call the layer with the same T. At
+decode sizes this moves T*N rows per rank per direction, the same order as the
+exact scheme.
 
-The device steps are the C ABI entry points d3_ep_plan, d3_ep_dispatch_meta,
-d3_gather_rows, d3_moe_experts and d3_combine_pairs. `ops` is injectable so the
+The device steps are the C ABI entry points d3_ep_plan, d3_ep_pack,
+d3_ep_unpack_meta, d3_ep_dispatch_meta, d3_gather_rows, d3_moe_experts and
+d3_combine_pairs. `ops` is injectable so the
 exchange logic can be exercised with CPU ranks (gloo) in tests; the default
 runs on the GPU.
 """
@@ -42,6 +46,12 @@ import torch.distributed as dist
 
 from . import ops as _ops
 from ._lib import call
+
+
+def ep_row_bytes(H: int, k: int) -> int:
+    """Bytes per packed dispatch row: x (2H) + k int64 ids + k bf16 weights,
+    rounded up to 16 (d3_ep_row_bytes)."""
+    return (2 * H + 10 * k + 15) // 16 * 16
 
 
 class CudaEPOps:
@@ -68,6 +78,26 @@ class CudaEPOps:
              send_starts.data_ptr(), sorted_pairs.data_ptr(), inv.data_ptr(), local_ids.data_ptr(),
              scratch.data_ptr(), _ops._stream(dev))
         return send_counts, sorted_pairs[:P], inv[:P], local_ids[:P]
+
+    def pack(self, x, ids, weights, experts_per_rank, ranks):
+        """Packed capacity-mode send buffer uint8 [ranks, T * row_bytes]."""
+        T, H = x.shape
+        k = ids.shape[1]
+        rb = ep_row_bytes(H, k)
+        send = torch.empty((ranks, T * rb), dtype=torch.uint8, device=x.device)
+        call("d3_ep_pack", x.data_ptr(), _ops._row_stride(x), ids.data_ptr(),
+             weights.contiguous().data_ptr(), T, k, H, experts_per_rank, ranks, send.data_ptr(),
+             _ops._stream(x.device))
+        return send
+
+    def unpack(self, recv, rows, k, H):
+        """Received packed rows -> (x rows bf16 [rows, H] strided view, ids, weights)."""
+        rb = ep_row_bytes(H, k)
+        ids = torch.empty((rows, k), dtype=torch.int64, device=recv.device)
+        w = torch.empty((rows, k), dtype=torch.bfloat16, device=recv.device)
+        call("d3_ep_unpack_meta", recv.data_ptr(), rows, k, H, ids.data_ptr(), w.data_ptr(),
+             _ops._stream(recv.device))
+        return recv.view(rows, rb).view(torch.bfloat16)[:, :H], ids, w
 
     def gather_rows(self, x, sorted_pairs, k):
         T, H = x.shape
@@ -141,6 +171,7 @@ class ExpertParallelMoE:
         self.shared = shared
         self.k = top_k
         self.ops = ops if ops is not None else CudaEPOps()
+        self._side = {}
 
     def _exchange(self, send, send_counts, recv_counts):
         """all_to_all_v of rows (first dim split by counts)."""
@@ -167,25 +198,56 @@ class ExpertParallelMoE:
             self._combine_index[key] = got
         return got
 
+    def _shared_begin(self, x):
+        """The shared expert on the layer's own rows; on CUDA it runs on a side
+        stream so it overlaps the dispatch exchange (joined in _shared_end)."""
+        if not x.is_cuda:
+            return self.ops.shared_expert(x, self.shared), None
+        main = torch.cuda.current_stream(x.device)
+        side = self._side.get(x.device)
+        if side is None:
+            side = torch.cuda.Stream(x.device)
+            self._side[x.device] = side
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            shared = self.ops.shared_expert(x, self.shared)
+        return shared, side
+
+    def _shared_end(self, shared, side):
+        if side is not None:
+            main = torch.cuda.current_stream(shared.device)
+            main.wait_stream(side)
+            shared.record_stream(main)
+        return shared
+
     def _forward_capacity(self, x, return_routing: bool):
         ops = self.ops
         N = self.world
         T, H = x.shape
         logits = ops.router_logits(x, self.router)
         weights, ids = ops.route(logits[:, : self.E], self.k, bias=self.router_bias)
-        meta_ids, meta_w = ops.dispatch_meta(ids, weights, self.E_local, N)
-        x_send = x.unsqueeze(0).expand(N, T, H).contiguous()
-        x_recv = torch.empty_like(x_send)
-        ids_recv = torch.empty_like(meta_ids)
-        w_recv = torch.empty_like(meta_w)
-        dist.all_to_all_single(x_recv, x_send, group=self.group)
-        dist.all_to_all_single(ids_recv, meta_ids, group=self.group)
-        dist.all_to_all_single(w_recv, meta_w, group=self.group)
-        partial = ops.local_experts_k(x_recv.view(N * T, H), ids_recv.view(N * T, self.k),
-                                      w_recv.view(N * T, self.k), self.experts)
+        shared, side = self._shared_begin(x)
+        if hasattr(ops, "pack"):
+            # one exchange of packed rows (token row + per-rank routing)
+            send = ops.pack(x, ids, weights, self.E_local, N)
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+            rows, ids_recv, w_recv = ops.unpack(recv, N * T, self.k, H)
+        else:
+            meta_ids, meta_w = ops.dispatch_meta(ids, weights, self.E_local, N)
+            x_send = x.unsqueeze(0).expand(N, T, H).contiguous()
+            x_recv = torch.empty_like(x_send)
+            ids_recv = torch.empty_like(meta_ids)
+            w_recv = torch.empty_like(meta_w)
+            dist.all_to_all_single(x_recv, x_send, group=self.group)
+            dist.all_to_all_single(ids_recv, meta_ids, group=self.group)
+            dist.all_to_all_single(w_recv, meta_w, group=self.group)
+            rows = x_recv.view(N * T, H)
+        partial = ops.local_experts_k(rows, ids_recv.view(N * T, self.k), w_recv.view(N * T, self.k),
+                                      self.experts)
         partial_back = torch.empty_like(partial)
         dist.all_to_all_single(partial_back, partial, group=self.group)
-        shared = ops.shared_expert(x, self.shared)
+        shared = self._shared_end(shared, side)
         inv, ones = self._combine_inputs(T, x.device)
         out = ops.combine(partial_back, inv, ones, shared, logits[:, self.E: self.E + 1])
         if return_routing:

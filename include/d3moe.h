@@ -357,6 +357,18 @@ D3_API int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, i
                                int experts_per_rank, int ranks, int64_t* meta_ids, void* meta_w,
                                d3_stream_t stream);
 
+/* Packed fixed-capacity dispatch: one buffer, one all_to_all. send holds
+ * [ranks][T] rows of d3_ep_row_bytes(H, k) bytes: x[t] (bf16, 2H bytes), the
+ * k owner-local ids of d3_ep_dispatch_meta (int64) and its k weights (bf16),
+ * zero padded. A received row's x part is a bf16 row with stride
+ * row_bytes / 2 elements; d3_ep_unpack_meta copies the ids [rows, k] and
+ * weights [rows, k] out of `rows` received rows. */
+D3_API int d3_ep_row_bytes(int H, int k, int* bytes);
+D3_API int d3_ep_pack(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
+                      int k, int H, int experts_per_rank, int ranks, uint8_t* send, d3_stream_t stream);
+D3_API int d3_ep_unpack_meta(const uint8_t* recv, int rows, int k, int H, int64_t* ids, void* weights,
+                             d3_stream_t stream);
+
 /* dst bf16 [rows, H] = src rows of token sorted_pairs[j] / k. */
 D3_API int d3_gather_rows(const void* src, int64_t src_stride, int T, int H, int k,
                           const int32_t* sorted_pairs, int rows, void* dst, d3_stream_t stream);

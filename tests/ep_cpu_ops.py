@@ -61,6 +61,30 @@ class CpuEPOps:
             meta_w[d][torch.from_numpy(mine)] = wn[torch.from_numpy(mine)]
         return torch.from_numpy(meta_ids), meta_w
 
+    def pack(self, x, ids, weights, experts_per_rank, ranks):
+        """The packed dispatch rows of d3_ep_pack, built from dispatch_meta."""
+        from d3moe.ep import ep_row_bytes
+        T, H = x.shape
+        k = ids.shape[1]
+        rb = ep_row_bytes(H, k)
+        meta_ids, meta_w = self.dispatch_meta(ids, weights, experts_per_rank, ranks)
+        send = torch.zeros((ranks, T, rb), dtype=torch.uint8)
+        xb = x.contiguous().view(torch.uint8).reshape(T, 2 * H)
+        for d in range(ranks):
+            send[d, :, : 2 * H] = xb
+            send[d, :, 2 * H: 2 * H + 8 * k] = meta_ids[d].contiguous().view(torch.uint8).reshape(T, 8 * k)
+            send[d, :, 2 * H + 8 * k: 2 * H + 10 * k] = meta_w[d].contiguous().view(torch.uint8).reshape(T, 2 * k)
+        return send.reshape(ranks, T * rb)
+
+    def unpack(self, recv, rows, k, H):
+        from d3moe.ep import ep_row_bytes
+        rb = ep_row_bytes(H, k)
+        r = recv.reshape(rows, rb)
+        x = r[:, : 2 * H].contiguous().view(torch.bfloat16)
+        ids = r[:, 2 * H: 2 * H + 8 * k].contiguous().view(torch.int64)
+        w = r[:, 2 * H + 8 * k: 2 * H + 10 * k].contiguous().view(torch.bfloat16)
+        return x, ids, w
+
     def local_experts_k(self, rows, ids, weights, experts):
         """Oracle expert sum over each row's valid ids (-1 = not routed here)."""
         r = _np(rows)

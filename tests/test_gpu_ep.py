@@ -83,3 +83,26 @@ def test_ep_multi_rank_matches_fused_layer(tmp_path, world, mode):
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), 64, mode), nprocs=world, join=True)
     _check(tmp_path, world)
+
+
+def test_ep_pack_unpack_matches_dispatch_meta():
+    """The packed dispatch rows carry exactly dispatch_meta's per-rank routing
+    and the token rows (d3_ep_pack / d3_ep_unpack_meta round trip)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from d3moe.ep import CudaEPOps
+    ops = CudaEPOps()
+    T, H, k, N, epr = 37, 2048, 8, 4, 32
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    x = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    ids = torch.randint(0, N * epr, (T, k), generator=g, device="cuda")
+    ids[3, 2] = -1  # an empty slot
+    w = torch.rand((T, k), generator=g, device="cuda").to(torch.bfloat16)
+    send = ops.pack(x, ids, w, epr, N)
+    rows, ids_u, w_u = ops.unpack(send, N * T, k, H)
+    meta_ids, meta_w = ops.dispatch_meta(ids, w, epr, N)
+    torch.cuda.synchronize()
+    assert torch.equal(ids_u, meta_ids.view(N * T, k))
+    assert torch.equal(w_u, meta_w.view(N * T, k))
+    assert torch.equal(rows, x.unsqueeze(0).expand(N, T, H).reshape(N * T, H))
