@@ -485,28 +485,52 @@ __global__ void __launch_bounds__(kPermuteThreads)
   pdl_wait();
   __shared__ int warp_tot[33];
   __shared__ int s_cnt[1024], s_start[1024];
+  __shared__ int s_part[kPermuteThreads];  // [part][E] chunk-slice sums, then their offsets
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // parts threads per expert, each owning a contiguous slice of the chunks
+  // (coalesced over e, independent loads); the slices are combined in part
+  // order, so every expert's running offsets are the sequential ones.
+  const int parts = E <= kPermuteThreads ? kPermuteThreads / E : 1;
+  const int part = tid / E, e_mine = tid - part * E;
+  const bool owner = part < parts && e_mine < E;
+  const int per = (chunks + parts - 1) / parts;
+  const int c0 = part * per, c1 = min(chunks, c0 + per);
+  int slice = 0;
+  if (owner) {
+#pragma unroll 8
+    for (int c = c0; c < c1; ++c) slice += cc[static_cast<int64_t>(c) * E + e_mine];
+    s_part[part * E + e_mine] = slice;
+  }
+  __syncthreads();
   const int e = tid;
   int c_tot = 0;
-  if (e < E)
-    for (int c = 0; c < chunks; ++c) c_tot += cc[static_cast<int64_t>(c) * E + e];
+  if (e < E) {
+    for (int p = 0; p < parts; ++p) {
+      const int v = s_part[p * E + e];
+      s_part[p * E + e] = c_tot;  // exclusive offset of slice p
+      c_tot += v;
+    }
+  }
   const int padded = (c_tot + bm - 1) / bm * bm;
   int total = 0;
   const int start = block_exclusive_scan(e < E ? padded : 0, warp_tot, total);
   if (e < E) {
-    int run = start;
-    for (int c = 0; c < chunks; ++c) {
-      const int64_t i = static_cast<int64_t>(c) * E + e;
-      const int v = cc[i];
-      cc[i] = run;
-      run += v;
-    }
     s_cnt[e] = c_tot;
     s_start[e] = start;
     counts[e] = c_tot;
     starts[e] = start;
   }
   __syncthreads();
+  if (owner) {
+    int run = s_start[e_mine] + s_part[part * E + e_mine];
+#pragma unroll 8
+    for (int c = c0; c < c1; ++c) {
+      const int64_t i = static_cast<int64_t>(c) * E + e_mine;
+      const int v = cc[i];
+      cc[i] = run;
+      run += v;
+    }
+  }
   for (int ee = warp; ee < E; ee += kPermuteThreads / 32) {
     const int c = s_cnt[ee], s = s_start[ee];
     const int pd = (c + bm - 1) / bm * bm;
