@@ -22,7 +22,10 @@ namespace {
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxChunks = 4;  // W <= 4 * 8 * 256 = 8192
 
-enum NormSrc { NS_ADD = 0, NS_COMBINE = 1, NS_ROWS = 2 };
+// NS_ROWS: fp32 expert rows; NS_ROWS_BF16: the bf16 expert rows of the
+// tcgen05 path.
+enum NormSrc { NS_ADD = 0, NS_COMBINE = 1, NS_ROWS = 2, NS_ROWS_BF16 = 3 };
+
 
 __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float (&f)[8]) {
   const uint4 v = *reinterpret_cast<const uint4*>(p);
@@ -42,6 +45,20 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float (&f)[8]) {
     o[i] = *reinterpret_cast<uint32_t*>(&p);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// 8 consecutive values of an expert row as fp32.
+template <int SRC>
+__device__ __forceinline__ void load_row8(const void* d, int64_t row, int W, int c, float (&f)[8]) {
+  if constexpr (SRC == NS_ROWS_BF16) {
+    load_bf16x8(static_cast<const __nv_bfloat16*>(d) + row * W + c, f);
+  } else {
+    const float* p = static_cast<const float*>(d) + row * W + c;
+    const float4 lo = *reinterpret_cast<const float4*>(p);
+    const float4 hi = *reinterpret_cast<const float4*>(p + 4);
+    f[0] = lo.x; f[1] = lo.y; f[2] = lo.z; f[3] = lo.w;
+    f[4] = hi.x; f[5] = hi.y; f[6] = hi.z; f[7] = hi.w;
+  }
 }
 
 // combined = fma.rn.bf16(shared, gate, routed) for 8 columns (inputs are bf16
@@ -74,7 +91,7 @@ __global__ void __launch_bounds__(kNormThreads)
   float v[kNormMaxChunks][8];
   float ss = 0.f;
   const int src = (SRC == NS_COMBINE && inverse) ? inverse[row]
-                  : SRC == NS_ROWS ? static_cast<int>(gather_row(rows, row)) : row;
+                  : (SRC == NS_ROWS || SRC == NS_ROWS_BF16) ? static_cast<int>(gather_row(rows, row)) : row;
   float g = 0.f;
   if (SRC != NS_ADD) g = sigmoid_bf16(gate + static_cast<int64_t>(src) * gate_stride);
 #pragma unroll
@@ -96,20 +113,19 @@ __global__ void __launch_bounds__(kNormThreads)
         load_bf16x8(static_cast<const __nv_bfloat16*>(p1) + static_cast<int64_t>(src) * W + c, shared);
       } else {
         // expert rows: fp32 rank-order sum weighted by the bf16 routing weight
-        const float* d = static_cast<const float*>(p0);
+        const void* d = p0;
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int r = 0; r < k; ++r) {
           const int dr = inv_rows[src * k + r];
           if (dr < 0) continue;
           const float w = __bfloat162float(weights[src * k + r]);
-          const float4 lo = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(dr) * W + c);
-          const float4 hi = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(dr) * W + c + 4);
-          acc[0] += lo.x * w; acc[1] += lo.y * w; acc[2] += lo.z * w; acc[3] += lo.w * w;
-          acc[4] += hi.x * w; acc[5] += hi.y * w; acc[6] += hi.z * w; acc[7] += hi.w * w;
+          float v[8];
+          load_row8<SRC>(d, dr, W, c, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += v[i] * w;
         }
-        const float4 slo = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + src) * W + c);
-        const float4 shi = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + src) * W + c + 4);
-        const float sh[8] = {slo.x, slo.y, slo.z, slo.w, shi.x, shi.y, shi.z, shi.w};
+        float sh[8];
+        load_row8<SRC>(d, P + src, W, c, sh);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           routed[i] = bf16_round(acc[i]);
@@ -163,7 +179,7 @@ int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
                                  const void* weights, int T, int k, const void* gate,
                                  int64_t gate_stride, void* residual, const void* norm_w, float eps,
                                  void* out, cudaStream_t s, const int64_t* inverse, int T_out,
-                                 int32_t* status) {
+                                 int32_t* status, bool rows_bf16) {
   if (T <= 0) return D3_OK;
   RowGather rows;
   rows.keep = inverse;
@@ -171,7 +187,8 @@ int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
   rows.status = status;
   const int nrows = inverse ? T_out : T;
   if (nrows <= 0) return D3_OK;
-  launch_kernel(add_norm_kernel<NS_ROWS>, dim3(nrows), dim3(kNormThreads), 0, s,
+  launch_kernel(rows_bf16 ? add_norm_kernel<NS_ROWS_BF16> : add_norm_kernel<NS_ROWS>, dim3(nrows),
+                dim3(kNormThreads), 0, s,
                 static_cast<const void*>(d), static_cast<const void*>(nullptr),
                 static_cast<const __nv_bfloat16*>(gate), gate_stride,
                 static_cast<const int32_t*>(nullptr), inv_rows,

@@ -57,9 +57,11 @@ void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half
 //   routed[t] = bf16(sum_r w[t,r] * d[inv_rows[t*k+r]])
 //   shared[t] = bf16(d[P+t])                                   (when with_shared)
 //   out[t]    = routed + bf16(shared * bf16(sigmoid(gate[t]))) (when gate != null)
+// rows_bf16: d holds bf16 rows (the tcgen05 path) instead of fp32.
 void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,
                          int T, int k, int with_shared, const void* gate, int64_t gate_stride,
-                         void* routed_out, void* shared_out, void* out, cudaStream_t s);
+                         void* routed_out, void* shared_out, void* out, cudaStream_t s,
+                         bool rows_bf16 = false);
 
 // Fused layer exit: routed/shared rows combined as in
 // d3_combine_experts_add_norm, residual updated in place, out = RMSNorm. With
@@ -68,7 +70,7 @@ int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
                                  const void* weights, int T, int k, const void* gate,
                                  int64_t gate_stride, void* residual, const void* norm_w, float eps,
                                  void* out, cudaStream_t s, const int64_t* inverse = nullptr,
-                                 int T_out = 0, int32_t* status = nullptr);
+                                 int T_out = 0, int32_t* status = nullptr, bool rows_bf16 = false);
 
 // Router projection (fixed fp32 summation order); from 256 tokens a tiled
 // kernel (same order) streams 32-token x 16-row tiles.

@@ -335,7 +335,21 @@ __global__ void combine_experts_kernel(const __nv_bfloat16* __restrict__ routed,
 
 // One thread per 4 output columns of one token. Expert rows are read in rank
 // order r = 0..k-1 and summed in fp32 with the bf16 routing weight.
-__global__ void combine_rows_kernel(const float* __restrict__ d, int H,
+// 4 consecutive values of an expert row as fp32, from fp32 rows or from the
+// bf16 rows of the tcgen05 path.
+template <bool BF16>
+__device__ __forceinline__ float4 load_row4(const void* d, int64_t row, int H, int c) {
+  if constexpr (BF16) {
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(d) + row * H + c);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+  } else {
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(d) + row * H + c);
+  }
+}
+
+template <bool BF16>
+__global__ void combine_rows_kernel(const void* __restrict__ d, int H,
                                     const int32_t* __restrict__ inv_rows,
                                     const __nv_bfloat16* __restrict__ weights, int T, int k,
                                     int with_shared, const __nv_bfloat16* __restrict__ gate,
@@ -353,7 +367,7 @@ __global__ void combine_rows_kernel(const float* __restrict__ d, int H,
     const int row = inv_rows[t * k + r];
     if (row < 0) continue;  // pair whose expert id was out of range: not routed
     const float w = __bfloat162float(weights[t * k + r]);
-    const float4 v = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(row) * H + c);
+    const float4 v = load_row4<BF16>(d, row, H, c);
     acc[0] += v.x * w;
     acc[1] += v.y * w;
     acc[2] += v.z * w;
@@ -363,7 +377,7 @@ __global__ void combine_rows_kernel(const float* __restrict__ d, int H,
 #pragma unroll
   for (int i = 0; i < 4; ++i) routed[i] = bf16_round(acc[i]);
   if (with_shared) {
-    const float4 v = *reinterpret_cast<const float4*>(d + static_cast<int64_t>(P + t) * H + c);
+    const float4 v = load_row4<BF16>(d, P + t, H, c);
     shared[0] = bf16_round(v.x);
     shared[1] = bf16_round(v.y);
     shared[2] = bf16_round(v.z);
@@ -617,11 +631,13 @@ void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half
 
 void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,
                          int T, int k, int with_shared, const void* gate, int64_t gate_stride,
-                         void* routed_out, void* shared_out, void* out, cudaStream_t s) {
+                         void* routed_out, void* shared_out, void* out, cudaStream_t s,
+                         bool rows_bf16) {
   const int64_t n = static_cast<int64_t>(T) * (H / 4);
   if (n <= 0) return;
-  launch_kernel(combine_rows_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s, 
-      d, H, inv_rows, static_cast<const __nv_bfloat16*>(weights), T, k, with_shared,
+  launch_kernel(rows_bf16 ? combine_rows_kernel<true> : combine_rows_kernel<false>,
+      dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+      static_cast<const void*>(d), H, inv_rows, static_cast<const __nv_bfloat16*>(weights), T, k, with_shared,
       static_cast<const __nv_bfloat16*>(gate), gate_stride,
       static_cast<__nv_bfloat16*>(routed_out), static_cast<__nv_bfloat16*>(shared_out),
       static_cast<__nv_bfloat16*>(out));

@@ -224,15 +224,17 @@ struct AddNorm {
 
 // Step 5: the fixed-order combine, or (with an AddNorm) the combine fused with
 // the residual update and RMSNorm of the layer exit.
+// rows_bf16: the expert rows in b.d are bf16 (written by the tcgen05 down
+// kernel) rather than fp32 (the decode engine).
 int finish_layer(const MoeBuffers& b, int H, const void* weights, int T, int k, int has_shared,
                  const void* gate, int64_t gate_stride, void* routed_out, void* shared_out,
-                 void* out, const AddNorm& an, cudaStream_t s) {
+                 void* out, const AddNorm& an, cudaStream_t s, bool rows_bf16 = false) {
   if (an.residual)
     return launch_combine_rows_add_norm(b.d, H, b.inv, weights, T, k, gate, gate_stride,
                                         an.residual, an.weight, an.eps, out, s, an.inverse,
-                                        an.T_out, an.status);
+                                        an.T_out, an.status, rows_bf16);
   launch_combine_rows(b.d, H, b.inv, weights, T, k, has_shared, gate, gate_stride, routed_out,
-                      shared_out, out, s);
+                      shared_out, out, s, rows_bf16);
   return check_launch("combine_rows");
 }
 
@@ -327,7 +329,7 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
     }
     stage_mark(3, s);
     rc = finish_layer(b, H, weights, T, k, has_shared, gate, gate_stride, routed_out, shared_out,
-                      out, an, s);
+                      out, an, s, true);
     stage_mark(4, s);
     return rc;
   }

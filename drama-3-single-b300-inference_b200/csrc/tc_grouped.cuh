@@ -29,8 +29,10 @@
 //            ([128 rows][128] fp32, 64 KB); the two activation warps (a row per
 //            thread) turn it into the row's 1x128 E4M3 scale and bytes and store
 //            them, while the promotion warps already work on the next tile;
-//   down     the promotion warps store the fp32 rows for the fixed-order
-//            combine through a small per-warp staging tile (coalesced stores).
+//   down     the promotion warps round the rows to bf16 (half the bytes of
+//            fp32 to store here and to read in the combine) and store them for
+//            the fixed-order combine through a small per-warp staging tile
+//            (coalesced stores).
 #pragma once
 
 #include "d3_common.cuh"
@@ -62,7 +64,7 @@ struct TcArgs {
   uint8_t* out_q;         // gate_up: a e4m3 [rows, I]
   float* out_qs;          // gate_up: sa f32 [rows, I/128]
   int I;
-  float* out_rows;        // down: f32 [rows, out_ld]
+  float* out_rows;        // down: bf16 [rows, out_ld] (stored through this pointer)
   int out_ld;
   int32_t* status;
 };
@@ -444,30 +446,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(hfull);
       } else {
-        // fp32 rows through a per-warp staging tile [32 rows][16 floats] whose
-        // 16-byte chunks are swizzled by (row >> 1) & 3 (conflict-free vector
-        // stores by row and loads by chunk): each global store instruction then
-        // writes 8 rows x 64 contiguous bytes instead of 32 scattered 16 bytes
-        float4* stg = reinterpret_cast<float4*>(aux) + ew * 32 * 4;
+        // bf16 rows (the tcgen05 path rounds its per-expert down rows to bf16
+        // before the fixed-order combine) through a per-warp staging tile
+        // [32 rows][4 x 16 bytes] whose chunks are swizzled by (row >> 1) & 3
+        // (conflict-free vector stores by row and loads by chunk): each global
+        // store instruction writes 8 rows x 64 contiguous bytes; a thread's 128
+        // columns go out in 4 steps of 32
+        uint4* stgu = reinterpret_cast<uint4*>(aux) + ew * 32 * 4;
         const int sr = lane >> 2, c4 = lane & 3;
-        float* obase = args.out_rows + static_cast<int64_t>(t.row0 + quad * 32) * args.out_ld +
-                       t.nt * 256 + 128 * wg;
+        __nv_bfloat16* obase = reinterpret_cast<__nv_bfloat16*>(args.out_rows) +
+                               static_cast<int64_t>(t.row0 + quad * 32) * args.out_ld + t.nt * 256 + 128 * wg;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const int j = 16 * (ch & 3) + 4 * c;
-            const float4 v = ch < 4 ? make_float4(acc0[j], acc0[j + 1], acc0[j + 2], acc0[j + 3])
-                                    : make_float4(acc1[j], acc1[j + 1], acc1[j + 2], acc1[j + 3]);
-            stg[lane * 4 + (c ^ ((lane >> 1) & 3))] = v;
+            const int j = 32 * (ch & 1) + 8 * c;
+            const float* src = ch < 2 ? acc0 + j : acc1 + j;
+            uint32_t p[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const __nv_bfloat162 b = __floats2bfloat162_rn(src[2 * i], src[2 * i + 1]);
+              p[i] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            stgu[lane * 4 + (c ^ ((lane >> 1) & 3))] = make_uint4(p[0], p[1], p[2], p[3]);
           }
           __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int r = sr + 8 * q;
             if (quad * 32 + r < t.mvalid)
-              *reinterpret_cast<float4*>(obase + static_cast<int64_t>(r) * args.out_ld + 16 * ch + 4 * c4) =
-                  stg[r * 4 + (c4 ^ ((r >> 1) & 3))];
+              *reinterpret_cast<uint4*>(obase + static_cast<int64_t>(r) * args.out_ld + 32 * ch + 8 * c4) =
+                  stgu[r * 4 + (c4 ^ ((r >> 1) & 3))];
           }
           __syncwarp();
         }

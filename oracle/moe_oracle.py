@@ -302,13 +302,16 @@ def expert_down_rows(a, sa, w2, s2, ids):
     return out
 
 
-def expert_down_combine(a, sa, w2, s2, ids, weights, skip=None):
+def expert_down_combine(a, sa, w2, s2, ids, weights, skip=None, rows_bf16=False):
     """src/drama3/kernels.py:304-322: y[t] = bf16(sum_r w[t,r] * down_r) with
     fp32 accumulation (rank order r = 0..k-1); pairs marked in `skip` [T,k]
-    are left out of the sum."""
+    are left out of the sum. rows_bf16: each down row is rounded to bf16
+    before the sum (the tcgen05 prefill path's intermediate rows)."""
     ids = np.asarray(ids, dtype=np.int64)
     T, k = ids.shape
     d = expert_down_rows(a, sa, w2, s2, ids).reshape(T, k, -1)
+    if rows_bf16:
+        d = bf16_round(d)
     w = np.asarray(weights, dtype=np.float32)
     acc = np.zeros((T, d.shape[2]), dtype=np.float32)
     for r in range(k):
@@ -403,10 +406,11 @@ class Experts:
         self.w13, self.s13, self.w2, self.s2 = w13, s13, w2, s2
 
 
-def moe_experts(x, ids, weights, ex: Experts, shared: Experts | None = None):
+def moe_experts(x, ids, weights, ex: Experts, shared: Experts | None = None, rows_bf16=False):
     """Routed (+ shared) experts for given routing, the arithmetic of
     small_batch_moe / native_moe (src/drama3/kernels.py:325-357, 702-779) with
-    the shared expert as an always-selected expert of weight 1.
+    the shared expert as an always-selected expert of weight 1. rows_bf16
+    restates the tcgen05 prefill path, whose per-expert down rows are bf16.
     Returns (routed bf16 [T,H], shared bf16 [T,H] or None)."""
     x = np.asarray(x, dtype=np.float32)
     ids = np.asarray(ids, dtype=np.int64)
@@ -414,7 +418,7 @@ def moe_experts(x, ids, weights, ex: Experts, shared: Experts | None = None):
     q, sx = quant_act_fp8(x)
     gu = expert_gate_up(q, sx, ex.w13, ex.s13, ids)
     a, sa = silu_mul_quant(gu)
-    routed = expert_down_combine(a, sa, ex.w2, ex.s2, ids, weights)
+    routed = expert_down_combine(a, sa, ex.w2, ex.s2, ids, weights, rows_bf16=rows_bf16)
     sh = None
     if shared is not None:
         sid = np.zeros((T, 1), dtype=np.int64)
@@ -424,7 +428,7 @@ def moe_experts(x, ids, weights, ex: Experts, shared: Experts | None = None):
     return routed, sh
 
 
-def moe_experts_q(q, sx, ids, weights, ex: Experts):
+def moe_experts_q(q, sx, ids, weights, ex: Experts, rows_bf16=False):
     """Routed experts over already-quantised activations (q e4m3 bytes [T,H],
     sx f32 [T,H/128]): the expert arithmetic of moe_experts after its input
     quantisation, the operands FlashInfer's trtllm_fp8_block_scale_moe gets
@@ -437,10 +441,10 @@ def moe_experts_q(q, sx, ids, weights, ex: Experts):
     safe = np.where(valid, ids, 0)
     gu = expert_gate_up(np.asarray(q), np.asarray(sx, np.float32), ex.w13, ex.s13, safe)
     a, sa = silu_mul_quant(gu)
-    return expert_down_combine(a, sa, ex.w2, ex.s2, safe, w, skip=~valid)
+    return expert_down_combine(a, sa, ex.w2, ex.s2, safe, w, skip=~valid, rows_bf16=rows_bf16)
 
 
-def moe_layer(x, router_w, ex: Experts, shared: Experts, k: int = 8, bias=None):
+def moe_layer(x, router_w, ex: Experts, shared: Experts, k: int = 8, bias=None, rows_bf16=False):
     """DramaModel.moe (src/drama3/model.py:485-541) for one FP8 layer: router
     projection over [E+1, H] (rows 0..E-1 router, row E shared-expert gate,
     model.py:236-245), top-k routing, routed + shared experts, combine.
@@ -449,13 +453,14 @@ def moe_layer(x, router_w, ex: Experts, shared: Experts, k: int = 8, bias=None):
     logits = router_logits(x, router_w, bias, nbias=E)
     w, ids = route(logits[:, :E], k)
     w = bf16_round(w)
-    routed, sh = moe_experts(x, ids, w, ex, shared)
+    routed, sh = moe_experts(x, ids, w, ex, shared, rows_bf16=rows_bf16)
     out = combine_experts(routed, sh, logits[:, E])
     return out, ids, w
 
 
 def moe_layer_rows(x, router_w, ex: Experts, shared: Experts, residual, norm_weight, eps=1e-6,
-                   k: int = 8, keep=None, inverse=None, row_slots=None, padding_start=None):
+                   k: int = 8, keep=None, inverse=None, row_slots=None, padding_start=None,
+                   rows_bf16=False):
     """The mixed decode + packed-prefill layer step (src/drama3/mixed_model.py:
     193-246): moe_parts over x[keep] (model.py:490-518) with the padding-router
     rule on row_slots (moe_input.py:32-36), then combine_experts_add_norm or its
@@ -467,7 +472,7 @@ def moe_layer_rows(x, router_w, ex: Experts, shared: Experts, residual, norm_wei
     logits = router_logits(xk, router_w)
     w, ids = route(logits[:, :E], k, row_slots=row_slots, padding_start=padding_start)
     w = bf16_round(w)
-    routed, sh = moe_experts(xk, ids, w, ex, shared)
+    routed, sh = moe_experts(xk, ids, w, ex, shared, rows_bf16=rows_bf16)
     out, res = combine_experts_add_norm(routed, sh, logits[:, E:E + 1], residual, norm_weight, eps,
                                         inverse=inverse)
     return out, res, ids, w

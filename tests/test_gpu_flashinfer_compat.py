@@ -67,7 +67,8 @@ def test_matches_oracle(layer, T, with_bias, prefill):
     bias_np = None if bias is None else bias.cpu().numpy()
     w_o, ids_o = O.route(logits.cpu().numpy(), K, bias=bias_np)
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
-    ref = O.moe_experts_q(fp8_bytes(q), s.cpu().numpy().T, ids_o, O.bf16_round(w_o), ex)
+    ref = O.moe_experts_q(fp8_bytes(q), s.cpu().numpy().T, ids_o, O.bf16_round(w_o), ex,
+                          rows_bf16=prefill)
     assert_close(out.float().cpu().numpy(), ref, what=f"flashinfer-compatible T={T}")
 
 

@@ -111,7 +111,7 @@ def test_mixed_layer_matches_oracle(layer, prefill):
     keep, inv = plan.keep.numpy(), plan.inverse.numpy()
     out_o, res_o, ids_o, _ = O.moe_layer_rows(x, from_bf16(lw.router), ex, sh, res0, nw, 1e-6, K,
                                               keep=keep, inverse=inv, row_slots=slots[keep],
-                                              padding_start=PAD)
+                                              padding_start=PAD, rows_bf16=prefill)
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
     within(from_bf16(rt), res_o, "residual")
     within(from_bf16(out), out_o, "out")

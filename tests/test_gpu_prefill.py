@@ -43,7 +43,7 @@ def test_prefill_layer_matches_oracle(layer, T):
     with ops.prefill_min_tokens(1):
         out, ids, w = ops.moe_layer(to_bf16(x), lw.router, lw.experts, lw.shared, K,
                                     return_routing=True, status=status)
-    ref, ids_o, _ = O.moe_layer(x, from_bf16(lw.router), ex, sh, K)
+    ref, ids_o, _ = O.moe_layer(x, from_bf16(lw.router), ex, sh, K, rows_bf16=True)
     assert int(status[0]) == 0
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
     assert_close(from_bf16(out), ref, what=f"prefill layer T={T}")
@@ -61,7 +61,7 @@ def test_prefill_hot_experts_span_tiles(layer):
     with ops.prefill_min_tokens(1):
         out, ids, _ = ops.moe_layer(to_bf16(x), lw.router, lw.experts, lw.shared, K,
                                     router_bias=torch.from_numpy(bias).cuda(), return_routing=True)
-    ref, ids_o, _ = O.moe_layer(x, from_bf16(lw.router), ex, sh, K, bias=bias)
+    ref, ids_o, _ = O.moe_layer(x, from_bf16(lw.router), ex, sh, K, bias=bias, rows_bf16=True)
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
     assert_close(from_bf16(out), ref, what="prefill hot experts")
 
@@ -82,7 +82,7 @@ def test_prefill_experts_other_geometry():
     with ops.prefill_min_tokens(1):
         routed, shared = ops.moe_experts(to_bf16(x), torch.from_numpy(ids).cuda(), to_bf16(w), ew)
     assert shared is None
-    ref, _ = O.moe_experts(x, ids, w, exo)
+    ref, _ = O.moe_experts(x, ids, w, exo, rows_bf16=True)
     assert_close(from_bf16(routed), ref, what="prefill experts E=8")
 
 
