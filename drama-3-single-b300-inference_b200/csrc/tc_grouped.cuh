@@ -9,7 +9,7 @@
 //            W2, K = I.
 // Warp roles (12 warps, three warpgroups):
 //   warp 0      TMA: A [128 x 128 B] and B [256 x 128 B] per 128-wide K block
-//               into a 3-stage (gate_up) / 4-stage (down) ring;
+//               into a 3-stage ring;
 //   warp 1      owns TMEM (512 columns = two 256-column accumulators) and
 //               issues 4 MMAs (M=128, N=256, K=32, kind::f8f6f4, E4M3 x E4M3
 //               -> fp32) per K block into one accumulator;
@@ -30,9 +30,9 @@
 //            thread) turn it into the row's 1x128 E4M3 scale and bytes and store
 //            them, while the promotion warps already work on the next tile;
 //   down     the promotion warps round the rows to bf16 (half the bytes of
-//            fp32 to store here and to read in the combine) and store them for
-//            the fixed-order combine through a small per-warp staging tile
-//            (coalesced stores).
+//            fp32 to store here and to read in the combine), put each row in
+//            shared memory and hand it to the bulk-copy engine, which stores it
+//            for the fixed-order combine while the warps go on to the next tile.
 #pragma once
 
 #include "d3_common.cuh"
@@ -78,10 +78,13 @@ constexpr int kTcABytes = 128 * 128;
 constexpr int kTcBBytes = 256 * 128;
 constexpr int kTcStageBytes = kTcABytes + kTcBBytes;
 constexpr int kTcMaxGroups = 1025;
+// down: staging row of one thread (128 bf16 columns + 16 bytes of padding,
+// which keeps the rows' 16-byte vector stores free of bank conflicts)
+constexpr int kTcDownStageRow = 272;
 
 template <int KIND>
 struct TcSmem {
-  static constexpr int kStages = KIND != TC_DOWN ? 3 : 4;
+  static constexpr int kStages = 3;
   static constexpr int kRing = kStages * kTcStageBytes;
   // full[S], empty[S], tfull[2], tempty[2], hfull, hempty
   static constexpr int kBars = kRing;
@@ -91,7 +94,7 @@ struct TcSmem {
   // gate_up: handoff tile [128 rows][32 chunks of 4 fp32] + row amax [2][128]
   // down:    staging tiles [8 warps][32 rows][4 chunks of 4 floats]
   static constexpr int kAux = (kPrefix + (kTcMaxGroups + 1) * 4 + 1023) / 1024 * 1024;
-  static constexpr int kAuxBytes = KIND != TC_DOWN ? 128 * 128 * 4 + 2 * 128 * 4 : 8 * 32 * 16 * 4;
+  static constexpr int kAuxBytes = KIND != TC_DOWN ? 128 * 128 * 4 + 2 * 128 * 4 : 8 * 32 * kTcDownStageRow;
   static constexpr size_t bytes() { return 1024 + kAux + kAuxBytes; }
 };
 static_assert(TcSmem<TC_GATE_UP>::bytes() <= 227 * 1024, "gate_up shared memory");
@@ -411,10 +414,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ffma2(acc1[16 * q + j], acc1[16 * q + j + 1], qb[q & 1][j], qb[q & 1][j + 1], f1);
           }
           if (q < 3) tc::tmem_ld_wait_regs(qa[(q + 1) & 1], qb[(q + 1) & 1]);
+          if (q == 2) {
+            // the last quarter is in registers: the accumulator is free for
+            // the MMA of K block kbc + 2 while that quarter is folded in
+            tc::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+          }
         }
-        tc::fence_before_thread_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
       }
       // ------------------------------------------------------ tile epilogue --
       if constexpr (KIND != TC_DOWN) {
@@ -447,42 +454,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(hfull);
       } else {
         // bf16 rows (the tcgen05 path rounds its per-expert down rows to bf16
-        // before the fixed-order combine) through a per-warp staging tile
-        // [32 rows][4 x 16 bytes] whose chunks are swizzled by (row >> 1) & 3
-        // (conflict-free vector stores by row and loads by chunk): each global
-        // store instruction writes 8 rows x 64 contiguous bytes; a thread's 128
-        // columns go out in 4 steps of 32
-        uint4* stgu = reinterpret_cast<uint4*>(aux) + ew * 32 * 4;
-        const int sr = lane >> 2, c4 = lane & 3;
-        __nv_bfloat16* obase = reinterpret_cast<__nv_bfloat16*>(args.out_rows) +
-                               static_cast<int64_t>(t.row0 + quad * 32) * args.out_ld + t.nt * 256 + 128 * wg;
+        // before the fixed-order combine). Thread = tile row: its 128 columns
+        // (acc0 then acc1) go to its own 256-byte row of the staging area and
+        // from there to global memory by one bulk copy, which runs while the
+        // warp goes on to the next tile. A row is rewritten only after its
+        // previous copy has read it (long done by then: a tile's K loop lies
+        // between). Rows past the group's end are neither staged nor stored.
+        uint8_t* srow = aux + (ew * 32 + lane) * kTcDownStageRow;
+        bulk_wait_read_all();
+        if (row < t.mvalid) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int j = 32 * (ch & 1) + 8 * c;
-            const float* src = ch < 2 ? acc0 + j : acc1 + j;
+          for (int c = 0; c < 16; ++c) {
+            const float* src = c < 8 ? acc0 + 8 * c : acc1 + 8 * (c - 8);
             uint32_t p[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const __nv_bfloat162 b = __floats2bfloat162_rn(src[2 * i], src[2 * i + 1]);
-              p[i] = *reinterpret_cast<const uint32_t*>(&b);
+              const __nv_bfloat162 v = __floats2bfloat162_rn(src[2 * i], src[2 * i + 1]);
+              p[i] = *reinterpret_cast<const uint32_t*>(&v);
             }
-            stgu[lane * 4 + (c ^ ((lane >> 1) & 3))] = make_uint4(p[0], p[1], p[2], p[3]);
+            *reinterpret_cast<uint4*>(srow + 16 * c) = make_uint4(p[0], p[1], p[2], p[3]);
           }
-          __syncwarp();
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int r = sr + 8 * q;
-            if (quad * 32 + r < t.mvalid)
-              *reinterpret_cast<uint4*>(obase + static_cast<int64_t>(r) * args.out_ld + 32 * ch + 8 * c4) =
-                  stgu[r * 4 + (c4 ^ ((r >> 1) & 3))];
-          }
-          __syncwarp();
+          fence_proxy_async_smem();
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out_rows) +
+                               static_cast<int64_t>(t.row0 + row) * args.out_ld + t.nt * 256 + 128 * wg;
+          bulk_store_s2g(dst, srow, 256);
+          bulk_commit();
         }
       }
       t = tn;
     }
+    // the staged rows must stay in place until their copies are done
+    if constexpr (KIND == TC_DOWN) bulk_wait_all();
   }
   tc::fence_before_thread_sync();
   __syncthreads();
