@@ -396,30 +396,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();  // the TMEM loads below are warp-collective
         tc::fence_after_thread_sync();
         const uint32_t tl = tbase + b * 256 + (static_cast<uint32_t>(quad * 32) << 16);
-        // four 16-column quarters of both runs, software-pipelined: the loads
-        // of quarter q+1 are in flight while quarter q is folded in
-        float qa[2][16], qb[2][16];
-        tc::tmem_ld_32x32b_x16(tl + c0, qa[0]);
-        tc::tmem_ld_32x32b_x16(tl + c1, qb[0]);
-        tc::tmem_ld_wait_regs(qa[0], qb[0]);
+        // two 32-column halves of both runs, each half's two loads waited for
+        // once (two TMEM round trips per K block)
+        float qa[32], qb[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (q < 3) {
-            tc::tmem_ld_32x32b_x16(tl + c0 + 16 * (q + 1), qa[(q + 1) & 1]);
-            tc::tmem_ld_32x32b_x16(tl + c1 + 16 * (q + 1), qb[(q + 1) & 1]);
-          }
-#pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            ffma2(acc0[16 * q + j], acc0[16 * q + j + 1], qa[q & 1][j], qa[q & 1][j + 1], f0);
-            ffma2(acc1[16 * q + j], acc1[16 * q + j + 1], qb[q & 1][j], qb[q & 1][j + 1], f1);
-          }
-          if (q < 3) tc::tmem_ld_wait_regs(qa[(q + 1) & 1], qb[(q + 1) & 1]);
-          if (q == 2) {
-            // the last quarter is in registers: the accumulator is free for
-            // the MMA of K block kbc + 2 while that quarter is folded in
+        for (int h = 0; h < 2; ++h) {
+          tc::tmem_ld_32x32b_x32(tl + c0 + 32 * h, qa);
+          tc::tmem_ld_32x32b_x32(tl + c1 + 32 * h, qb);
+          tc::tmem_ld_wait_regs(qa, qb);
+          if (h == 1) {
+            // the last half is in registers: the accumulator is free for the
+            // MMA of K block kbc + 2 while that half is folded in
             tc::fence_before_thread_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            ffma2(acc0[32 * h + j], acc0[32 * h + j + 1], qa[j], qa[j + 1], f0);
+            ffma2(acc1[32 * h + j], acc1[32 * h + j + 1], qb[j], qb[j + 1], f1);
           }
         }
       }
