@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(kRtThreads)
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
+        if (h == 1 && nr <= 8) break;  // the tile's rows 8..15 do not exist (the last tile of R = E + 1)
         uint32_t ww[8][4];
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
