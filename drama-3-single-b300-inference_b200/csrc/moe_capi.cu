@@ -211,8 +211,7 @@ int check_experts(const d3_experts_t* e, const char* what) {
   return D3_OK;
 }
 
-// Steps 1-5 on an already carved workspace. ids/weights are device tensors
-// [T,k]; gate (nullable) feeds the shared-expert combine.
+// Residual update and RMSNorm fused into the combine (the layer exit).
 struct AddNorm {
   void* residual = nullptr;         // bf16 [T (or T_out), H], updated in place
   const void* weight = nullptr;     // bf16 [H]
@@ -246,12 +245,33 @@ struct PreQuant {
   int transposed = 0;
 };
 
-int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
-                int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
-                int64_t gate_stride, void* routed_out, void* shared_out, void* out,
-                const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted,
-                const AddNorm& an = AddNorm{}, const RowGather& rg = RowGather{},
-                const PreQuant& pq = PreQuant{}) {
+// Whether the expert GEMMs of a T-token call run on tcgen05 (prefill) or on
+// the decode engine. Both stages of a call take this decision the same way,
+// so the threshold must not change between them.
+bool use_tc(int T, int H) { return T >= prefill_min_tokens() && H % 256 == 0; }
+
+TcArgs tc_common(const MoeBuffers& b, int E, int I, int T, int P, int R, int has_shared,
+                 int32_t* status) {
+  TcArgs a{};
+  a.counts = b.counts;
+  a.starts = b.starts;
+  a.E = E;
+  a.has_shared = has_shared;
+  a.shared_row0 = P;
+  a.shared_count = T;
+  a.act_rows = R;
+  a.I = I;
+  a.status = status;
+  return a;
+}
+
+// Steps 1-3 on an already carved workspace: the bucketing (unless done),
+// x into expert order as e4m3 (or pre-quantised rows copied there), and
+// gate_up + SiLU*mul + FP8 requant into b.a / b.sa.
+int experts_up(const void* x, int64_t x_stride, const int64_t* ids, int T, int k,
+               const d3_experts_t* ex, const d3_experts_t* sh, const MoeBuffers& b,
+               int32_t* status, cudaStream_t s, bool permuted, const RowGather& rg,
+               const PreQuant& pq) {
   const int E = ex->E, I = ex->I, H = ex->H;
   const int P = T * k;
   const int has_shared = sh ? 1 : 0;
@@ -273,18 +293,9 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
 
   const int sms = sm_count();
   stage_mark(1, s);
-  if (T >= prefill_min_tokens() && H % 256 == 0) {
-    // ---- prefill: both expert GEMMs on tcgen05
-    TcArgs a{};
-    a.counts = b.counts;
-    a.starts = b.starts;
-    a.E = E;
-    a.has_shared = has_shared;
-    a.shared_row0 = P;
-    a.shared_count = T;
-    a.act_rows = R;
-    a.I = I;
-    a.status = status;
+  if (use_tc(T, H)) {
+    // ---- prefill: tcgen05
+    TcArgs a = tc_common(b, E, I, T, P, R, has_shared, status);
     {
       CUtensorMap tw, twsh, ta;
       if ((rc = encode_tmap_2d(&tw, ex->w13, 1, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128))) return rc;
@@ -306,7 +317,68 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
                : launch_tc<TC_GATE_UP>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s);
       if (rc) return rc;
     }
-    stage_mark(2, s);
+  } else {
+    // ---- gate_up
+    {
+      CUtensorMap tw, twsh, ta;
+      if ((rc = encode_tmap_2d(&tw, ex->w13, 1, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w13 : ex->w13, 1, H,
+                               static_cast<uint64_t>(2) * I, H, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&ta, b.xq, 1, H, R, H, 128, 16))) return rc;
+      EngineArgs a{};
+      a.counts = b.counts;
+      a.starts = b.starts;
+      a.active = b.active;
+      a.n_active = b.n_active;
+      a.num_experts = E;
+      // gate_up keeps two accumulator sets (gate, up): at most 4 token chunks
+      // (32 tokens) per group fit the 168 registers a 9-warp CTA gets
+      const int nch = nch_for(T) < 4 ? nch_for(T) : 4;
+      a.shared_chunk = nch * 8;
+      a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
+      a.shared_row0 = P;
+      a.shared_count = T;
+      a.tiles = I / 128;
+      a.KB = H / 128;
+      a.ksplit = 1;
+      a.kb_per_split = a.KB;
+      a.rows_per_expert = 2 * I;
+      a.first_off = gate_first_row(ex);
+      a.up_offset = up_minus_gate(ex);
+      a.wscale = ex->s13;
+      a.wscale_sh = has_shared ? sh->s13 : ex->s13;
+      a.act_scale = b.sx;
+      a.out_q = b.a;
+      a.out_qs = b.sa;
+      a.out_cols = I;
+      a.status = status;
+      a.work_counter = b.work;
+      const int max_items = (E + a.shared_groups) * (I / 128);
+      const int grid = max_items < sms ? max_items : sms;
+      rc = launch_engine<EPI_GATE_UP, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s);
+      if (rc) return rc;
+    }
+  }
+  stage_mark(2, s);
+  return D3_OK;
+}
+
+// Steps 4-5: down into b.d and the fixed-order combine, or the combine fused
+// with the layer exit.
+int experts_down(const void* weights, int T, int k, const d3_experts_t* ex,
+                 const d3_experts_t* sh, const void* gate, int64_t gate_stride, void* routed_out,
+                 void* shared_out, void* out, const MoeBuffers& b, int32_t* status,
+                 cudaStream_t s, const AddNorm& an) {
+  const int E = ex->E, I = ex->I, H = ex->H;
+  const int P = T * k;
+  const int has_shared = sh ? 1 : 0;
+  const int R = P + (has_shared ? T : 0);
+  const int sms = sm_count();
+  const bool tc = use_tc(T, H);
+  int rc = D3_OK;
+  if (tc) {
+    // ---- prefill: tcgen05, bf16 rows
+    TcArgs a = tc_common(b, E, I, T, P, R, has_shared, status);
     {
       CUtensorMap tw, twsh, ta;
       if ((rc = encode_tmap_2d(&tw, ex->w2, 1, I, static_cast<uint64_t>(E) * H, I, 128, 128))) return rc;
@@ -327,96 +399,65 @@ int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void*
       rc = launch_tc<TC_DOWN>(ta, tw, twsh, a, tc_grid(R, E + has_shared, a.ntiles, sms), s);
       if (rc) return rc;
     }
-    stage_mark(3, s);
-    rc = finish_layer(b, H, weights, T, k, has_shared, gate, gate_stride, routed_out, shared_out,
-                      out, an, s, true);
-    stage_mark(4, s);
-    return rc;
-  }
-  // ---- gate_up
-  {
-    CUtensorMap tw, twsh, ta;
-    if ((rc = encode_tmap_2d(&tw, ex->w13, 1, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128))) return rc;
-    if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w13 : ex->w13, 1, H,
-                             static_cast<uint64_t>(2) * I, H, 128, 128))) return rc;
-    if ((rc = encode_tmap_2d(&ta, b.xq, 1, H, R, H, 128, 16))) return rc;
-    EngineArgs a{};
-    a.counts = b.counts;
-    a.starts = b.starts;
-    a.active = b.active;
-    a.n_active = b.n_active;
-    a.num_experts = E;
-    // gate_up keeps two accumulator sets (gate, up): at most 4 token chunks
-    // (32 tokens) per group fit the 168 registers a 9-warp CTA gets
-    const int nch = nch_for(T) < 4 ? nch_for(T) : 4;
-    a.shared_chunk = nch * 8;
-    a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
-    a.shared_row0 = P;
-    a.shared_count = T;
-    a.tiles = I / 128;
-    a.KB = H / 128;
-    a.ksplit = 1;
-    a.kb_per_split = a.KB;
-    a.rows_per_expert = 2 * I;
-    a.first_off = gate_first_row(ex);
-    a.up_offset = up_minus_gate(ex);
-    a.wscale = ex->s13;
-    a.wscale_sh = has_shared ? sh->s13 : ex->s13;
-    a.act_scale = b.sx;
-    a.out_q = b.a;
-    a.out_qs = b.sa;
-    a.out_cols = I;
-    a.status = status;
-    a.work_counter = b.work;
-    const int max_items = (E + a.shared_groups) * (I / 128);
-    const int grid = max_items < sms ? max_items : sms;
-    rc = launch_engine<EPI_GATE_UP, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s);
-    if (rc) return rc;
-  }
-  stage_mark(2, s);
-  // ---- down
-  {
-    CUtensorMap tw, twsh, ta;
-    if ((rc = encode_tmap_2d(&tw, ex->w2, 1, I, static_cast<uint64_t>(E) * H, I, 128, 128))) return rc;
-    if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w2 : ex->w2, 1, I, H, I, 128, 128))) return rc;
-    if ((rc = encode_tmap_2d(&ta, b.a, 1, I, R, I, 128, 16))) return rc;
-    EngineArgs a{};
-    a.counts = b.counts;
-    a.starts = b.starts;
-    a.active = b.active;
-    a.n_active = b.n_active;
-    a.num_experts = E;
-    // pairs of 128-row tiles per item when H allows (two accumulator sets:
-    // at most 4 token chunks per group, like gate_up)
-    const bool pair = H % 256 == 0;
-    const int nch = pair ? (nch_for(T) < 4 ? nch_for(T) : 4) : nch_for(T);
-    a.shared_chunk = nch * 8;
-    a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
-    a.shared_row0 = P;
-    a.shared_count = T;
-    a.tiles = pair ? H / 256 : H / 128;
-    a.KB = I / 128;
-    a.ksplit = 1;
-    a.kb_per_split = a.KB;
-    a.rows_per_expert = H;
-    a.wscale = ex->s2;
-    a.wscale_sh = has_shared ? sh->s2 : ex->s2;
-    a.act_scale = b.sa;
-    a.out_rows = b.d;
-    a.out_ld = H;
-    a.status = status;
-    a.work_counter = b.work + 1;
-    const int max_items = (E + a.shared_groups) * a.tiles;
-    const int grid = max_items < sms ? max_items : sms;
-    rc = pair ? launch_engine<EPI_DOWN2, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s)
-              : launch_engine<EPI_DOWN, false, kStagesDown>(nch, tw, twsh, ta, a, grid, s);
-    if (rc) return rc;
+  } else {
+    // ---- down
+    {
+      CUtensorMap tw, twsh, ta;
+      if ((rc = encode_tmap_2d(&tw, ex->w2, 1, I, static_cast<uint64_t>(E) * H, I, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&twsh, has_shared ? sh->w2 : ex->w2, 1, I, H, I, 128, 128))) return rc;
+      if ((rc = encode_tmap_2d(&ta, b.a, 1, I, R, I, 128, 16))) return rc;
+      EngineArgs a{};
+      a.counts = b.counts;
+      a.starts = b.starts;
+      a.active = b.active;
+      a.n_active = b.n_active;
+      a.num_experts = E;
+      // pairs of 128-row tiles per item when H allows (two accumulator sets:
+      // at most 4 token chunks per group, like gate_up)
+      const bool pair = H % 256 == 0;
+      const int nch = pair ? (nch_for(T) < 4 ? nch_for(T) : 4) : nch_for(T);
+      a.shared_chunk = nch * 8;
+      a.shared_groups = has_shared ? (T + a.shared_chunk - 1) / a.shared_chunk : 0;
+      a.shared_row0 = P;
+      a.shared_count = T;
+      a.tiles = pair ? H / 256 : H / 128;
+      a.KB = I / 128;
+      a.ksplit = 1;
+      a.kb_per_split = a.KB;
+      a.rows_per_expert = H;
+      a.wscale = ex->s2;
+      a.wscale_sh = has_shared ? sh->s2 : ex->s2;
+      a.act_scale = b.sa;
+      a.out_rows = b.d;
+      a.out_ld = H;
+      a.status = status;
+      a.work_counter = b.work + 1;
+      const int max_items = (E + a.shared_groups) * a.tiles;
+      const int grid = max_items < sms ? max_items : sms;
+      rc = pair ? launch_engine<EPI_DOWN2, false, kStagesGateUp>(nch, tw, twsh, ta, a, grid, s)
+                : launch_engine<EPI_DOWN, false, kStagesDown>(nch, tw, twsh, ta, a, grid, s);
+      if (rc) return rc;
+    }
   }
   stage_mark(3, s);
   rc = finish_layer(b, H, weights, T, k, has_shared, gate, gate_stride, routed_out, shared_out, out,
-                    an, s);
+                    an, s, tc);
   stage_mark(4, s);
   return rc;
+}
+
+// Steps 1-5: ids/weights are device tensors [T,k]; gate (nullable) feeds the
+// shared-expert combine.
+int run_experts(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
+                int k, const d3_experts_t* ex, const d3_experts_t* sh, const void* gate,
+                int64_t gate_stride, void* routed_out, void* shared_out, void* out,
+                const MoeBuffers& b, int32_t* status, cudaStream_t s, bool permuted,
+                const AddNorm& an = AddNorm{}, const RowGather& rg = RowGather{},
+                const PreQuant& pq = PreQuant{}) {
+  int rc = experts_up(x, x_stride, ids, T, k, ex, sh, b, status, s, permuted, rg, pq);
+  if (rc) return rc;
+  return experts_down(weights, T, k, ex, sh, gate, gate_stride, routed_out, shared_out, out, b,
+                      status, s, an);
 }
 
 }  // namespace
@@ -485,6 +526,41 @@ extern "C" int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* id
   stage_mark(0, s);
   return run_experts(x, x_stride, ids, weights, T, k, experts, shared, nullptr, 0, routed_out,
                      shared_out, nullptr, b, status ? status : b.status, s, false);
+}
+
+extern "C" int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_t* ids, int T,
+                                   int k, const d3_experts_t* experts, const d3_experts_t* shared,
+                                   void* workspace, size_t workspace_bytes, int32_t* status,
+                                   d3_stream_t stream) {
+  int rc = check_common(x, x_stride, T, k, experts, shared, workspace, workspace_bytes,
+                        "moe_gate_up_silu");
+  if (rc) return rc;
+  D3_REQUIRE(ids != nullptr, "moe_gate_up_silu: null ids");
+  if (T == 0) return D3_OK;
+  auto b = carve_moe(workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr, 1);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  stage_mark(0, s);
+  return experts_up(x, x_stride, ids, T, k, experts, shared, b, status ? status : b.status, s,
+                    false, RowGather{}, PreQuant{});
+}
+
+extern "C" int d3_moe_down_combine(const void* weights, int T, int k, const d3_experts_t* experts,
+                                   const d3_experts_t* shared, void* routed_out, void* shared_out,
+                                   void* workspace, size_t workspace_bytes, int32_t* status,
+                                   d3_stream_t stream) {
+  D3_REQUIRE(experts != nullptr, "moe_down_combine: expert weights missing");
+  // no input rows here: the checks of the shared entry point run with x absent
+  int rc = check_common(nullptr, experts->H, T, k, experts, shared, workspace, workspace_bytes,
+                        "moe_down_combine");
+  if (rc) return rc;
+  D3_REQUIRE(weights && routed_out, "moe_down_combine: null weights or output");
+  D3_REQUIRE(aligned(routed_out, 16) && (!shared_out || aligned(shared_out, 16)),
+             "moe_down_combine: outputs must be 16-byte aligned");
+  if (T == 0) return D3_OK;
+  auto b = carve_moe(workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr, 1);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return experts_down(weights, T, k, experts, shared, nullptr, 0, routed_out, shared_out, nullptr,
+                      b, status ? status : b.status, s, AddNorm{});
 }
 
 extern "C" int d3_moe_experts_fp8(const uint8_t* q, int64_t q_stride, const float* q_scales,

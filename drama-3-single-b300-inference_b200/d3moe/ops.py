@@ -385,6 +385,54 @@ def moe_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
     return routed, shared_out
 
 
+def moe_gate_up_silu(x: torch.Tensor, topk_ids: torch.Tensor, experts, shared=None,
+                     workspace: torch.Tensor | None = None,
+                     status: torch.Tensor | None = None) -> torch.Tensor:
+    """First stage of moe_experts: the pairs bucketed by expert, x quantised
+    into expert order, gate_up + SiLU*mul + FP8 requant (the reference's
+    expert_up_kernel and silu_mul_quant, src/drama3/kernels.py:290-301, 344).
+    Returns the workspace that holds the activations; moe_down_combine reads
+    them from it with the same routing, experts and shared expert."""
+    _require_cuda(x, topk_ids)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("x must be bfloat16")
+    ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
+    sv = None if shared is None else (shared if isinstance(shared, ExpertView) else ExpertView(shared))
+    T, H = x.shape
+    if H != ev.H:
+        raise ValueError(f"hidden size {H} != expert H {ev.H}")
+    if topk_ids.dtype != torch.int64 or not topk_ids.is_contiguous() or topk_ids.shape[0] != T:
+        raise ValueError("topk_ids must be contiguous int64 [T, k]")
+    k = topk_ids.shape[1]
+    if workspace is None:
+        workspace = moe_workspace(T, k, ev.E, ev.I, ev.H, sv is not None, x.device)
+    call("d3_moe_gate_up_silu", x.data_ptr(), _row_stride(x), topk_ids.data_ptr(), T, k,
+         ctypes.byref(ev.struct), ctypes.byref(sv.struct) if sv is not None else None,
+         workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(x.device))
+    return workspace
+
+
+def moe_down_combine(topk_weights: torch.Tensor, workspace: torch.Tensor, experts, shared=None,
+                     status: torch.Tensor | None = None):
+    """Second stage of moe_experts, from the workspace moe_gate_up_silu filled:
+    down GEMM and the fixed-order combine (src/drama3/kernels.py:304-322).
+    Returns (routed, shared|None) like moe_experts, bit for bit."""
+    _require_cuda(topk_weights, workspace)
+    ev = experts if isinstance(experts, ExpertView) else ExpertView(experts)
+    sv = None if shared is None else (shared if isinstance(shared, ExpertView) else ExpertView(shared))
+    if topk_weights.dim() != 2:
+        raise ValueError("topk_weights must be [T, k]")
+    T, k = topk_weights.shape
+    topk_weights = topk_weights.to(torch.bfloat16).contiguous()
+    routed = torch.empty((T, ev.H), dtype=torch.bfloat16, device=topk_weights.device)
+    shared_out = (torch.empty((T, ev.H), dtype=torch.bfloat16, device=topk_weights.device)
+                  if sv is not None else None)
+    call("d3_moe_down_combine", topk_weights.data_ptr(), T, k, ctypes.byref(ev.struct),
+         ctypes.byref(sv.struct) if sv is not None else None, routed.data_ptr(), _ptr(shared_out),
+         workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(topk_weights.device))
+    return routed, shared_out
+
+
 def moe_experts_fp8(q: torch.Tensor, scales: torch.Tensor, topk_ids: torch.Tensor,
                     topk_weights: torch.Tensor, experts, transposed: bool = True,
                     workspace: torch.Tensor | None = None, status: torch.Tensor | None = None):

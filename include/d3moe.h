@@ -265,6 +265,26 @@ D3_API int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* ids, c
                    void* routed_out, void* shared_out, void* workspace, size_t workspace_bytes,
                    int32_t* status, d3_stream_t stream);
 
+/* The two stages of d3_moe_experts as separate calls, for callers that
+ * schedule other work between the expert GEMMs (the reference's decode path
+ * runs expert_up_kernel, then the down kernel: src/drama3/kernels.py:290-322,
+ * 344-350; FlashInfer's FC1 / FC2 split in trtllm_fp8_block_scale_moe).
+ * d3_moe_gate_up_silu buckets the pairs, quantises x into expert order and
+ * runs gate_up + SiLU*mul + FP8 requant; the activations stay in `workspace`.
+ * d3_moe_down_combine then runs the down GEMM and the fixed-order combine
+ * from that workspace and writes routed_out (and shared_out with a shared
+ * expert). Both calls take the same T, k, experts, shared and workspace, on
+ * the same stream, with the prefill threshold unchanged in between; the pair
+ * gives d3_moe_experts' outputs bit for bit. */
+D3_API int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_t* ids, int T, int k,
+                               const d3_experts_t* experts, const d3_experts_t* shared,
+                               void* workspace, size_t workspace_bytes, int32_t* status,
+                               d3_stream_t stream);
+D3_API int d3_moe_down_combine(const void* weights, int T, int k, const d3_experts_t* experts,
+                               const d3_experts_t* shared, void* routed_out, void* shared_out,
+                               void* workspace, size_t workspace_bytes, int32_t* status,
+                               d3_stream_t stream);
+
 /* Routed experts over already-quantised activations, the calling convention
  * of FlashInfer's trtllm_fp8_block_scale_moe (src/drama3/model.py:544-580):
  * q e4m3 [T,H] (row stride q_stride bytes, a multiple of 16), q_scales f32
