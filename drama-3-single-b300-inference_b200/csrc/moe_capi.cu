@@ -528,6 +528,46 @@ extern "C" int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* id
                      shared_out, nullptr, b, status ? status : b.status, s, false);
 }
 
+namespace {
+// Host-side record of the workspaces d3_moe_gate_up_silu filled, with the
+// call's shape, so that d3_moe_down_combine refuses a workspace whose bucketing
+// and activations it would otherwise read unchecked (garbage counts or rows
+// would send its kernels' stores anywhere). The record costs no device work
+// and no synchronisation; it does not see device-side reuse of the workspace
+// by other calls between the two stages, which the caller must avoid.
+struct StageRecord {
+  const void* ws;
+  int T, k, E, I, H, has_shared;
+  bool operator==(const StageRecord& o) const {
+    return ws == o.ws && T == o.T && k == o.k && E == o.E && I == o.I && H == o.H &&
+           has_shared == o.has_shared;
+  }
+};
+constexpr size_t kMaxStageRecords = 64;
+std::mutex g_stage_mutex;
+StageRecord g_stage_records[kMaxStageRecords];
+size_t g_stage_count = 0, g_stage_next = 0;
+
+void stage_record(const StageRecord& r) {
+  std::lock_guard<std::mutex> lock(g_stage_mutex);
+  for (size_t i = 0; i < g_stage_count; ++i)
+    if (g_stage_records[i].ws == r.ws) {
+      g_stage_records[i] = r;
+      return;
+    }
+  g_stage_records[g_stage_next] = r;  // oldest record replaced once the table is full
+  g_stage_next = (g_stage_next + 1) % kMaxStageRecords;
+  if (g_stage_count < kMaxStageRecords) ++g_stage_count;
+}
+
+bool stage_recorded(const StageRecord& r) {
+  std::lock_guard<std::mutex> lock(g_stage_mutex);
+  for (size_t i = 0; i < g_stage_count; ++i)
+    if (g_stage_records[i] == r) return true;
+  return false;
+}
+}  // namespace
+
 extern "C" int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_t* ids, int T,
                                    int k, const d3_experts_t* experts, const d3_experts_t* shared,
                                    void* workspace, size_t workspace_bytes, int32_t* status,
@@ -540,8 +580,11 @@ extern "C" int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_
   auto b = carve_moe(workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr, 1);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   stage_mark(0, s);
-  return experts_up(x, x_stride, ids, T, k, experts, shared, b, status ? status : b.status, s,
-                    false, RowGather{}, PreQuant{});
+  rc = experts_up(x, x_stride, ids, T, k, experts, shared, b, status ? status : b.status, s, false,
+                  RowGather{}, PreQuant{});
+  if (rc == D3_OK)
+    stage_record({workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr});
+  return rc;
 }
 
 extern "C" int d3_moe_down_combine(const void* weights, int T, int k, const d3_experts_t* experts,
@@ -554,6 +597,11 @@ extern "C" int d3_moe_down_combine(const void* weights, int T, int k, const d3_e
                         "moe_down_combine");
   if (rc) return rc;
   D3_REQUIRE(weights && routed_out, "moe_down_combine: null weights or output");
+  D3_REQUIRE(T == 0 || stage_recorded({workspace, T, k, experts->E, experts->I, experts->H,
+                                       shared != nullptr}),
+             "moe_down_combine: the workspace was not filled by d3_moe_gate_up_silu with T=%d, "
+             "k=%d, E=%d, I=%d, H=%d and %s shared expert", T, k, experts->E, experts->I,
+             experts->H, shared ? "a" : "no");
   D3_REQUIRE(aligned(routed_out, 16) && (!shared_out || aligned(shared_out, 16)),
              "moe_down_combine: outputs must be 16-byte aligned");
   if (T == 0) return D3_OK;

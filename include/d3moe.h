@@ -275,7 +275,11 @@ D3_API int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* ids, c
  * from that workspace and writes routed_out (and shared_out with a shared
  * expert). Both calls take the same T, k, experts, shared and workspace, on
  * the same stream, with the prefill threshold unchanged in between; the pair
- * gives d3_moe_experts' outputs bit for bit. */
+ * gives d3_moe_experts' outputs bit for bit. d3_moe_down_combine returns
+ * D3_EINVAL for a workspace that d3_moe_gate_up_silu has not filled with the
+ * same T, k, expert shapes and shared expert (a host-side record, no device
+ * work); other use of the workspace between the two calls is the caller's to
+ * avoid. */
 D3_API int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_t* ids, int T, int k,
                                const d3_experts_t* experts, const d3_experts_t* shared,
                                void* workspace, size_t workspace_bytes, int32_t* status,

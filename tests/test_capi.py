@@ -84,6 +84,19 @@ def test_invalid_arguments_fail_before_launch(lib):
     assert b"multiples of 128" in lib.d3_last_error_string()
 
 
+def test_down_stage_refuses_an_unfilled_workspace(lib):
+    """d3_moe_down_combine checks its host-side record of the first stage
+    before anything reaches the device."""
+    from d3moe import _lib
+    ex = _lib.D3Experts(16, 16, 16, 16, 128, 768, 2048)
+    need = ctypes.c_size_t()
+    assert lib.d3_moe_workspace_size(4, 8, 128, 768, 2048, 0, ctypes.byref(need)) == 0
+    rc = lib.d3_moe_down_combine(16, 4, 8, ctypes.byref(ex), None, 256, None, 4096, need.value,
+                                 None, None)
+    assert rc == _lib.D3_EINVAL
+    assert b"not filled by d3_moe_gate_up_silu" in lib.d3_last_error_string()
+
+
 def test_python_wrappers_reject_cpu_tensors():
     torch = pytest.importorskip("torch")
     from d3moe import kernels, moe_input
