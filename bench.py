@@ -52,18 +52,64 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) during the timed region."""
+    """SM clock and throttle reasons during the timed region. NVML is read
+    every 5 ms from a thread, the first sample before the region starts, so a
+    region of a few tens of milliseconds still gets several samples; without
+    NVML it falls back to `nvidia-smi -lms 200`. Read-only: nothing is set."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.stop = threading.Event()
         self.lines: list[str] = []
+        self.samples: list[tuple[float, float, frozenset]] = []
+
+    def _nvml(self):
+        import pynvml as nv
+        import torch
+        nv.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.gpu)
+            h = nv.nvmlDeviceGetHandleByPciBusId(
+                f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+        except Exception:
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+        bits = dict(zip(self.NAMES, (nv.nvmlClocksEventReasonHwSlowdown,
+                                     nv.nvmlClocksEventReasonHwThermalSlowdown,
+                                     nv.nvmlClocksEventReasonSwThermalSlowdown,
+                                     nv.nvmlClocksEventReasonSwPowerCap)))
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        return nv, h, bits, mx
 
     def __enter__(self):
+        try:
+            nv, h, bits, mx = self._nvml()
+
+            def run():
+                while True:
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((sm, mx, frozenset(n for n, b in bits.items() if r & b)))
+                    except Exception:
+                        pass
+                    if self.stop.wait(0.005):
+                        return
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 1.0:
+                time.sleep(0.001)
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -80,6 +126,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=1.0)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -89,7 +138,10 @@ class ClockSampler:
 
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s_mhz, m_mhz, rs in self.samples:
+            sm.append(s_mhz)
+            mx = m_mhz
+            reasons |= rs
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
@@ -99,11 +151,12 @@ class ClockSampler:
                 mx = float(parts[2])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(self.NAMES, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml, 5 ms" if self.samples else "nvidia-smi, 200 ms"}
 
 
 def algorithmic_bytes(ids_host, T: int) -> dict:
