@@ -9,7 +9,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from helpers import (assert_close, experts_to_oracle, fp8_bytes, from_bf16, to_bf16,  # noqa: E402
+from helpers import (assert_close, fp8_bytes, from_bf16, to_bf16,  # noqa: E402
                      to_fp8, ulps_bf16)
 from oracle import moe_oracle as O  # noqa: E402
 
