@@ -125,6 +125,7 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i32, _i32, ctypes.POINTER(D3Experts), ctypes.POINTER(D3Experts), _c_void_p,
          _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
+    "d3_wait_timeout_probe": (_i32, [_c_void_p, _c_void_p]),
     "d3_set_stage_events": (_i32, [ctypes.POINTER(_c_void_p), _i32]),
     "d3_set_prefill_min_tokens": (_i32, [_i32]),
     "d3_ep_plan": (

@@ -58,6 +58,12 @@ typedef struct CUstream_st* d3_stream_t; /* == cudaStream_t */
 D3_API int d3_version(void);
 D3_API const char* d3_last_error_string(void);
 
+/* Self-test of the bounded-wait failure path: one thread waits, through the
+ * same bounded wait every waiting kernel uses, on a barrier nothing arrives
+ * on; after the wait limit (2 s) the kernel writes D3_STATUS_WAIT_TIMEOUT to
+ * *status (device int32) and exits. No fault, and the context stays usable. */
+D3_API int d3_wait_timeout_probe(int32_t* status, d3_stream_t stream);
+
 /* ------------------------------------------------------------- (a3) quant --
  * Activation FP8 quantisation per 1x128 group: scale = max(amax,1e-10)/448,
  * q = e4m3(clamp(x/scale, -448, 448)) with IEEE division and round-to-nearest-
