@@ -42,6 +42,12 @@ sys.path.insert(0, str(PKG))
 E, I, H, TOPK = 128, 768, 2048, 8
 N_QKV, N_O = 4096, 2048
 
+# DRAM traffic of one gate_up launch of the default decode step, as ncu
+# measured it (not measured by this script; see the profile named here).
+GATE_UP_TRAFFIC_BYTES = 404.28e6
+GATE_UP_TRAFFIC_SOURCE = ("profiles/expert_gemv_T64_full.md: dram__bytes_read.sum + "
+                          "dram__bytes_write.sum of the gate_up launch, ncu --set full")
+
 
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -506,24 +512,25 @@ def prefill_lengths() -> list[int]:
     return [int(v) for v in np.random.default_rng(3).integers(16, 513, size=64)]
 
 
-def run_prefill(args, dev) -> None:
-    """One FP8 MoE layer over a ragged prefill batch (all prompts' tokens in one
-    call), Zipf(1.1) router bias for hot experts. Expert GEMMs run on the
-    tcgen05 grouped kernel; the roofline line reports its tensor throughput
-    against the FP8 dense peak (2x the measured bf16 GEMM peak)."""
+def measure_prefill(dev, lens: list[int], steps: int, warmup: int, seed: int = 3,
+                    router_bias: str | None = "zipf", cpu_seconds: float = 0.0) -> dict:
+    """One FP8 MoE layer over a prefill batch (all prompts' tokens in one
+    call). Expert GEMMs run on the tcgen05 grouped kernel; the roofline
+    reports its tensor throughput against the FP8 dense peak (2x the measured
+    bf16 GEMM peak). Two weight sets alternate between steps."""
     import numpy as np
     import torch
 
     from d3moe import _lib, ops, synth
 
-    lens = [args.prefill_tokens] if args.prefill_tokens > 0 else prefill_lengths()
     T = sum(lens)
     lib = _lib.load()
-    layers = [synth.make_layer(E, I, H, seed=3 + li, device=dev, router_bias="zipf") for li in range(2)]
+    layers = [synth.make_layer(E, I, H, seed=seed + li, device=dev, router_bias=router_bias)
+              for li in range(2)]
     views = [(ops.ExpertView(l.experts), ops.ExpertView(l.shared)) for l in layers]
     ws = ops.moe_workspace(T, TOPK, E, I, H, True, dev)
     gin = torch.Generator(device=dev)
-    gin.manual_seed(3)
+    gin.manual_seed(seed)
     xs = torch.randn((2, T, H), generator=gin, device=dev).to(torch.bfloat16)
     y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     ids = torch.empty((T, TOPK), dtype=torch.int64, device=dev)
@@ -540,49 +547,50 @@ def run_prefill(args, dev) -> None:
                   ctypes.byref(sv.struct), y.data_ptr(), None if ids_out is None else ids_out.data_ptr(),
                   None, ws.data_ptr(), ws.numel(), status.data_ptr(), sptr)
 
-    stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(steps)]
     for evs in stage_events:
         for e in evs:
             e.record(stream)
     stage_arrays = [(ctypes.c_void_p * 5)(*[e._as_parameter_.value for e in evs]) for evs in stage_events]
-    for i in range(args.warmup):
-        step(i, xs[i % 2])
-    torch.cuda.synchronize(dev)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index or 0) as clocks:
-        start.record(stream)
-        for i in range(args.steps):
-            lib.d3_set_stage_events(stage_arrays[i], 5)
-            step(i, xs[i % 2], ids if i == 0 else None)
-            lib.d3_set_stage_events(None, 0)
-        end.record(stream)
+    with ops.prefill_min_tokens(1024):
+        for i in range(warmup):
+            step(i, xs[i % 2])
         torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index or 0) as clocks:
+            start.record(stream)
+            for i in range(steps):
+                lib.d3_set_stage_events(stage_arrays[i], 5)
+                step(i, xs[i % 2], ids if i == 0 else None)
+                lib.d3_set_stage_events(None, 0)
+            end.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = start.elapsed_time(end) / steps
+
+            # end to end through the C ABI with host buffers
+            hx = xs[0].cpu().pin_memory()
+            hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+            dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+            for i in range(2):
+                dx.copy_(hx, non_blocking=True)
+                step(i, dx)
+                hy.copy_(y, non_blocking=True)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(steps):
+                dx.copy_(hx, non_blocking=True)
+                step(i, dx)
+                hy.copy_(y, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            e2e_ms = e0.elapsed_time(e1) / steps
     if int(status.item()) != 0:
         raise RuntimeError(f"device status word {int(status.item())}: a bounded wait timed out")
-    ms = start.elapsed_time(end) / args.steps
     gate_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in stage_events)
     down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in stage_events)
     pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in stage_events)
     post_ms = statistics.mean(e[3].elapsed_time(e[4]) for e in stage_events)
-
-    # end to end through the C ABI with host buffers
-    hx = xs[0].cpu().pin_memory()
-    hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-    dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    for i in range(2):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx)
-        hy.copy_(y, non_blocking=True)
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx)
-        hy.copy_(y, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1) / args.steps
 
     R = T * TOPK + T
     gate_flops = 2.0 * R * (2 * I) * H
@@ -591,13 +599,14 @@ def run_prefill(args, dev) -> None:
     fp8_peak = 2.0 * pk["bf16_tflops"]
     achieved = gate_flops / (gate_ms * 1e-3) / 1e12
     counts = np.bincount(ids.cpu().numpy().reshape(-1), minlength=E)
+    ragged = len(lens) > 1
     line = {
         "metric": "fp8_moe_layer_prefill_tokens_per_s",
         "value": T / (ms * 1e-3),
         "unit": "tokens/s",
         "n_gpus": 1,
-        "steps": args.steps,
-        "warmup": args.warmup,
+        "steps": steps,
+        "warmup": warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
@@ -605,9 +614,11 @@ def run_prefill(args, dev) -> None:
         "dtype": "fp8_e4m3 x fp8_e4m3 -> f32 (tcgen05 kind::f8f6f4)",
         "data": "synthetic",
         "config": {
-            "workload": (f"prefill: 64 ragged prompts uniform in [16,512] (seed 3), T={T} tokens"
-                         if args.prefill_tokens <= 0 else f"prefill: one batch of T={T} tokens")
-                        + ", one MoE layer (H=2048, E=128, I=768, top-8, shared expert), Zipf(1.1) router bias",
+            "workload": (f"prefill: {len(lens)} ragged prompts uniform in [16,512] (seed {seed}), T={T} tokens"
+                         if ragged else f"prefill: one batch of T={T} tokens (seed {seed})")
+                        + ", one MoE layer (H=2048, E=128, I=768, top-8, shared expert)"
+                        + (", Zipf(1.1) router bias" if router_bias == "zipf" else
+                           ", N(0,1) router bias" if router_bias == "normal" else ", no router bias"),
             "tokens": T,
             "l2": "every step writes > 1 GB of activations/partials (8x the 126 MB L2) and alternates "
                   "two 620 MB weight sets",
@@ -620,25 +631,254 @@ def run_prefill(args, dev) -> None:
             "peak": fp8_peak,
             "unit": "TFLOP/s",
             "frac": achieved / fp8_peak,
-            "peak_source": f"2 x {pk['source']} bf16 cuBLAS peak (FP8 dense rate = 2x bf16)",
+            "peak_source": f"2 x the {pk['source']} bf16 cuBLAS burst peak {pk['bf16_tflops']} TFLOP/s "
+                           "(FP8 dense rate = 2x bf16)",
             "traffic": None,
             "algorithmic_flops_per_launch": gate_flops,
             "avg_launch_ms": gate_ms,
             "down_kernel": {"achieved": down_flops / (down_ms * 1e-3) / 1e12, "avg_launch_ms": down_ms,
-                            "algorithmic_flops_per_launch": down_flops},
+                            "algorithmic_flops_per_launch": down_flops,
+                            "frac": down_flops / (down_ms * 1e-3) / 1e12 / fp8_peak},
             "expert_tflops_whole_layer": (gate_flops + down_flops) / (ms * 1e-3) / 1e12,
+            "layer_frac": (gate_flops + down_flops) / (ms * 1e-3) / 1e12 / fp8_peak,
             "stage_ms": {"router_route_permute_quant": pre_ms, "gate_up": gate_ms, "down": down_ms,
                          "combine": post_ms},
         },
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
         # router, route, permute (hist, scan, scatter), quant_scatter, gate_up, down, combine
-        "gpu_launches": 9 * args.steps,
+        "gpu_launches": 9 * steps,
         "clocks": clocks.summary(),
     }
-    if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_prefill_baseline(layers[0], args.cpu_seconds)
+    if cpu_seconds > 0:
+        line["cpu_baseline"] = cpu_prefill_baseline(layers[0], cpu_seconds)
+    del layers, views, ws, xs
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_prefill(args, dev) -> None:
+    """--workload prefill: the ragged 64-prompt batch (config 4) or, with
+    --prefill-tokens, one flat batch."""
+    lens = [args.prefill_tokens] if args.prefill_tokens > 0 else prefill_lengths()
+    line = measure_prefill(dev, lens, args.steps, args.warmup, seed=3, router_bias="zipf",
+                           cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds)
     print(json.dumps(line), flush=True)
+
+
+def measure_stack24(dev, replays: int = 1000, warmup: int = 3, T: int = 64, nlayers: int = 24,
+                    seed: int = 2) -> dict:
+    """a decode step through a stack of `nlayers`
+    distinct layers (seed 2), each the FP8 QKV and o_proj GEMVs followed by
+    the MoE layer with its fused exit (residual update + RMSNorm feeding the
+    next layer), T tokens, per-expert router bias ~ N(0,1) in every layer. The
+    whole step is captured in one CUDA graph and replayed `replays` times with
+    a fresh N(0,1) input copied in before each replay."""
+    import torch
+
+    from d3moe import _lib, ops, synth
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    layers, dense, norms = [], [], []
+    for li in range(nlayers):
+        lw = synth.make_layer(E, I, H, seed=1000 * seed + li, device=dev, router_bias="normal")
+        layers.append((lw, ops.ExpertView(lw.experts), ops.ExpertView(lw.shared)))
+        wq, sq = synth.block_quantize(torch.randn((N_QKV, H), generator=g, device=dev) * 0.02)
+        wo, so = synth.block_quantize(torch.randn((N_O, H), generator=g, device=dev) * 0.02)
+        dense.append((wq, sq, wo, so))
+        norms.append((torch.randn(H, generator=g, device=dev) * 0.1).to(torch.bfloat16))
+    weight_bytes = sum(l[0].nbytes() for l in layers) + sum(
+        t.numel() * t.element_size() for d in dense for t in d)
+    lib = _lib.load()
+    ws_moe = ops.moe_workspace(T, TOPK, E, I, H, True, dev)
+    nb = ctypes.c_size_t()
+    lib.d3_fp8_gemv_workspace_size(T, N_QKV, H, ctypes.byref(nb))
+    ws_dense = torch.empty(nb.value, dtype=torch.uint8, device=dev)
+    x_static = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    residual = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    hbuf = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    qkv = torch.empty((T, N_QKV), dtype=torch.bfloat16, device=dev)
+    o = torch.empty((T, N_O), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((nlayers, T, TOPK), dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    inputs = torch.randn((8, T, H), generator=g, device=dev).to(torch.bfloat16)
+
+    def gemv(x, wq_, sq_, n, out):
+        _lib.call("d3_fp8_gemv", x.data_ptr(), x.stride(0), wq_.data_ptr(), sq_.data_ptr(), T, n, H,
+                  out.data_ptr(), out.stride(0), ws_dense.data_ptr(), ws_dense.numel(),
+                  status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+
+    def step():
+        residual.copy_(x_static)
+        h = x_static
+        for li in range(nlayers):
+            lw, ev, sv = layers[li]
+            wq_, sq_, wo_, so_ = dense[li]
+            gemv(h, wq_, sq_, N_QKV, qkv)
+            gemv(qkv, wo_, so_, N_O, o)
+            nxt = hbuf[li % 2]
+            _lib.call("d3_moe_layer_add_norm", o.data_ptr(), o.stride(0), lw.router.data_ptr(),
+                      lw.router_bias.data_ptr(), T, TOPK, ctypes.byref(ev.struct), ctypes.byref(sv.struct),
+                      residual.data_ptr(), norms[li].data_ptr(), ctypes.c_float(1e-6), nxt.data_ptr(),
+                      ids[li].data_ptr(), None, ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(),
+                      torch.cuda.current_stream(dev).cuda_stream)
+            h = nxt
+
+    x_static.copy_(inputs[0])
+    stream = torch.cuda.current_stream(dev)
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        step()  # eager once on the capture stream (first-use attributes set outside capture)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            step()
+    stream.wait_stream(cap)
+    for i in range(warmup):
+        x_static.copy_(inputs[i % len(inputs)])
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clocks:
+        g0.record(stream)
+        for i in range(replays):
+            x_static.copy_(inputs[i % len(inputs)])
+            graph.replay()
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = g0.elapsed_time(g1) / replays
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status word {int(status.item())}: a bounded wait timed out")
+    ids_host = ids.cpu().numpy()
+    per_layer = [algorithmic_bytes(ids_host[li], T) for li in range(nlayers)]
+    step_bytes = sum(p["total"] for p in per_layer)
+    pk = peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    out = {
+        "config": f"BASELINE configuration 3: {nlayers} distinct layers (seed {seed}) of FP8 QKV[4096x2048] + "
+                  f"o_proj[2048x2048] GEMV + MoE layer with fused residual+RMSNorm exit, T={T}, per-expert "
+                  "router bias ~ N(0,1) per layer; one CUDA graph per step, replayed",
+        "replays": replays,
+        "ms_per_step": ms,
+        "ms_per_layer": ms / nlayers,
+        "tokens_per_s": T / (ms * 1e-3),
+        "weight_bytes": weight_bytes,
+        "step_bytes": step_bytes,
+        "achieved_gbs": achieved,
+        "peak_gbs": pk["hbm_gbs"],
+        "frac": achieved / pk["hbm_gbs"],
+        "mean_active_experts": sum(p["U"] for p in per_layer) / nlayers,
+        "min_active_experts": min(p["U"] for p in per_layer),
+        "gpu_launches_per_step": nlayers * 11,
+        "l2": f"{weight_bytes / 1e9:.1f} GB of weights per step (> 100 x L2)",
+        "clocks": clocks.summary(),
+    }
+    del graph, layers, dense, ws_moe, ws_dense, inputs
+    torch.cuda.empty_cache()
+    return out
+
+
+def _load_flashinfer_moe():
+    """FlashInfer's trtllm_fp8_block_scale_moe (the reference's decode MoE for
+    T > 8, src/drama3/model.py:556-580). Its launcher module is JIT-compiled
+    by FlashInfer; the copy prebuilt in baseline/_flashinfer (git-ignored,
+    made by baseline/flashinfer_prebuild.py) is loaded, and compiling it here
+    is refused (it takes tens of minutes of nvcc), so without the prebuilt
+    copy the comparison reports itself unavailable."""
+    pre = ROOT / "baseline" / "_flashinfer" / "aot"
+    if not (pre / "fused_moe_trtllm_sm100" / "fused_moe_trtllm_sm100.so").exists():
+        raise FileNotFoundError("prebuilt FlashInfer MoE launcher missing "
+                                "(run baseline/flashinfer_prebuild.py)")
+    os.environ["FLASHINFER_DISABLE_JIT"] = "1"
+    import flashinfer.jit.env as jit_env
+
+    jit_env.FLASHINFER_AOT_DIR = pre
+    from flashinfer.fused_moe import trtllm_fp8_block_scale_moe
+    return trtllm_fp8_block_scale_moe
+
+
+def flashinfer_comparison(dev, sizes=(64, 1344, 8192), iters: int = 20, warmup: int = 3) -> dict:
+    """Same-box comparison with the reference's own Blackwell MoE kernel:
+    FlashInfer trtllm_fp8_block_scale_moe called exactly as
+    src/drama3/model.py:556-580 calls it (fp32 logits, RenormalizeNaive
+    routing, MajorK [up | gate] weights, pre-quantised e4m3 hidden states with
+    [H/128, T] scales), against this library's drop-in with the same
+    arguments (d3moe.flashinfer_compat). Both are captured in CUDA graphs and
+    replayed; CUDA events on the launching stream."""
+    import torch
+
+    from d3moe import flashinfer_compat as fc, ops, synth
+
+    try:
+        fi_moe = _load_flashinfer_moe()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer import failed: {type(e).__name__}: {e}"[:300]}
+    ex = synth.make_experts(E, I, H, seed=77, device=dev)
+    gate, up = ex.w13_weight.chunk(2, dim=1)
+    w13 = torch.cat((up, gate), dim=1).contiguous()
+    gs, us = ex.w13_scale_inv.chunk(2, dim=1)
+    s13 = torch.cat((us, gs), dim=1).contiguous()
+    w2, s2 = ex.w2_weight, ex.w2_scale_inv
+    del gate, up, gs, us
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    stream = torch.cuda.current_stream(dev)
+    out = {"kernel": "flashinfer.fused_moe.trtllm_fp8_block_scale_moe (trtllm-gen sm100f cubins, "
+                     "flashinfer 0.6.11.post2)",
+           "ours": "d3moe.flashinfer_compat.trtllm_fp8_block_scale_moe (route_topk + moe_experts_fp8)",
+           "what": "routed experts only (the reference's call has no shared expert), E=128 I=768 H=2048 top-8",
+           "sizes": {}}
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                res = fn()
+        stream.wait_stream(cap)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / iters, res.clone()
+
+    for T in sizes:
+        try:
+            x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+            q, qs = ops.quant_act_fp8(x, transposed=True)
+            logits = torch.randn((T, E), generator=g, device=dev)
+            kw = dict(routing_logits=logits, routing_bias=None, hidden_states=q, hidden_states_scale=qs,
+                      gemm1_weights=w13, gemm1_weights_scale=s13, gemm2_weights=w2,
+                      gemm2_weights_scale=s2, num_experts=E, top_k=TOPK, n_group=None, topk_group=None,
+                      intermediate_size=I, local_expert_offset=0, local_num_experts=E,
+                      routed_scaling_factor=1.0, routing_method_type=4, use_shuffled_weight=False,
+                      weight_layout=0, tune_max_num_tokens=max(4096, T), enable_pdl=None)
+
+            def run_fi():
+                r = fi_moe(**kw)
+                return r[0] if isinstance(r, (list, tuple)) else r
+
+            fi_ms, fi_y = timed(run_fi)
+            our_ms, our_y = timed(lambda: fc.trtllm_fp8_block_scale_moe(**kw))
+            d = (fi_y.float() - our_y.float())
+            rel = float(d.norm() / our_y.float().norm().clamp_min(1e-30))
+            out["sizes"][str(T)] = {"flashinfer_ms": fi_ms, "ours_ms": our_ms,
+                                    "speedup_vs_flashinfer": fi_ms / our_ms,
+                                    "rel_l2_between_outputs": rel}
+        except Exception as e:  # noqa: BLE001
+            out["sizes"][str(T)] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    del ex, w13, s13
+    torch.cuda.empty_cache()
+    return out
 
 
 def mixed_rows(reuse: bool):
@@ -978,6 +1218,10 @@ def main() -> None:
                     help="prefill: a flat batch of this many tokens instead of the ragged 64-prompt batch")
     ap.add_argument("--eager", action="store_true",
                     help="with N > 1: launch the step op by op instead of replaying its CUDA graph")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode line only: skip the prefill, 24-layer stack and FlashInfer objects")
+    ap.add_argument("--stack-replays", type=int, default=1000,
+                    help="replays of the 24-layer stack step (BASELINE configuration 3)")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1: independent full-layer replicas instead of expert parallelism")
     args = ap.parse_args()
@@ -1090,14 +1334,17 @@ def main() -> None:
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for i in range(args.steps):
-            lib.d3_set_stage_events(stage_arrays[i], 5)
-            step(args.warmup + i, xs[(args.warmup + i) % len(xs)], ids_all[i], dense_events[i])
-            lib.d3_set_stage_events(None, 0)
-        end.record(stream)
-        torch.cuda.synchronize(dev)
+    # one clock record over every timed region below: the eager loop, the
+    # graph replays that give `value`, and the end-to-end loop
+    clocks = ClockSampler(local)
+    clocks.__enter__()
+    start.record(stream)
+    for i in range(args.steps):
+        lib.d3_set_stage_events(stage_arrays[i], 5)
+        step(args.warmup + i, xs[(args.warmup + i) % len(xs)], ids_all[i], dense_events[i])
+        lib.d3_set_stage_events(None, 0)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     ms = start.elapsed_time(end) / args.steps
@@ -1191,6 +1438,7 @@ def main() -> None:
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    clocks.__exit__(None, None, None)
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -1235,9 +1483,10 @@ def main() -> None:
             "unit": "GB/s",
             "frac": achieved / pk["hbm_gbs"],
             "peak_source": pk["source"],
-            # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch,
-            # from an ncu --set full capture of this workload
-            "traffic": 404.28e6,
+            # not measured in this run: dram__bytes_read.sum + dram__bytes_write.sum
+            # of one gate_up launch from the ncu capture named in traffic_source
+            "traffic": GATE_UP_TRAFFIC_BYTES,
+            "traffic_source": GATE_UP_TRAFFIC_SOURCE,
             "algorithmic_bytes_per_launch": gate_bytes,
             "avg_launch_ms": gate_avg,
             "down_kernel": {"achieved": down_bytes / (down_avg * 1e-3) / 1e9, "avg_launch_ms": down_avg,
@@ -1269,6 +1518,18 @@ def main() -> None:
                        so_.cpu().numpy(), layers[0].router.float().cpu().numpy(), cpu_ex(layers[0].experts),
                        cpu_ex(layers[0].shared))
         line["cpu_baseline"] = cpu_baseline(T, args.cpu_seconds, weights_cpu)
+    if world == 1 and not args.no_extras:
+        # the metric's prefill half, BASELINE configuration 3 and the same-box
+        # comparison with the reference's FlashInfer kernel, on this GPU
+        del graphs, layers, dense, views, ws_moe, xs
+        torch.cuda.empty_cache()
+        line["prefill"] = {
+            "T8192": measure_prefill(dev, [8192], 10, 3, seed=4, router_bias=None,
+                                     cpu_seconds=0.0 if args.no_cpu_baseline else 6.0),
+            "config4": measure_prefill(dev, prefill_lengths(), 10, 3, seed=3, router_bias="zipf"),
+        }
+        line["stack24"] = measure_stack24(dev, replays=args.stack_replays)
+        line["vs_flashinfer"] = flashinfer_comparison(dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -20,6 +20,8 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT_DIR = HERE / "d3moe" / "_lib"
 LIB = OUT_DIR / "libd3moe.so"
+# test-only library (csrc/selftest/): failure-path probes kept out of the product
+SELFTEST_LIB = OUT_DIR / "libd3moe_selftest.so"
 INCLUDE = HERE.parent / "include"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -47,11 +49,27 @@ def sources() -> list[Path]:
 
 
 def needs_build() -> bool:
-    if not LIB.exists():
+    if not LIB.exists() or not SELFTEST_LIB.exists():
         return True
-    lib_time = LIB.stat().st_mtime
-    deps = list(CSRC.glob("*")) + list(INCLUDE.glob("*.h")) + [Path(__file__)]
+    lib_time = min(LIB.stat().st_mtime, SELFTEST_LIB.stat().st_mtime)
+    deps = list(CSRC.rglob("*")) + list(INCLUDE.glob("*.h")) + [Path(__file__)]
     return any(p.stat().st_mtime > lib_time for p in deps if p.is_file())
+
+
+def _link(cc: str, srcs: list[Path], out: Path, objdir: Path, verbose: bool) -> None:
+    objs = []
+    for src in srcs:
+        obj = objdir / (src.stem + ".o")
+        cmd = [cc, *ARCH_FLAGS, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+        if verbose:
+            cmd += ["-Xptxas", "-v"]
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        objs.append(str(obj))
+    tmp = out.with_suffix(".so.tmp")
+    cmd = [cc, *ARCH_FLAGS, "-shared", "-Xlinker", "--no-undefined", "-o", str(tmp), *objs, "-lcudart"]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, out)
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -61,19 +79,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objdir = HERE / "_build"
     objdir.mkdir(exist_ok=True)
     cc = nvcc()
-    objs = []
-    for src in sources():
-        obj = objdir / (src.stem + ".o")
-        cmd = [cc, *ARCH_FLAGS, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
-        if verbose:
-            cmd += ["-Xptxas", "-v"]
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
-        objs.append(str(obj))
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [cc, *ARCH_FLAGS, "-shared", "-Xlinker", "--no-undefined", "-o", str(tmp), *objs, "-lcudart"]
-    subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
+    _link(cc, sources(), LIB, objdir, verbose)
+    _link(cc, sorted((CSRC / "selftest").glob("*.cu")), SELFTEST_LIB, objdir, verbose)
     return LIB
 
 

@@ -566,6 +566,14 @@ bool stage_recorded(const StageRecord& r) {
     if (g_stage_records[i] == r) return true;
   return false;
 }
+
+// A down_combine that ran consumes its record: the next one needs a fresh
+// gate_up_silu into the workspace.
+void stage_forget(const StageRecord& r) {
+  std::lock_guard<std::mutex> lock(g_stage_mutex);
+  for (size_t i = 0; i < g_stage_count; ++i)
+    if (g_stage_records[i] == r) g_stage_records[i].ws = nullptr;
+}
 }  // namespace
 
 extern "C" int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_t* ids, int T,
@@ -607,8 +615,11 @@ extern "C" int d3_moe_down_combine(const void* weights, int T, int k, const d3_e
   if (T == 0) return D3_OK;
   auto b = carve_moe(workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr, 1);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return experts_down(weights, T, k, experts, shared, nullptr, 0, routed_out, shared_out, nullptr,
-                      b, status ? status : b.status, s, AddNorm{});
+  rc = experts_down(weights, T, k, experts, shared, nullptr, 0, routed_out, shared_out, nullptr, b,
+                    status ? status : b.status, s, AddNorm{});
+  if (rc == D3_OK)
+    stage_forget({workspace, T, k, experts->E, experts->I, experts->H, shared != nullptr});
+  return rc;
 }
 
 extern "C" int d3_moe_experts_fp8(const uint8_t* q, int64_t q_stride, const float* q_scales,
@@ -955,4 +966,20 @@ extern "C" int d3_fp8_gemv_noalloc(const void* x, int64_t x_stride, const uint8_
   const int sms = sm_count();
   const int grid = items < sms ? items : sms;
   return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
+}
+
+// The bounded waits of d3_fp8_gemv_noalloc record a timeout in the first word
+// of the fixed array, and nothing else reads that word. This copies it to the
+// caller (stream-ordered) and clears it, so a timeout is reported once.
+extern "C" int d3_fp8_gemv_noalloc_status(int32_t* status_out, d3_stream_t stream) {
+  D3_REQUIRE(status_out != nullptr, "fp8_gemv_noalloc_status: null output");
+  uint8_t* base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(status_out, base, sizeof(int32_t), cudaMemcpyDefault, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(base, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess)
+    return set_error(D3_ECUDA, "fp8_gemv_noalloc_status: %s", cudaGetErrorString(e));
+  return D3_OK;
 }

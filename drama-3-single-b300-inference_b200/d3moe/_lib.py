@@ -12,6 +12,9 @@ from pathlib import Path
 
 _HERE = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("D3MOE_LIB", _HERE / "_lib" / "libd3moe.so"))
+# Test-only library (include/d3moe_selftest.h): failure-path probes that the
+# product library does not carry.
+SELFTEST_LIB_PATH = LIB_PATH.parent / "libd3moe_selftest.so"
 
 D3_OK = 0
 D3_EINVAL = -1
@@ -109,6 +112,7 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _i64, _c_void_p],
     ),
+    "d3_fp8_gemv_noalloc_status": (_i32, [_c_void_p, _c_void_p]),
     "d3_moe_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_size_t)]),
     "d3_moe_experts": (
         _i32,
@@ -125,7 +129,6 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i32, _i32, ctypes.POINTER(D3Experts), ctypes.POINTER(D3Experts), _c_void_p,
          _c_void_p, _c_void_p, _size_t, _c_void_p, _c_void_p],
     ),
-    "d3_wait_timeout_probe": (_i32, [_c_void_p, _c_void_p]),
     "d3_set_stage_events": (_i32, [ctypes.POINTER(_c_void_p), _i32]),
     "d3_set_prefill_min_tokens": (_i32, [_i32]),
     "d3_ep_plan": (

@@ -2,10 +2,14 @@
  * d3moe.h — C ABI of the B200 (sm_100a) FP8 mixture-of-experts hot path.
  *
  * Every entry point is stream-ordered (it only enqueues work on `stream`),
- * performs no device or pinned allocation, never synchronises the device and
- * keeps no global mutable state apart from a per-thread error string. That
- * makes every call capturable into a CUDA graph, the way the reference runtime
- * captures its decode step (reference: src/drama3/engine.py:84-92).
+ * performs no device or pinned allocation and never synchronises the device.
+ * That makes every call capturable into a CUDA graph, the way the reference
+ * runtime captures its decode step (reference: src/drama3/engine.py:84-92).
+ * Process-wide state is small and named: a per-thread error string, the
+ * prefill token threshold (d3_set_prefill_min_tokens), the host-side record
+ * of workspaces d3_moe_gate_up_silu filled, per-device kernel attributes set
+ * on first use, the fixed scratch of d3_fp8_gemv_noalloc, and the per-thread
+ * profiling hook d3_set_stage_events (off unless a caller sets it).
  *
  * Return value: D3_OK (0) or a negative D3_E* code. Argument errors are found
  * on the host before anything is launched; d3_last_error_string() explains the
@@ -57,12 +61,6 @@ typedef struct CUstream_st* d3_stream_t; /* == cudaStream_t */
 
 D3_API int d3_version(void);
 D3_API const char* d3_last_error_string(void);
-
-/* Self-test of the bounded-wait failure path: one thread waits, through the
- * same bounded wait every waiting kernel uses, on a barrier nothing arrives
- * on; after the wait limit (2 s) the kernel writes D3_STATUS_WAIT_TIMEOUT to
- * *status (device int32) and exits. No fault, and the context stays usable. */
-D3_API int d3_wait_timeout_probe(int32_t* status, d3_stream_t stream);
 
 /* ------------------------------------------------------------- (a3) quant --
  * Activation FP8 quantisation per 1x128 group: scale = max(amax,1e-10)/448,
@@ -225,7 +223,9 @@ D3_API int d3_fp8_gated_gemv(const void* x, int64_t x_stride, const void* gate, 
  * The first call on a device looks up the array's device address (once per
  * device), so make that first call before any stream capture. All calls share
  * the array: calls whose GPU work overlaps (other streams or host threads)
- * race on it and must be serialised by the caller. */
+ * race on it and must be serialised by the caller. The device address is
+ * kept for the life of the process: after cudaDeviceReset (or any other end
+ * of the device's primary context) the entry point must not be called again. */
 #define D3_GEMV_NOALLOC_MAX_T 64
 #define D3_GEMV_NOALLOC_MAX_N 4096
 #define D3_GEMV_NOALLOC_MAX_K 4096
@@ -233,6 +233,16 @@ D3_API int d3_fp8_gated_gemv(const void* x, int64_t x_stride, const void* gate, 
 D3_API int d3_fp8_gemv_noalloc(const void* x, int64_t x_stride, const uint8_t* wq, const float* s,
                                int T, int N, int K, void* y, int64_t y_stride,
                                d3_stream_t stream);
+
+/* Status of the calls above. d3_fp8_gemv_noalloc has no status argument: its
+ * bounded waits record D3_STATUS_WAIT_TIMEOUT in a word inside the fixed
+ * array, where it stays until read. This call enqueues on `stream` a copy of
+ * that word for the current device into *status_out (device memory, or host
+ * memory the GPU can address: read it after the stream has synchronised) and
+ * then clears the word. A result other than D3_STATUS_OK means that some
+ * call since the previous read gave up a wait, and its y is not valid.
+ * Allocates nothing. */
+D3_API int d3_fp8_gemv_noalloc_status(int32_t* status_out, d3_stream_t stream);
 
 /* --------------------------------------------- (a5-a8) routed experts --
  * Expert weights of one MoE layer (reference container: experts.w13_weight,
@@ -284,8 +294,11 @@ D3_API int d3_moe_experts(const void* x, int64_t x_stride, const int64_t* ids, c
  * gives d3_moe_experts' outputs bit for bit. d3_moe_down_combine returns
  * D3_EINVAL for a workspace that d3_moe_gate_up_silu has not filled with the
  * same T, k, expert shapes and shared expert (a host-side record, no device
- * work); other use of the workspace between the two calls is the caller's to
- * avoid. */
+ * work). The record is best-effort: it is keyed on the workspace address and
+ * the shapes, so a different allocation that lands at the same address with
+ * the same shapes passes it; each successful d3_moe_down_combine consumes the
+ * record, so one d3_moe_gate_up_silu call permits one d3_moe_down_combine.
+ * Other use of the workspace between the two calls is the caller's to avoid. */
 D3_API int d3_moe_gate_up_silu(const void* x, int64_t x_stride, const int64_t* ids, int T, int k,
                                const d3_experts_t* experts, const d3_experts_t* shared,
                                void* workspace, size_t workspace_bytes, int32_t* status,
@@ -410,11 +423,13 @@ D3_API int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const voi
                             int T, int k, int H, const void* shared, const void* gate,
                             int64_t gate_stride, void* out, d3_stream_t stream);
 
-/* Benchmark hook: while set, d3_moe_experts / d3_moe_layer calls made by the
- * calling thread record events[i] (cudaEvent_t handles, n >= 5) on their
- * stream at stage boundaries: 0 call start, 1 before the gate_up engine,
- * 2 after gate_up, 3 after the down engine, 4 call end. NULL clears it.
- * No counterpart in the reference (its scripts time whole calls). */
+/* Profiling hook, off by default: while set, d3_moe_experts / d3_moe_layer
+ * calls made by the calling thread (the setting is per host thread) record
+ * events[i] (cudaEvent_t handles, n >= 5) on their stream at stage
+ * boundaries: 0 call start, 1 before the gate_up engine, 2 after gate_up,
+ * 3 after the down engine, 4 call end. NULL clears it. A caller that never
+ * sets it sees no effect. No counterpart in the reference (its scripts time
+ * whole calls with CUDA events, src/drama3/profiling.py:11-102). */
 D3_API int d3_set_stage_events(void* const* events, int n);
 
 /* Token count T from which d3_moe_experts / d3_moe_layer run both expert GEMMs

@@ -44,6 +44,19 @@ def test_library_exports_every_declared_symbol(lib):
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def test_selftest_library_is_separate_and_exports_its_probe(lib):
+    """The failure-path probe ships in the test-only libd3moe_selftest.so
+    (include/d3moe_selftest.h), not in the product library."""
+    from d3moe import _lib
+    text = (ROOT / "include" / "d3moe_selftest.h").read_text()
+    syms = sorted(set(re.findall(r"D3_API\s+[\w\s\*]+?\b(d3_\w+)\s*\(", text)))
+    assert syms == ["d3_wait_timeout_probe"]
+    st = ctypes.CDLL(str(_lib.SELFTEST_LIB_PATH))
+    for name in syms:
+        assert hasattr(st, name)
+        assert not hasattr(lib, name), f"{name} leaked into the product library"
+
+
 def test_version_and_error_string(lib):
     assert lib.d3_version() >= 1
     assert isinstance(lib.d3_last_error_string(), bytes)

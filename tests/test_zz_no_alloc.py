@@ -4,9 +4,12 @@ Some callers cannot hand this library a workspace: a host runtime that gives
 a plugin only its inputs, outputs and a stream, and does not let it allocate
 device memory while a request runs. For them the library keeps the GEMV's
 scratch in a fixed array of its own. These tests call that entry point through
-the C ABI and check it against the workspace entry point (d3_fp8_gemv) on two
-calls in a row with different shapes, so the second call proves that whatever
-the first call left in the shared array does not leak into the result.
+the C ABI and check it against the workspace entry point (d3_fp8_gemv) on
+calls in a row with different shapes, in both orders (a small call before a
+large one and after it, and an N whose last 128-row tile is partial), so each
+later call proves that whatever the earlier calls left in the shared array
+does not leak into its result. The array's status word, read through
+d3_fp8_gemv_noalloc_status, must report no timeout and read back cleared.
 This file is collected last on purpose.
 """
 
@@ -39,11 +42,21 @@ def _noalloc(x, wq, s, N):
     return y
 
 
+def _noalloc_status(device):
+    from d3moe import _lib, ops
+    st = torch.full((1,), -1, dtype=torch.int32, device=device)
+    _lib.call("d3_fp8_gemv_noalloc_status", st.data_ptr(), ops._stream(device))
+    torch.cuda.synchronize()
+    return int(st.item())
+
+
 def test_noalloc_gemv_matches_workspace_gemv_on_consecutive_calls():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from d3moe import ops
-    for T, N, K, seed in ((64, 4096, 2048, 1), (13, 2048, 4096, 2)):
+    cases = ((64, 4096, 2048, 1), (13, 2048, 4096, 2), (1, 4096 - 64, 4096, 3),
+             (1, 2048, 2048, 4), (64, 4096, 4096, 5))
+    for T, N, K, seed in cases:
         x, wq, s = _case(T, N, K, seed)
         got = from_bf16(_noalloc(x, wq, s, N))
         ref = from_bf16(ops.fp8_gemv(x, wq, s, n=N))
@@ -52,6 +65,9 @@ def test_noalloc_gemv_matches_workspace_gemv_on_consecutive_calls():
         # round to neighbouring bf16 values
         assert ulps_bf16(got, ref).max() <= 1
         assert_close(got, ref, what=f"noalloc gemv T={T} N={N} K={K}")
+    dev = torch.device("cuda")
+    assert _noalloc_status(dev) == 0, "a bounded wait of the no-allocation GEMV timed out"
+    assert _noalloc_status(dev) == 0, "the status word was not cleared by the read"
 
 
 def test_noalloc_gemv_rejects_sizes_beyond_its_scratch():
