@@ -492,8 +492,8 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
                 "ms_per_step": e2e_ms},
-        # dense 2 x (prep + engine), router, route, dispatch meta, routed experts (permute, gather,
-        # gate_up, down, combine), shared expert (the same five), combine_pairs
+        # dense 2 x (activation split + tcgen05 GEMV), router, route, dispatch meta, routed experts
+        # (permute, gather, gate_up, down, combine), shared expert (the same five), combine_pairs
         "gpu_launches": 18 * args.steps,
         "clocks": clocks.summary(),
     }
@@ -1097,7 +1097,12 @@ def run_dense(args, dev) -> None:
     rows = []
     total_bytes, total_ms = 0.0, 0.0
     launches = 0
-    for N, K, name in DENSE_SHAPES:
+    shapes = DENSE_SHAPES
+    if args.dense_shape:
+        n_, k_ = (int(v) for v in args.dense_shape.split("x"))
+        shapes = tuple(sh for sh in DENSE_SHAPES if sh[:2] == (n_, k_)) or ((n_, k_, "custom"),)
+    t_values = (args.dense_t,) if args.dense_t else (1, 8, 16, 32, 64)
+    for N, K, name in shapes:
         wbytes = N * K + (N // 128) * (K // 128) * 4
         sets = max(2, -(-260_000_000 // wbytes))
         g = torch.Generator(device=dev)
@@ -1110,7 +1115,7 @@ def run_dense(args, dev) -> None:
                                             .to(torch.bfloat16))
             ws_q.append(q)
             ws_s.append(sc)
-        for T in (1, 8, 16, 32, 64):
+        for T in t_values:
             x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
             y = torch.empty((T, N), dtype=torch.bfloat16, device=dev)
             nb = ctypes.c_size_t()
@@ -1124,13 +1129,28 @@ def run_dense(args, dev) -> None:
             for i in range(max(args.warmup, sets)):
                 call(i)
             torch.cuda.synchronize(dev)
+            # the calls are captured in one CUDA graph and replayed, so the
+            # time is the device's (back-to-back GEMVs, as in a captured
+            # decode step) rather than the host's launch rate
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(stream)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(graph, stream=cap):
+                    for i in range(args.steps):
+                        _lib.call("d3_fp8_gemv", x.data_ptr(), K, ws_q[i % sets].data_ptr(),
+                                  ws_s[i % sets].data_ptr(), T, N, K, y.data_ptr(), N, ws.data_ptr(),
+                                  nb.value, None, cap.cuda_stream)
+            stream.wait_stream(cap)
+            graph.replay()
+            torch.cuda.synchronize(dev)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            for i in range(args.steps):
-                call(i)
+            graph.replay()
             e1.record(stream)
             torch.cuda.synchronize(dev)
             ms = e0.elapsed_time(e1) / args.steps
+            del graph
             nbytes = wbytes + T * K * 2 + T * N * 2
             total_bytes += nbytes * args.steps
             total_ms += ms * args.steps
@@ -1152,12 +1172,13 @@ def run_dense(args, dev) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "e4m3 weights x f16 activations -> f32 (mma.sync), bf16 out",
+        "dtype": "e4m3 weights x bf16 activations split exactly into two e4m3 terms -> f32 "
+                 "(tcgen05 kind::f8f6f4), bf16 out",
         "data": "synthetic",
         "config": {"workload": "weight-only FP8 GEMV, real Drama-3 projection shapes and the benchmark's, "
                                "T in {1,8,16,32,64}, weights rotated over > 260 MB per shape",
                    "per_shape": rows},
-        "roofline": {"bound": "hbm", "kernel": "expert_gemv_kernel<EPI_DENSE> (+ dense_act_prep)",
+        "roofline": {"bound": "hbm", "kernel": "dense_tc_kernel (tcgen05 weight-only FP8 GEMV, + dense_split)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"], "traffic": None},
         "gpu_launches": launches,
@@ -1218,6 +1239,9 @@ def main() -> None:
                     help="prefill: a flat batch of this many tokens instead of the ragged 64-prompt batch")
     ap.add_argument("--eager", action="store_true",
                     help="with N > 1: launch the step op by op instead of replaying its CUDA graph")
+    ap.add_argument("--dense-shape", default="",
+                    help="dense: one weight shape NxK (e.g. 4096x2048) instead of the list")
+    ap.add_argument("--dense-t", type=int, default=0, help="dense: one token count instead of 1..64")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode line only: skip the prefill, 24-layer stack and FlashInfer objects")
     ap.add_argument("--stack-replays", type=int, default=1000,
@@ -1316,7 +1340,8 @@ def main() -> None:
                   None if ids_buf is None else ids_buf.data_ptr(), wts.data_ptr(),
                   ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
 
-    # (act prep + engine) x 2 GEMVs; router, route, permute, quant_scatter, gate_up, down, combine
+    # (activation split + tcgen05 GEMV) x 2; router, route, permute, quant_scatter, gate_up, down,
+    # combine
     launches_per_step = 2 * 2 + 7
 
     # per-step stage events (gate_up / down engine launches) inside the timed region

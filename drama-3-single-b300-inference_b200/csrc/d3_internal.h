@@ -53,6 +53,14 @@ void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half
                            const void* gate = nullptr, int64_t gate_stride = 0,
                            int mode = GATE_NONE);
 
+// Activations of the tcgen05 dense GEMV split into two E4M3 terms per 1x128
+// group: x * 2^s = hi + lo / 16 (exact for every element within 2^13 of the
+// group maximum), hi / lo e4m3 [T,K] (row stride K), sc f32 [T,K/128] = 2^-s.
+// With a gate (GATE_SWIGLU / GATE_SIGMOID) x is first bf16(x * act(gate)).
+void launch_dense_split(const void* x, int64_t x_stride, int T, int K, const void* gate,
+                        int64_t gate_stride, int mode, uint8_t* hi, uint8_t* lo, float* sc,
+                        cudaStream_t s);
+
 // Final combine of the expert rows (see d3_moe_experts / d3_moe_layer).
 //   routed[t] = bf16(sum_r w[t,r] * d[inv_rows[t*k+r]])
 //   shared[t] = bf16(d[P+t])                                   (when with_shared)

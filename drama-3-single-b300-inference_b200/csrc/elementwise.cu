@@ -241,6 +241,75 @@ __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64
   }
 }
 
+// Activations of the tcgen05 dense GEMV, split exactly into two E4M3 terms.
+// Per 1x128 group, xs = x * 2^s with s chosen so that max|xs| lies in
+// [2^7, 2^8) (a power of two: exact), hi = e4m3(xs) (round to nearest even),
+// lo = e4m3((xs - hi) * 16). An 8-bit bf16 significand rounded to its top 4
+// bits leaves a remainder of at most 3 significant bits, so xs = hi + lo / 16
+// exactly whenever |xs| >= 2^-6 (every element within 2^13 of its group's
+// maximum); smaller elements are carried with an absolute error below
+// 2^-21 times the group maximum. sc[t][g] = 2^-s. With a gate, x is first
+// replaced by bf16(x * bf16(act(gate))) like dense_act_prep_kernel.
+// One warp per (row, pair of groups): 16 lanes x 8 elements per group.
+__global__ void dense_split_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T, int K,
+                                   const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
+                                   int mode, uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
+                                   float* __restrict__ sc) {
+  pdl_wait();
+  const int G = K / 128;
+  const RowPair rp = row_pair(G);
+  const int row = rp.row;
+  if (row >= T) return;
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  const int g = 2 * rp.gp + half;
+  const bool valid = g < G;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + row * x_stride + g * 128 + hl * 8));
+  float f[8];
+  unpack_bf16x8(v, f);
+  if (mode != GATE_NONE) {
+    uint4 gv = make_uint4(0, 0, 0, 0);
+    if (valid) gv = __ldg(reinterpret_cast<const uint4*>(gate + row * gate_stride + g * 128 + hl * 8));
+    float gf[8];
+    unpack_bf16x8(gv, gf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = bf16_round(f[i] * gate_activation(gf[i], mode));
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+  amax = half_warp_max(amax);
+  int e = 8;
+  if (amax > 0.f && isfinite(amax)) frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+  const int sh = 8 - e;
+  const float mul = ldexpf(1.0f, sh);
+  if (!valid) return;
+  uint32_t h[2], l[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float xs[4], hf[4], lv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xs[j] = f[4 * i + j] * mul;
+    const uint16_t h01 = f32x2_to_e4m3x2(xs[0], xs[1]), h23 = f32x2_to_e4m3x2(xs[2], xs[3]);
+    const uint32_t hh01 = e4m3x2_to_f16x2(h01), hh23 = e4m3x2_to_f16x2(h23);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hh01));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hh23));
+    hf[0] = a.x;
+    hf[1] = a.y;
+    hf[2] = b.x;
+    hf[3] = b.y;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) lv[j] = (xs[j] - hf[j]) * 16.0f;
+    h[i] = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
+    l[i] = static_cast<uint32_t>(f32x2_to_e4m3x2(lv[0], lv[1])) |
+           (static_cast<uint32_t>(f32x2_to_e4m3x2(lv[2], lv[3])) << 16);
+  }
+  const int64_t off = static_cast<int64_t>(row) * K + g * 128 + hl * 8;
+  *reinterpret_cast<uint2*>(hi + off) = make_uint2(h[0], h[1]);
+  *reinterpret_cast<uint2*>(lo + off) = make_uint2(l[0], l[1]);
+  if (hl == 0) sc[static_cast<int64_t>(row) * G + g] = ldexpf(1.0f, -sh);
+}
+
 __device__ __forceinline__ float silu_bf16(float gate_bf16) {
   // silu(g) = g * sigmoid(g), rounded to bf16 like the reference kernel.
   return bf16_round(gate_bf16 * (1.0f / (1.0f + expf(-gate_bf16))));
@@ -627,6 +696,15 @@ void launch_dense_act_prep(const void* x, int64_t x_stride, int T, int K, __half
   launch_kernel(dense_act_prep_kernel, dim3(pair_blocks(T, K)), dim3(256), 0, s,
                 static_cast<const __nv_bfloat16*>(x), x_stride, T, K, xh, inv, zero, nzero,
                 static_cast<const __nv_bfloat16*>(gate), gate_stride, gate ? mode : GATE_NONE);
+}
+
+void launch_dense_split(const void* x, int64_t x_stride, int T, int K, const void* gate,
+                        int64_t gate_stride, int mode, uint8_t* hi, uint8_t* lo, float* sc,
+                        cudaStream_t s) {
+  if (T <= 0) return;
+  launch_kernel(dense_split_kernel, dim3(pair_blocks(T, K)), dim3(256), 0, s,
+                static_cast<const __nv_bfloat16*>(x), x_stride, T, K,
+                static_cast<const __nv_bfloat16*>(gate), gate_stride, gate ? mode : GATE_NONE, hi, lo, sc);
 }
 
 void launch_combine_rows(const float* d, int H, const int32_t* inv_rows, const void* weights,

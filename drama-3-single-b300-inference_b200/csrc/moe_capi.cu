@@ -16,6 +16,7 @@
 
 #include "d3_host.h"
 #include "d3_internal.h"
+#include "dense_tc.cuh"
 #include "expert_gemv.cuh"
 #include "tc_grouped.cuh"
 
@@ -749,36 +750,110 @@ extern "C" int d3_moe_layer_rows(const void* x, int64_t x_stride, const void* ro
 }
 
 namespace {
-constexpr int kMaxDenseSplit = 8;
-
+// Workspace of d3_fp8_gemv / d3_fp8_gated_gemv: a status word and the
+// activations split into two E4M3 terms (hi, lo [T, K]) with their group
+// scales [T, K/128].
 struct DenseBuffers {
   int32_t* status;
-  __half* xh;
-  float* inv;
-  float* partials;
-  int32_t* counters;
+  uint8_t* hi;
+  uint8_t* lo;
+  float* sc;
   size_t bytes;
 };
 
-DenseBuffers carve_dense(void* ws, int T, int N, int K) {
+DenseBuffers carve_dense(void* ws, int T, int K) {
   Carve c{static_cast<uint8_t*>(ws)};
-  const int tiles = (N + 127) / 128;
-  const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
   DenseBuffers b;
   b.status = c.take<int32_t>(4);
-  b.xh = c.take<__half>(static_cast<size_t>(T) * K);
-  b.inv = c.take<float>(static_cast<size_t>(T) * (K / 128));
-  b.partials = c.take<float>(static_cast<size_t>(kMaxDenseSplit) * T * tiles * 128);
-  b.counters = c.take<int32_t>(static_cast<size_t>(tiles) * (groups > 0 ? groups : 1));
+  b.hi = c.take<uint8_t>(static_cast<size_t>(T) * K);
+  b.lo = c.take<uint8_t>(static_cast<size_t>(T) * K);
+  b.sc = c.take<float>(static_cast<size_t>(T) * (K / 128));
   b.bytes = c.off + 256;
   return b;
+}
+
+// Most clusters of `split` CTAs of the TP instance that can be resident at
+// once (cached per device).
+template <int TP>
+int dense_max_clusters(int dev, int split) {
+  static int cache[64][kDtMaxSplit + 1] = {};
+  if (dev >= 0 && dev < 64 && cache[dev][split]) return cache[dev][split];
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(split, 1, 1);
+  cfg.blockDim = dim3(kDtThreads);
+  cfg.dynamicSmemBytes = DtSmem<TP>::bytes();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, dense_tc_kernel<TP>, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 1;
+  }
+  if (dev >= 0 && dev < 64) cache[dev][split] = n;
+  return n;
+}
+
+template <int TP>
+int launch_dense_tc(const CUtensorMap& tw, const CUtensorMap& thi, const CUtensorMap& tlo, DenseTcArgs a,
+                    int tiles, int groups, cudaStream_t s) {
+  auto kern = dense_tc_kernel<TP>;
+  const size_t smem = DtSmem<TP>::bytes();
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return set_error(D3_ECUDA, "dense GEMV: cannot reserve %zu bytes of shared memory", smem);
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  // K ranges per tile (a power of two up to 8): enough CTAs for about one
+  // wave of SMs, in clusters that can all be resident at once, and at most
+  // kDtMaxKbPerCta K blocks per CTA
+  const int clusters = tiles * groups;
+  const int cap = sm_count() / clusters;
+  int need = 1;  // smallest split that keeps a CTA's K range within the limit
+  while (need * kDtMaxKbPerCta < a.KB) need *= 2;
+  if (need > kDtMaxSplit)
+    return set_error(D3_EUNSUPPORTED, "dense GEMV: K=%d above %d", a.KB * 128,
+                     kDtMaxSplit * kDtMaxKbPerCta * 128);
+  int split = need;
+  while (split * 2 <= cap && split * 2 <= kDtMaxSplit && split * 2 <= a.KB) split *= 2;
+  while (split > need && dense_max_clusters<TP>(dev, split) < clusters) split /= 2;
+  a.split = split;
+  a.kb_per_split = (a.KB + split - 1) / split;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(tiles * split, groups);
+  cfg.blockDim = dim3(kDtThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  int na = 1;
+  if (split > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = split;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaLaunchKernelEx(&cfg, kern, tw, thi, tlo, a);
+  return check_launch("dense tcgen05 GEMV");
 }
 }  // namespace
 
 extern "C" int d3_fp8_gemv_workspace_size(int T, int N, int K, size_t* bytes) {
   D3_REQUIRE(bytes != nullptr && T >= 0 && N > 0 && K > 0 && K % 128 == 0,
              "fp8_gemv_workspace_size: bad arguments T=%d N=%d K=%d", T, N, K);
-  *bytes = carve_dense(nullptr, T, N, K).bytes;
+  *bytes = carve_dense(nullptr, T, K).bytes;
   return D3_OK;
 }
 
@@ -791,49 +866,38 @@ static int fp8_gemv_impl(const void* x, int64_t x_stride, const void* gate, int6
   D3_REQUIRE(y_stride >= N, "fp8_gemv: y row stride must be >= N");
   D3_REQUIRE(x && wq && s && y && aligned(x, 16) && aligned(wq, 16), "fp8_gemv: null or misaligned pointer");
   D3_REQUIRE(workspace && aligned(workspace, 256), "fp8_gemv: workspace must be 256-byte aligned");
-  const DenseBuffers need = carve_dense(nullptr, T, N, K);
+  const DenseBuffers need = carve_dense(nullptr, T, K);
   if (workspace_bytes < need.bytes)
     return set_error(D3_EWORKSPACE, "fp8_gemv: workspace %zu bytes < %zu", workspace_bytes, need.bytes);
   if (T == 0) return D3_OK;
-  const DenseBuffers b = carve_dense(workspace, T, N, K);
+  const DenseBuffers b = carve_dense(workspace, T, K);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int tiles = (N + 127) / 128, KB = K / 128;
-  const int sms = sm_count();
-  // K splits so that tiles * splits fills about one wave of SMs
-  int split = sms / tiles;
-  split = split < 1 ? 1 : (split > kMaxDenseSplit ? kMaxDenseSplit : split);
-  split = split > KB ? KB : split;
-  const int kbps = (KB + split - 1) / split;
-  split = (KB + kbps - 1) / kbps;
-  const int groups = (T + kTokensPerGroup - 1) / kTokensPerGroup;
-  // the split-K tile counters are zeroed by the activation prep kernel
-  launch_dense_act_prep(x, x_stride, T, K, b.xh, b.inv, st, b.counters, split > 1 ? tiles * groups : 0,
-                        gate, gate_stride, mode);
-  int rc = check_launch("dense_act_prep");
+  // activations (gated first, for d3_fp8_gated_gemv) split into hi + lo / 16
+  launch_dense_split(x, x_stride, T, K, gate, gate_stride, mode, b.hi, b.lo, b.sc, st);
+  int rc = check_launch("dense_split");
   if (rc) return rc;
-  CUtensorMap tw, ta;
+  const int tiles = (N + 127) / 128;
+  const int groups = (T + kDtTokens - 1) / kDtTokens;
+  const int TP = T > 32 ? 64 : (T > 16 ? 32 : 16);
+  CUtensorMap tw, thi, tlo;
   if ((rc = encode_tmap_2d(&tw, wq, 1, K, N, K, 128, 128))) return rc;
-  if ((rc = encode_tmap_2d(&ta, b.xh, 2, K, T, static_cast<uint64_t>(K) * 2, 64, 16))) return rc;
-  EngineArgs a{};
-  a.num_groups = 1;
-  a.dense_count = T;
-  a.tiles = tiles;
-  a.KB = KB;
-  a.ksplit = split;
-  a.kb_per_split = kbps;
-  a.partials = b.partials;
-  a.tile_counters = b.counters;
-  a.rows_per_expert = 0;
+  if ((rc = encode_tmap_2d(&thi, b.hi, 1, K, T, K, 128, TP))) return rc;
+  if ((rc = encode_tmap_2d(&tlo, b.lo, 1, K, T, K, 128, TP))) return rc;
+  DenseTcArgs a{};
   a.wscale = s;
-  a.wscale_sh = s;
-  a.act_scale = b.inv;
-  a.out_bf16 = static_cast<__nv_bfloat16*>(y);
-  a.out_ld = static_cast<int>(y_stride);
-  a.out_cols = N;
+  a.xscale = b.sc;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.y_ld = y_stride;
+  a.T = T;
+  a.N = N;
+  a.KB = K / 128;
+  a.vec_store = (y_stride % 4 == 0 && aligned(y, 8)) ? 1 : 0;
   a.status = status ? status : b.status;
-  const int items = tiles * split;
-  const int grid = items < sms ? items : sms;
-  return launch_engine<EPI_DENSE, true, kStagesDense>(nch_for(T), tw, tw, ta, a, grid, st);
+  switch (TP) {
+    case 16: return launch_dense_tc<16>(tw, thi, tlo, a, tiles, groups, st);
+    case 32: return launch_dense_tc<32>(tw, thi, tlo, a, tiles, groups, st);
+    default: return launch_dense_tc<64>(tw, thi, tlo, a, tiles, groups, st);
+  }
 }
 
 extern "C" int d3_fp8_gemv(const void* x, int64_t x_stride, const uint8_t* wq, const float* s,

@@ -11,6 +11,17 @@ operands and runs them on this library's kernels: RenormalizeNaive routing
 [up | gate] weights read in place (no copy), FP8 gate_up with SiLU*mul and
 requantisation, FP8 down and the fixed-order routed combine. Arguments outside
 what the reference passes raise instead of running a different algorithm.
+
+Weights in FlashInfer's BlockMajorK layout (use_shuffled_weight=True,
+weight_layout=BlockMajorK: what the reference passes when
+DRAMA3_MOE_LAYOUT=blocked, model.py:152, 203-206, 574-576, shuffled by
+blocked_moe_weight, model.py:41-52) are brought back to the MajorK
+checkpoint layout once per weight tensor (a copy, cached by data_ptr) and
+then run like MajorK weights. The shuffle moves 128-byte K blocks to the
+front ([E, K/128, rows, 128]) and permutes the rows inside each K block by
+FlashInfer's epilogue row map for a 64-row tile
+(flashinfer.utils.get_shuffle_matrix_a_row_indices); the scales keep their
+logical order.
 """
 
 from __future__ import annotations
@@ -39,6 +50,37 @@ class RoutingMethodType:
 
 
 _views: dict = {}
+_unshuffled: dict = {}
+
+
+def unshuffle_block_major_k(weight: torch.Tensor) -> torch.Tensor:
+    """Inverse of the reference's blocked_moe_weight (model.py:41-52): e4m3
+    [E, K/128, rows, 128] (the shape blocked_moe_weight returns) or the same
+    bytes as [E, rows, K] -> the MajorK tensor [E, rows, K] it was made from.
+    Cached per input tensor (data_ptr, shape)."""
+    key = (weight.data_ptr(), tuple(weight.shape))
+    hit = _unshuffled.get(key)
+    if hit is not None:
+        return hit
+    from flashinfer.utils import get_shuffle_matrix_a_row_indices
+
+    if weight.dim() == 4:
+        E, KB, rows, last = weight.shape
+        if last != 128:
+            raise ValueError("BlockMajorK weights are [E, K/128, rows, 128]")
+        K = KB * 128
+    else:
+        E, rows, K = weight.shape
+        if K % 128:
+            raise ValueError("BlockMajorK weights need K a multiple of 128")
+    order = get_shuffle_matrix_a_row_indices(torch.empty((rows, K), dtype=torch.uint8), 64)
+    inverse = torch.empty_like(order)
+    inverse[order] = torch.arange(rows, dtype=order.dtype)
+    blocks = weight.view(torch.uint8).reshape(E, K // 128, rows, 128)
+    out = blocks[:, :, inverse.to(weight.device), :].permute(0, 2, 1, 3).contiguous()
+    out = out.view(E, rows, K).view(weight.dtype)
+    _unshuffled[key] = out
+    return out
 
 
 def _expert_view(w13, s13, w2, s2) -> ops.ExpertView:
@@ -69,8 +111,12 @@ def trtllm_fp8_block_scale_moe(routing_logits, routing_bias, hidden_states, hidd
         raise NotImplementedError("only routing_method_type=4 (RenormalizeNaive) is implemented")
     if n_group or topk_group:
         raise NotImplementedError("grouped top-k routing (n_group/topk_group) is not implemented")
-    if use_shuffled_weight or weight_layout != WeightLayout.MajorK:
-        raise NotImplementedError("only WeightLayout.MajorK (unshuffled) expert weights are implemented")
+    if use_shuffled_weight != (weight_layout == WeightLayout.BlockMajorK) or weight_layout == WeightLayout.MajorMn:
+        raise NotImplementedError("weights must be MajorK (unshuffled) or BlockMajorK with "
+                                  "use_shuffled_weight=True, the two layouts the reference passes")
+    if weight_layout == WeightLayout.BlockMajorK:
+        gemm1_weights = unshuffle_block_major_k(gemm1_weights)
+        gemm2_weights = unshuffle_block_major_k(gemm2_weights)
     if routed_scaling_factor not in (None, 1.0):
         raise NotImplementedError("routed_scaling_factor other than 1.0 is not implemented")
     if not do_finalize:

@@ -6,6 +6,7 @@ Signatures follow the reference so a caller swaps the import:
   native_moe(x, ids, weights, experts, ...)       kernels.py:702-779
   silu_mul(projected)                             kernels.py:396-402
   combine_experts(routed, shared, gate)           kernels.py:442-445
+  linear(x, weight)                               kernels.py:274-287
 The reference's tile knobs (up_rows, down_rows, down_warps, block_m, group_m,
 atomic) are accepted for call compatibility; the B200 kernels choose their own
 tiling (weight-streaming engine for few tokens per expert).
@@ -15,7 +16,22 @@ from __future__ import annotations
 
 import torch
 
-from . import ops
+from . import experimental_fp8, ops
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """y [M, N] = x [M, K] . weight [N, K]^T (kernels.py:274-287).
+
+    The reference dispatches its BF16 projections to a Triton GEMV (M = 1),
+    FlashInfer's mm_bf16 (2 <= M <= 32) or F.linear. Here every projection is
+    the weight-only FP8 GEMV with 128x128 block scales, the dense FP8
+    projection of this path: a weight is quantised once, on its first use
+    (experimental_fp8.register, keyed by data_ptr like the reference's
+    WEIGHTS table), and every later call reuses it. Activations stay bf16
+    and the sums fp32, for any M."""
+    if weight.data_ptr() not in experimental_fp8.WEIGHTS:
+        experimental_fp8.register(weight)
+    return experimental_fp8.linear(x, weight)
 
 
 def route(logits: torch.Tensor, k: int = 8):

@@ -1,22 +1,81 @@
 """Model-level MoE entry points with the reference's signatures
 (DramaModel.moe / moe_parts / routed_moe, src/drama3/model.py:485-583).
 
-`layer` is any object with:
-  experts                   routed expert container (w13_weight, ...)
-  shared_expert             shared expert container (E = 1 or unbatched)
-  router_weight             bf16 [E+1, H]: router rows + shared-expert gate row
-  router_bias (optional)    f32 [E], added to the router logits
+`layer` is either the reference's own MoE layer object or this package's
+container:
+  reference layer (src/drama3/model.py:195-245, 495-517):
+    experts                               routed FP8 experts (w13_weight,
+                                          w13_scale_inv, w2_weight, w2_scale_inv)
+    gate.weight                           bf16 [E, H] router
+    shared_expert_gate.weight             bf16 [1, H] shared-expert gate
+    shared_expert.gate_proj / up_proj / down_proj .weight
+                                          bf16 shared expert (or its
+                                          packed_gate_up [2I, H])
+  This package's container:
+    experts, shared_expert (FP8, E = 1), router_weight bf16 [E+1, H],
+    router_bias (optional) f32 [E], added to the router logits.
+A reference layer is converted once, on first use, and the result is cached
+on the layer (`_d3moe_view`): the router and shared-gate rows are packed into
+[E+1, H] (the packed projection of model.py:236-245) and the bf16 shared
+expert is quantised into 128x128 block-scaled FP8, the format the benchmark
+configurations give the shared expert.
 
 Routing always runs on the device (route_topk); the routed and shared experts
 run in the same launches of the expert engine. No host synchronisation, so a
 decode step built from these calls is CUDA-graph capturable.
+
+`decode` is accepted as in the reference. There it chooses the routing code
+(the Triton route kernel or torch softmax/top-k, model.py:522-528) and
+whether the shared expert runs on a side stream (model.py:506-517). Here both
+routings are the same computation (fp32 softmax over the bf16 logits, top-k
+with ties to the lower id, renormalised) and the shared expert already runs
+inside the routed experts' launches, so `decode` changes no result and no
+kernel: the kernel choice follows the token count, as the reference's own
+small_moe_max_batch / tuned-prefill switch does.
 """
 
 from __future__ import annotations
 
+from types import SimpleNamespace
+
 import torch
 
 from . import ops
+from .synth import ExpertWeights
+
+
+def _weight(module_or_tensor) -> torch.Tensor:
+    return module_or_tensor.weight if hasattr(module_or_tensor, "weight") else module_or_tensor
+
+
+def _quantize_expert(gate_up: torch.Tensor, down: torch.Tensor) -> ExpertWeights:
+    """bf16 gate_up [2I, H] (rows [gate | up]) and down [H, I] -> one FP8
+    expert with 128x128 block scales (experimental_fp8.py:10-18 quantiser)."""
+    w13, s13 = ops.fp8_quantize_weight(gate_up.to(torch.bfloat16).contiguous())
+    w2, s2 = ops.fp8_quantize_weight(down.to(torch.bfloat16).contiguous())
+    return ExpertWeights(w13[None], s13[None], w2[None], s2[None])
+
+
+def layer_view(layer):
+    """The (experts, shared_expert, router_weight, router_bias) view of `layer`
+    that the kernels take; reference layers are converted once and cached."""
+    if hasattr(layer, "router_weight"):
+        return layer
+    view = getattr(layer, "_d3moe_view", None)
+    if view is not None:
+        return view
+    router = _weight(layer.gate)
+    gate = _weight(layer.shared_expert_gate)
+    router_weight = torch.cat((router, gate.reshape(1, -1)), 0).to(torch.bfloat16).contiguous()
+    sh = layer.shared_expert
+    packed = getattr(sh, "packed_gate_up", None)
+    if packed is None:
+        packed = torch.cat((_weight(sh.gate_proj), _weight(sh.up_proj)), 0)
+    shared = _quantize_expert(packed, _weight(sh.down_proj))
+    view = SimpleNamespace(experts=layer.experts, shared_expert=shared, router_weight=router_weight,
+                           router_bias=getattr(layer, "router_bias", None))
+    layer._d3moe_view = view
+    return view
 
 
 class MoE:
@@ -49,6 +108,7 @@ class MoE:
 
     def moe(self, x: torch.Tensor, layer, decode: bool = False, *, row_slots=None) -> torch.Tensor:
         """out = routed + bf16(shared * bf16(sigmoid(gate))) in one pipeline."""
+        layer = layer_view(layer)
         slots, start = self._padding(row_slots)
         return ops.moe_layer(x, layer.router_weight, layer.experts, layer.shared_expert, self.top_k,
                              router_bias=getattr(layer, "router_bias", None),
@@ -61,6 +121,7 @@ class MoE:
         (src/drama3/mixed_model.py:200-246): moe_parts over x[keep] with the
         padding-router rule on row_slots, then combine_experts_add_norm(_inverse)
         into residual. Returns the normalised rows [len(residual), H]."""
+        layer = layer_view(layer)
         slots, start = self._padding(row_slots)
         T = len(keep) if keep is not None else len(x)
         return ops.moe_layer(x, layer.router_weight, layer.experts, layer.shared_expert, self.top_k,
@@ -71,6 +132,7 @@ class MoE:
 
     def moe_parts(self, x: torch.Tensor, layer, decode: bool = False, *, row_slots=None):
         """Returns (routed, shared, shared_gate) like model.py:490-518."""
+        layer = layer_view(layer)
         E = layer.experts.w13_weight.shape[0]
         logits = ops.router_logits(x, layer.router_weight)
         router, shared_gate = logits[:, :E], logits[:, E:E + 1]

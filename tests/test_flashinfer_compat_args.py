@@ -34,8 +34,9 @@ def args(**over):
     dict(routing_method_type=RoutingMethodType.DeepSeekV3),
     dict(routing_method_type=RoutingMethodType.Renormalize),
     dict(n_group=4, topk_group=2),
-    dict(use_shuffled_weight=True),
-    dict(weight_layout=WeightLayout.BlockMajorK),
+    dict(use_shuffled_weight=True),  # shuffled bytes need the BlockMajorK tag
+    dict(weight_layout=WeightLayout.BlockMajorK),  # and the tag needs shuffled bytes
+    dict(weight_layout=WeightLayout.MajorMn),
     dict(routed_scaling_factor=2.5),
     dict(do_finalize=False),
     dict(activation_type=4),
@@ -55,3 +56,24 @@ def test_unsupported_arguments_raise(over):
 def test_inconsistent_shapes_raise(over):
     with pytest.raises(ValueError):
         trtllm_fp8_block_scale_moe(**args(**over))
+
+
+def test_block_major_k_unshuffle_inverts_the_reference_shuffle():
+    """BlockMajorK weights (the reference's blocked_moe_weight, model.py:41-52,
+    restated here: K blocks to the front, rows permuted by FlashInfer's 64-row
+    epilogue map) come back to the MajorK bytes exactly, from the 4-D shape the
+    shuffle returns and from the same bytes viewed [E, rows, K]."""
+    pytest.importorskip("flashinfer")
+    from flashinfer.utils import get_shuffle_matrix_a_row_indices
+
+    from d3moe.flashinfer_compat import unshuffle_block_major_k
+
+    g = torch.Generator().manual_seed(0)
+    for E_, rows, K in ((2, 256, 384), (3, 1536, 2048)):
+        w = torch.randint(0, 256, (E_, rows, K), generator=g, dtype=torch.uint8)
+        order = get_shuffle_matrix_a_row_indices(w[0], 64)
+        blocked = w.view(E_, rows, K // 128, 128).permute(0, 2, 1, 3)[:, :, order, :].contiguous()
+        for shaped in (blocked, blocked.view(E_, rows, K)):
+            back = unshuffle_block_major_k(shaped.view(torch.float8_e4m3fn))
+            assert back.shape == (E_, rows, K)
+            assert torch.equal(back.view(torch.uint8), w)

@@ -107,3 +107,35 @@ def test_local_expert_offset(layer):
     assert ((local >= 0) & (local < E)).any() and ((local < 0) | (local >= E)).any()
     ref = O.moe_experts_q(fp8_bytes(q), s.cpu().numpy().T, local, O.bf16_round(w_o), ex)
     assert_close(out.float().cpu().numpy(), ref, what="local experts")
+
+
+def test_block_major_k_weights_give_the_major_k_result(layer):
+    """Weights shuffled into FlashInfer's BlockMajorK layout the way the
+    reference does it (blocked_moe_weight, model.py:41-52, restated: K blocks
+    first, rows permuted by FlashInfer's 64-row epilogue map), passed with
+    use_shuffled_weight=True and weight_layout=BlockMajorK, give the MajorK
+    call's output bit for bit."""
+    pytest.importorskip("flashinfer")
+    from flashinfer.utils import get_shuffle_matrix_a_row_indices
+
+    from d3moe.flashinfer_compat import WeightLayout, trtllm_fp8_block_scale_moe
+
+    lw, fi, _ = layer
+    _, q, s, logits = inputs(64, E, seed=5)
+
+    def blocked(w):
+        e_, rows, k_ = w.shape
+        order = get_shuffle_matrix_a_row_indices(w[0].view(torch.uint8).cpu(), 64).to(w.device)
+        b = w.view(torch.uint8).view(e_, rows, k_ // 128, 128).permute(0, 2, 1, 3)[:, :, order, :]
+        return b.contiguous().view(w.dtype)
+
+    ref = call(logits, None, q, s, fi, E)
+    out = trtllm_fp8_block_scale_moe(
+        routing_logits=logits, routing_bias=None, hidden_states=q, hidden_states_scale=s,
+        gemm1_weights=blocked(fi[0]), gemm1_weights_scale=fi[1], gemm2_weights=blocked(fi[2]),
+        gemm2_weights_scale=fi[3], num_experts=E, top_k=K, n_group=None, topk_group=None,
+        intermediate_size=I, local_expert_offset=0, local_num_experts=E, routed_scaling_factor=1.0,
+        routing_method_type=4, use_shuffled_weight=True, weight_layout=WeightLayout.BlockMajorK,
+        tune_max_num_tokens=4096, enable_pdl=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)

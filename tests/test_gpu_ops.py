@@ -186,6 +186,27 @@ def test_dense_fp8_golden(d3, golden):
     assert ulps_bf16(from_bf16(y), O.bf16_from_bits(g["y"])).max() <= 1
 
 
+@pytest.mark.parametrize("T", [1, 64])
+def test_dense_fp8_gemv_every_e4m3_code(d3, T):
+    """Weights holding every non-NaN E4M3 code (zeros, subnormals, +-448) in
+    every position of a 128-byte row, and activations spanning many binades
+    within a group (so the activation split meets tiny elements): the result
+    is the float64 value correctly rounded, up to fp32 summation-order noise."""
+    codes = np.array([c for c in range(256) if c not in (0x7F, 0xFF)], np.uint8)
+    N, K = 256, 512
+    idx = (np.arange(N)[:, None] * 7 + np.arange(K)[None, :]) % len(codes)
+    q = codes[idx]
+    rng = np.random.default_rng(11)
+    s = rng.uniform(1e-4, 1e-2, (N // 128, K // 128)).astype(np.float32)
+    x = O.bf16_round((rng.standard_normal((T, K)) * np.exp(rng.uniform(-12, 3, (T, K)))).astype(np.float32))
+    y = d3["ops"].fp8_gemv(to_bf16(x), to_fp8(q), torch.from_numpy(s).cuda(), n=N)
+    got = from_bf16(y)
+    exact = x.astype(np.float64) @ O.dequant_blocks(q, s).astype(np.float64).T
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exact), 1e-30))) - 7)
+    bound = 0.5 * ulp + np.sqrt((exact ** 2).mean()) * 2.0 ** -16
+    assert (np.abs(got - exact) <= bound).all()
+
+
 @pytest.mark.parametrize("T", [1, 8, 16, 32, 64, 100])
 # the benchmark's QKV and o_proj, an odd size, and the reference model's real
 # projections: QKV 9216x2048, GDN in 12352x2048, out / o_proj 2048x4096

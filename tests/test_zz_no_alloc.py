@@ -21,7 +21,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from helpers import assert_close, from_bf16, to_bf16, to_fp8, ulps_bf16  # noqa: E402
+from helpers import assert_close, from_bf16, to_bf16, to_fp8  # noqa: E402
 from oracle import moe_oracle as O  # noqa: E402
 
 
@@ -30,7 +30,18 @@ def _case(T, N, K, seed):
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     q, s = O.quantize_weight_blocks(w)
     x = O.bf16_round(rng.standard_normal((T, K)).astype(np.float32))
-    return to_bf16(x), to_fp8(q), torch.from_numpy(s).cuda()
+    return x, q, s
+
+
+def _within_rounding_bound(got, x, q, s, N, what):
+    """The float64 value of the same dequantise-then-matmul, correctly rounded
+    to bf16 up to fp32 summation-order noise (half a bf16 ulp + 2^-16 of the
+    output rms): the bound every dense GEMV test of this library uses."""
+    exact = x.astype(np.float64) @ O.dequant_blocks(q, s)[:N].astype(np.float64).T
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exact), 1e-30))) - 7)
+    bound = 0.5 * ulp + np.sqrt((exact ** 2).mean()) * 2.0 ** -16
+    excess = np.abs(got - exact) - bound
+    assert (excess <= 0).all(), f"{what}: {float(excess.max())} above the rounding bound"
 
 
 def _noalloc(x, wq, s, N):
@@ -57,14 +68,18 @@ def test_noalloc_gemv_matches_workspace_gemv_on_consecutive_calls():
     cases = ((64, 4096, 2048, 1), (13, 2048, 4096, 2), (1, 4096 - 64, 4096, 3),
              (1, 2048, 2048, 4), (64, 4096, 4096, 5))
     for T, N, K, seed in cases:
-        x, wq, s = _case(T, N, K, seed)
+        xn, qn, sn = _case(T, N, K, seed)
+        x, wq, s = to_bf16(xn), to_fp8(qn), torch.from_numpy(sn).cuda()
         got = from_bf16(_noalloc(x, wq, s, N))
         ref = from_bf16(ops.fp8_gemv(x, wq, s, n=N))
         torch.cuda.synchronize()
-        # same products; the K-split count may differ, so the fp32 sums may
-        # round to neighbouring bf16 values
-        assert ulps_bf16(got, ref).max() <= 1
-        assert_close(got, ref, what=f"noalloc gemv T={T} N={N} K={K}")
+        # the two entry points add the same products in different orders, so
+        # each is held to the exact value's rounding bound, and to each other
+        # within the layer tolerance
+        what = f"noalloc gemv T={T} N={N} K={K}"
+        _within_rounding_bound(got, xn, qn, sn, N, what)
+        _within_rounding_bound(ref, xn, qn, sn, N, what + " (workspace entry point)")
+        assert_close(got, ref, what=what)
     dev = torch.device("cuda")
     assert _noalloc_status(dev) == 0, "a bounded wait of the no-allocation GEMV timed out"
     assert _noalloc_status(dev) == 0, "the status word was not cleared by the read"
