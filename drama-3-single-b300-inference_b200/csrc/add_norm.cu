@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kNormThreads)
                     const __nv_bfloat16* __restrict__ weights, int k, int P,
                     __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ norm_w,
                     float eps, int W, __nv_bfloat16* __restrict__ out, RowGather rows) {
-  pdl_wait();
+  pdl_enter();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   const int nchunks = W / 8;

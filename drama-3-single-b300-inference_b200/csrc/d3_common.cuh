@@ -63,6 +63,17 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Entry of the library's short kernels: allow the next kernel of the stream
+// to start launching right away, then wait for the previous one. The next
+// kernel is released only once every CTA of this grid has executed the
+// trigger (so all of them are resident and none can be starved of an SM by
+// it), and its own pdl_wait() still waits for this whole grid to complete,
+// so only launch latency and prologue overlap, never data.
+__device__ __forceinline__ void pdl_enter() {
+  pdl_trigger();
+  pdl_wait();
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -35,6 +35,18 @@ void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
                           cudaStream_t s, int32_t* zero = nullptr, int nzero = 0,
                           const RowGather& rg = RowGather{});
 
+// The bucketing (block_m = 1: counts, starts, total, inverse rows, active list)
+// fused with launch_quant_scatter, one CTA per token, for fewer than
+// kFusedPermuteMaxPairs pairs and E <= kFusedPermuteMaxExperts. Same outputs
+// as launch_permute followed by launch_quant_scatter.
+constexpr int kFusedPermuteMaxPairs = 2048;
+constexpr int kFusedPermuteMaxExperts = 1024;
+void launch_permute_quant(const void* x, int64_t x_stride, int T, int H, int k, const int64_t* ids,
+                          int E, int with_shared, uint8_t* xq, float* sx, int32_t* counts,
+                          int32_t* starts, int32_t* total, int32_t* inv_rows, int32_t* active,
+                          int32_t* n_active, cudaStream_t s, int32_t* zero = nullptr, int nzero = 0,
+                          const RowGather& rg = RowGather{});
+
 // Already-quantised activations (q e4m3 [T,H], scales [H/128,T] when
 // transposed, else [T,H/128]) copied into expert order like
 // launch_quant_scatter (routed rows only).

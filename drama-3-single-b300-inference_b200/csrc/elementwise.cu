@@ -73,7 +73,7 @@ __device__ __forceinline__ RowPair row_pair(int G) {
 __global__ void quant_act_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                  int H, uint8_t* __restrict__ q, float* __restrict__ scales,
                                  int transposed) {
-  pdl_wait();
+  pdl_enter();
   const int G = H / 128;
   const RowPair rp = row_pair(G);
   if (rp.row >= T) return;
@@ -87,7 +87,7 @@ __global__ void prepare_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
                                int T, int H, int E, const void* row_slots, int slots64,
                                int64_t padding_start, uint8_t* __restrict__ q,
                                float* __restrict__ scales_t, float* __restrict__ logits) {
-  pdl_wait();
+  pdl_enter();
   const int G = H / 128;
   const RowPair rp = row_pair(G);
   const int row = rp.row;
@@ -116,7 +116,7 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
                                      int with_shared, uint8_t* __restrict__ xq,
                                      float* __restrict__ sx, int32_t* __restrict__ zero, int nzero,
                                      RowGather rg) {
-  pdl_wait();
+  pdl_enter();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   const int G = H / 128;
@@ -146,6 +146,111 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
   }
 }
 
+// Bucketing and activation quantisation in one kernel, for calls of fewer
+// than kFusedPermuteMaxPairs pairs (the decode sizes). CTA t owns token t:
+//   * the expert-ordered row of each of its pairs p = t*k + j is the pair's
+//     position in the stable counting sort of all pairs by expert, i.e. the
+//     number of valid pairs q with (ids[q], q) < (ids[p], p); one warp counts
+//     it for one pair by scanning all P ids (ids outside [0, E) are skipped
+//     and get row -1). This is the row the one-CTA permute kernel assigns.
+//   * the token's row is quantised once (1x128 E4M3) and written to those
+//     rows and, with a shared expert, to row P + t, as quant_scatter_kernel.
+// CTA 0 also writes the per-expert counts and starts, the total, the active
+// expert list and its length (the outputs of the permute kernel with
+// block_m = 1) and zeroes `zero` (the engines' work counters).
+__global__ void __launch_bounds__(256)
+    permute_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T, int H, int k,
+                         const int64_t* __restrict__ ids, int E, int with_shared,
+                         uint8_t* __restrict__ xq, float* __restrict__ sx,
+                         int32_t* __restrict__ counts, int32_t* __restrict__ starts,
+                         int32_t* __restrict__ total, int32_t* __restrict__ inv_rows,
+                         int32_t* __restrict__ active, int32_t* __restrict__ n_active,
+                         int32_t* __restrict__ zero, int nzero, RowGather rg) {
+  pdl_enter();
+  __shared__ int slot[32];
+  __shared__ int hist[kFusedPermuteMaxExperts];
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = T * k;
+  for (int j = warp; j < k; j += 8) {
+    const int p = t * k + j;
+    const int64_t e = __ldg(ids + p);
+    const bool ok = e >= 0 && e < E;
+    int c = 0;
+    if (ok)
+      for (int q = lane; q < P; q += 32) {
+        const int64_t f = __ldg(ids + q);
+        c += (f >= 0 && f < E && (f < e || (f == e && q < p))) ? 1 : 0;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == 0) {
+      slot[j] = ok ? c : -1;
+      inv_rows[p] = ok ? c : -1;
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    for (int q = threadIdx.x; q < P; q += blockDim.x) {
+      const int64_t f = __ldg(ids + q);
+      if (f >= 0 && f < E) atomicAdd(&hist[f], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int run = 0, nact = 0;
+      for (int base = 0; base < E; base += 32) {
+        const int e = base + lane;
+        const int c = e < E ? hist[e] : 0;
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const unsigned act = __ballot_sync(0xffffffffu, c > 0);
+        if (e < E) {
+          counts[e] = c;
+          starts[e] = run + incl - c;
+          if (c > 0) active[nact + __popc(act & ((1u << lane) - 1u))] = e;
+        }
+        run += __shfl_sync(0xffffffffu, incl, 31);
+        nact += __popc(act);
+      }
+      if (lane == 0) {
+        total[0] = run;
+        n_active[0] = nact;
+      }
+    }
+  }
+  __syncthreads();
+  const int G = H / 128;
+  const int half = lane >> 4, hl = lane & 15;
+  const int64_t src = gather_row(rg, t);
+  for (int gp = warp; gp < (G + 1) / 2; gp += 8) {
+    const int g = 2 * gp + half;
+    const bool valid = g < G;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + src * x_stride + g * 128 + hl * 8));
+    float f[8];
+    unpack_bf16x8(v, f);
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    amax = half_warp_max(amax);
+    const float scale = act_scale_from_amax(amax);
+    const uint2 qb = quant8(f, scale);
+    if (!valid) continue;
+    const int ndest = k + (with_shared ? 1 : 0);
+    for (int j = 0; j < ndest; ++j) {
+      const int d = j < k ? slot[j] : P + t;
+      if (d < 0) continue;
+      *reinterpret_cast<uint2*>(xq + static_cast<int64_t>(d) * H + g * 128 + hl * 8) = qb;
+      if (hl == 0) sx[static_cast<int64_t>(d) * G + g] = scale;
+    }
+  }
+}
+
 // Already-quantised activations into expert order (the FlashInfer calling
 // convention): q e4m3 [T, H] rows are copied unchanged to rows inv_rows[t*k + j]
 // (negative = skipped) and their group scales, read from [H/128, T]
@@ -155,7 +260,7 @@ __global__ void prequant_scatter_kernel(const uint8_t* __restrict__ q, int64_t q
                                         int k, const int32_t* __restrict__ inv_rows,
                                         uint8_t* __restrict__ xq, float* __restrict__ sx,
                                         int32_t* __restrict__ zero, int nzero) {
-  pdl_wait();
+  pdl_enter();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   const int chunks = H / 16, G = H / 128;
@@ -192,7 +297,7 @@ __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64
                                       int32_t* __restrict__ zero, int nzero,
                                       const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                       int mode) {
-  pdl_wait();
+  pdl_enter();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   const int G = K / 128;
@@ -255,7 +360,7 @@ __global__ void dense_split_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                    int mode, uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
                                    float* __restrict__ sc) {
-  pdl_wait();
+  pdl_enter();
   const int G = K / 128;
   const RowPair rp = row_pair(G);
   const int row = rp.row;
@@ -317,7 +422,7 @@ __device__ __forceinline__ float silu_bf16(float gate_bf16) {
 
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride, int rows,
                                 int W, __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = W / 8;
   if (idx >= static_cast<int64_t>(rows) * per_row) return;
@@ -340,7 +445,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t in
 __global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride,
                                       int rows, int W, uint8_t* __restrict__ q,
                                       float* __restrict__ scales) {
-  pdl_wait();
+  pdl_enter();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int G = W / 128;
@@ -382,7 +487,7 @@ __global__ void combine_experts_kernel(const __nv_bfloat16* __restrict__ routed,
                                        const __nv_bfloat16* __restrict__ shared,
                                        const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                        int T, int H, __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = H / 8;
   if (idx >= static_cast<int64_t>(T) * per_row) return;
@@ -425,7 +530,7 @@ __global__ void combine_rows_kernel(const void* __restrict__ d, int H,
                                     int64_t gate_stride, __nv_bfloat16* __restrict__ routed_out,
                                     __nv_bfloat16* __restrict__ shared_out,
                                     __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = H / 4;
   if (idx >= static_cast<int64_t>(T) * per_row) return;
@@ -478,7 +583,7 @@ __global__ void combine_rows_kernel(const void* __restrict__ d, int H,
 // One CTA per 128x128 weight block; 256 threads x 64 elements.
 __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, int K,
                                     uint8_t* __restrict__ q, float* __restrict__ scales) {
-  pdl_wait();
+  pdl_enter();
   const int nb = blockIdx.x, kb = blockIdx.y, KB = K / 128;
   __shared__ float red[8];
   const int tid = threadIdx.x;
@@ -527,7 +632,7 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, 
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t src_stride,
                                    int T, int H, int k, const int32_t* __restrict__ sorted_pairs,
                                    int rows, __nv_bfloat16* __restrict__ dst) {
-  pdl_wait();
+  pdl_enter();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int p = sorted_pairs[row];
@@ -546,7 +651,7 @@ __global__ void combine_pairs_kernel(const __nv_bfloat16* __restrict__ rows, int
                                      const __nv_bfloat16* __restrict__ shared,
                                      const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                      __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = H / 8;
   if (idx >= static_cast<int64_t>(T) * per_row) return;
@@ -589,7 +694,7 @@ __global__ void ep_dispatch_meta_kernel(const int64_t* __restrict__ ids,
                                         int experts_per_rank, int ranks,
                                         int64_t* __restrict__ meta_ids,
                                         __nv_bfloat16* __restrict__ meta_w) {
-  pdl_wait();
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n = static_cast<int64_t>(ranks) * T * k;
   if (idx >= n) return;
@@ -609,7 +714,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
                                const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
                                int T, int k, int H, int experts_per_rank, int ranks, int row_bytes,
                                uint8_t* __restrict__ send) {
-  pdl_wait();
+  pdl_enter();
   const int chunks = row_bytes / 16;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n = static_cast<int64_t>(ranks) * T * chunks;
@@ -651,7 +756,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_st
 __global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, int rows, int k, int H,
                                       int row_bytes, int64_t* __restrict__ ids,
                                       __nv_bfloat16* __restrict__ w) {
-  pdl_wait();
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(rows) * k) return;
   const int64_t r = idx / k;
@@ -678,6 +783,17 @@ void launch_quant_scatter(const void* x, int64_t x_stride, int T, int H, int k,
   launch_kernel(quant_scatter_kernel, dim3(pair_blocks(T, H)), dim3(256), 0, s,
                 static_cast<const __nv_bfloat16*>(x), x_stride, T, H, k, inv_rows, P, with_shared, xq,
                 sx, zero, nzero, rg);
+}
+
+void launch_permute_quant(const void* x, int64_t x_stride, int T, int H, int k, const int64_t* ids,
+                          int E, int with_shared, uint8_t* xq, float* sx, int32_t* counts,
+                          int32_t* starts, int32_t* total, int32_t* inv_rows, int32_t* active,
+                          int32_t* n_active, cudaStream_t s, int32_t* zero, int nzero,
+                          const RowGather& rg) {
+  if (T <= 0) return;
+  launch_kernel(permute_quant_kernel, dim3(T), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x),
+                x_stride, T, H, k, ids, E, with_shared, xq, sx, counts, starts, total, inv_rows, active,
+                n_active, zero, nzero, rg);
 }
 
 void launch_prequant_scatter(const uint8_t* q, int64_t q_stride, const float* qs, int transposed,

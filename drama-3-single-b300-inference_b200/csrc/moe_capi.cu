@@ -246,6 +246,12 @@ struct PreQuant {
   int transposed = 0;
 };
 
+// Whether the bucketing of a call runs fused into the activation
+// quantisation (one CTA per token, every CTA counting over all pairs).
+bool fused_permute(int T, int k, int E) {
+  return static_cast<int64_t>(T) * k < kFusedPermuteMaxPairs && E <= kFusedPermuteMaxExperts;
+}
+
 // Whether the expert GEMMs of a T-token call run on tcgen05 (prefill) or on
 // the decode engine. Both stages of a call take this decision the same way,
 // so the threshold must not change between them.
@@ -278,19 +284,26 @@ int experts_up(const void* x, int64_t x_stride, const int64_t* ids, int T, int k
   const int has_shared = sh ? 1 : 0;
   const int R = P + (has_shared ? T : 0);
   int rc = D3_OK;
-  if (!permuted) {
-    // the pipeline reads counts, starts, the inverse map and the active list;
-    // the reference's sorted-pair and per-tile expert buffers are not written
-    rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
-                        b.inv, b.active, b.n_active, s, b.permute_scratch);
-    if (rc) return rc;
+  if (!permuted && !pq.q && fused_permute(T, k, E)) {
+    // decode sizes: bucketing and activation quantisation in one kernel
+    launch_permute_quant(x, x_stride, T, H, k, ids, E, has_shared, b.xq, b.sx, b.counts, b.starts,
+                         b.total, b.inv, b.active, b.n_active, s, b.work, 2, rg);
+    if ((rc = check_launch("permute_quant"))) return rc;
+  } else {
+    if (!permuted) {
+      // the pipeline reads counts, starts, the inverse map and the active list;
+      // the reference's sorted-pair and per-tile expert buffers are not written
+      rc = launch_permute(ids, T, k, E, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
+                          b.inv, b.active, b.n_active, s, b.permute_scratch);
+      if (rc) return rc;
+    }
+    if (pq.q)
+      launch_prequant_scatter(pq.q, pq.q_stride, pq.scales, pq.transposed, T, H, k, b.inv, b.xq,
+                              b.sx, s, b.work, 2);
+    else
+      launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2, rg);
+    if ((rc = check_launch("quant_scatter"))) return rc;
   }
-  if (pq.q)
-    launch_prequant_scatter(pq.q, pq.q_stride, pq.scales, pq.transposed, T, H, k, b.inv, b.xq, b.sx,
-                            s, b.work, 2);
-  else
-    launch_quant_scatter(x, x_stride, T, H, k, b.inv, P, has_shared, b.xq, b.sx, s, b.work, 2, rg);
-  if ((rc = check_launch("quant_scatter"))) return rc;
 
   const int sms = sm_count();
   stage_mark(1, s);
@@ -685,12 +698,19 @@ static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
   launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s, rg);
   if ((rc = check_launch("router_logits"))) return rc;
   const int P = T * k;
-  rc = launch_route_permute(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts,
-                            D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
-                            b.inv, b.active, b.n_active, s, b.permute_scratch, pr);
-  if (rc) return rc;
+  const bool fused = fused_permute(T, k, E);
+  if (fused) {
+    // the bucketing runs inside the quantisation kernel of run_experts
+    launch_route_topk(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts, D3_DTYPE_BF16, s, pr);
+    if ((rc = check_launch("route_topk"))) return rc;
+  } else {
+    rc = launch_route_permute(b.logits, D3_DTYPE_BF16, E + 1, T, E, k, nullptr, ids, wts,
+                              D3_DTYPE_BF16, 1, b.counts, b.starts, b.total, nullptr, nullptr, P,
+                              b.inv, b.active, b.n_active, s, b.permute_scratch, pr);
+    if (rc) return rc;
+  }
   return run_experts(x, x_stride, ids, wts, T, k, experts, shared, b.logits + E, E + 1, nullptr,
-                     nullptr, out, b, st, s, true, an, rg);
+                     nullptr, out, b, st, s, !fused, an, rg);
 }
 
 extern "C" int d3_moe_layer(const void* x, int64_t x_stride, const void* router_w,

@@ -25,7 +25,7 @@ __global__ void __launch_bounds__(256)
                          const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
                          int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
                          int64_t out_stride, RowGather rg) {
-  pdl_wait();
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kRtThreads)
                                const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
                                int nbias, int R, int H, int T, __nv_bfloat16* __restrict__ out,
                                int64_t out_stride, RowGather rg) {
-  pdl_wait();
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -296,7 +296,7 @@ __global__ void route_kernel(const void* __restrict__ logits, int f32_in, int64_
                              int E, int k, const float* __restrict__ bias,
                              int64_t* __restrict__ ids, void* __restrict__ weights, int f32_out,
                              PaddingRoute pr) {
-  pdl_wait();
+  pdl_enter();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
   route_token<PER_LANE>(logits, f32_in, stride, t, padding_row(pr, t) ? 0 : t, E, k, bias, ids,
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
                    int32_t* __restrict__ expert_ids, int64_t max_rows,
                    int32_t* __restrict__ inv_rows, int32_t* __restrict__ active,
                    int32_t* __restrict__ n_active) {
-  pdl_wait();
+  pdl_enter();
   extern __shared__ int sm[];
   auto id_at = [&](int p) -> int {
     const int64_t v = ids[p];
@@ -463,7 +463,7 @@ inline int permute_chunk_pairs(int P) {
 __global__ void __launch_bounds__(kPermuteThreads)
     permute_hist_kernel(const int64_t* __restrict__ ids, int P, int E, int chunk,
                         int32_t* __restrict__ cc) {
-  pdl_wait();
+  pdl_enter();
   extern __shared__ int cnt[];
   for (int e = threadIdx.x; e < E; e += kPermuteThreads) cnt[e] = 0;
   __syncthreads();
@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
                         int32_t* __restrict__ total_out, int32_t* __restrict__ sorted_ids,
                         int32_t* __restrict__ expert_ids, int64_t max_rows,
                         int32_t* __restrict__ active, int32_t* __restrict__ n_active) {
-  pdl_wait();
+  pdl_enter();
   __shared__ int warp_tot[33];
   __shared__ int s_cnt[1024], s_start[1024];
   __shared__ int s_part[kPermuteThreads];  // [part][E] chunk-slice sums, then their offsets
@@ -558,7 +558,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
     permute_scatter_kernel(const int64_t* __restrict__ ids, int P, int E, int chunk,
                            const int32_t* __restrict__ cc, int32_t* __restrict__ sorted_ids,
                            int32_t* __restrict__ inv_rows) {
-  pdl_wait();
+  pdl_enter();
   extern __shared__ int sm[];
   int* cursor = sm;        // [E]
   int* wcnt = sm + E;      // [32][E]
@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(kPermuteThreads)
                    int32_t* __restrict__ total, int32_t* __restrict__ sorted_pairs,
                    int32_t* __restrict__ scratch_tiles, int32_t* __restrict__ inv_rows,
                    int64_t* __restrict__ local_ids) {
-  pdl_wait();
+  pdl_enter();
   extern __shared__ int sm[];
   const int E = experts_per_rank * ranks;
   auto id_at = [&](int p) -> int {
