@@ -1436,6 +1436,38 @@ def main() -> None:
         if int(status.item()) != 0:
             raise RuntimeError(f"device status word {int(status.item())}: a bounded wait timed out")
 
+    # ---- the MoE layer alone, captured and replayed the same way (no stage
+    # events between its kernels, so their launches overlap as in the step):
+    # the layer time the HBM roofline target is quoted on
+    layer_graph_ms = None
+    if not args.eager:
+        lgraphs = []
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            for li in range(args.layers):
+                g = torch.cuda.CUDAGraph()
+                lw = layers[li]
+                ev, sv = views[li]
+                with torch.cuda.graph(g, stream=cap):
+                    _lib.call("d3_moe_layer", o.data_ptr(), o.stride(0), lw.router.data_ptr(), None, T,
+                              TOPK, ctypes.byref(ev.struct), ctypes.byref(sv.struct), y.data_ptr(), None,
+                              wts.data_ptr(), ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(),
+                              cap.cuda_stream)
+                lgraphs.append(g)
+        stream.wait_stream(cap)
+        for i in range(args.warmup):
+            lgraphs[i % args.layers].replay()
+        torch.cuda.synchronize(dev)
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for i in range(args.steps):
+            lgraphs[i % args.layers].replay()
+        l1.record(stream)
+        torch.cuda.synchronize(dev)
+        layer_graph_ms = l0.elapsed_time(l1) / args.steps
+        del lgraphs
+
     # ---- end-to-end through the C ABI with host buffers (pinned H2D + D2H per step)
     hx = torch.randn((T, H)).to(torch.bfloat16).pin_memory()
     hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
@@ -1517,6 +1549,9 @@ def main() -> None:
             "down_kernel": {"achieved": down_bytes / (down_avg * 1e-3) / 1e9, "avg_launch_ms": down_avg,
                             "algorithmic_bytes_per_launch": down_bytes},
             "moe_layer_ms": statistics.mean(moe_ms),
+            "moe_layer_graph_ms": layer_graph_ms,
+            "moe_layer_frac": (None if layer_graph_ms is None else
+                               (gate_bytes + down_bytes) / (layer_graph_ms * 1e-3) / 1e9 / pk["hbm_gbs"]),
             "stage_ms": {"qkv_gemv": statistics.mean(qkv_ms), "o_proj_gemv": statistics.mean(oproj_ms),
                          "router_route_permute_quant": statistics.mean(pre_ms),
                          "gate_up": gate_avg, "down": down_avg, "combine": statistics.mean(post_ms)},

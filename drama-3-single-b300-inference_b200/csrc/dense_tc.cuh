@@ -117,8 +117,13 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&r)[N]) {
   }
 }
 
+// Relaxed arrival: no release ordering of this thread's earlier memory
+// operations (with .release the arrive waited for the weight TMA loads thread 0
+// had just issued, over a microsecond). The barriers' visibility comes from
+// fence.mbarrier_init.release.cluster, and the pushes complete through the
+// receivers' mbarriers, so the cluster barriers only order lifetimes.
 __device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
