@@ -272,7 +272,7 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     import torch.distributed as dist
 
     from d3moe import _lib, ops, synth
-    from d3moe.ep import CudaEPOps, ExpertParallelMoE
+    from d3moe.ep import CudaEPOps, ExpertParallelMoE, ep_row_bytes_fp8
 
     T = args.tokens
     lib = _lib.load()
@@ -280,24 +280,55 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     stage = {"events": None}
 
     class TimedOps(CudaEPOps):
-        """Records the stage events around this rank's routed-expert launches."""
+        """Marks the EP stage boundaries on the current stream (EP_STAGES) and
+        records the library's stage events around the routed-expert call."""
 
-        def local_experts_k(self, rows, ids, weights, experts):
+        marks = None  # name -> torch.cuda.Event while stage timing is on
+
+        def mark(self, name):
+            if self.marks is not None:
+                self.marks[name].record(torch.cuda.current_stream(dev))
+
+        def router_logits(self, x, router_weight):
+            self.mark("layer")
+            return super().router_logits(x, router_weight)
+
+        def pack_fp8(self, *a, **kw):
+            self.mark("pack")
+            return super().pack_fp8(*a, **kw)
+
+        def unpack_fp8(self, *a, **kw):
+            self.mark("dispatched")
+            return super().unpack_fp8(*a, **kw)
+
+        def local_experts_fp8(self, *a, **kw):
+            self.mark("experts")
             if stage["events"] is not None:
                 lib.d3_set_stage_events(stage["events"], 5)
             try:
-                return super().local_experts_k(rows, ids, weights, experts)
+                out = super().local_experts_fp8(*a, **kw)
             finally:
                 lib.d3_set_stage_events(None, 0)
+            self.mark("experts_done")
+            return out
+
+        def combine(self, *a, **kw):
+            self.mark("combine")
+            out = super().combine(*a, **kw)
+            self.mark("end")
+            return out
 
     eops = TimedOps()
-    layers, dense = [], []
+    layers, dense, routers, experts_all, shareds = [], [], [], [], []
     for li in range(args.layers):
         gen = torch.Generator(device="cpu")
         gen.manual_seed(li)
         router = (torch.randn((E + 1, H), generator=gen) * 0.02).to(torch.bfloat16).to(dev)
         experts = synth.make_experts(E_local, I, H, 1000 * li + 7 + rank, dev)
         shared = synth.make_experts(1, I, H, 1000 * li + 3, dev)
+        routers.append(router)
+        experts_all.append(experts)
+        shareds.append(shared)
         layers.append(ExpertParallelMoE(router, experts, shared, E, TOPK, ops=eops))
         g = torch.Generator(device=dev)
         g.manual_seed(li + 77)
@@ -326,6 +357,7 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     def step(i, x, keep_ids=False):
         li = i % args.layers
         wq, sq, wo_, so_ = dense[li]
+        eops.mark("step")
         gemv(x, wq, sq, N_QKV, qkv)
         gemv(qkv, wo_, so_, N_O, o)
         out, ids, _ = layers[li].forward(o, return_routing=True)
@@ -345,6 +377,7 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
     # input is copied into the graph's static buffer before each replay.
     graphs, x_static, y_static = [], [], []
     graph_ms = None
+    kernels = None
     if not args.eager:
         cap = torch.cuda.Stream(dev)
         cap.wait_stream(stream)
@@ -352,7 +385,7 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
             for li in range(args.layers):
                 xb = xs[li % len(xs)].clone()
                 step(li, xb)  # warm the capture stream's allocations
-                g = torch.cuda.CUDAGraph()
+                g = torch.cuda.CUDAGraph(keep_graph=(li == 0))
                 with torch.cuda.graph(g, stream=cap):
                     yb = step(li, xb)
                 graphs.append(g)
@@ -361,6 +394,7 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
         stream.wait_stream(cap)
         torch.cuda.synchronize(dev)
         dist.barrier()
+        kernels = graph_kernels(graphs[0])
         # the replay must reproduce the eager step bit for bit
         y_eager = step(0, x_static[0]).clone()
         y_static[0].zero_()
@@ -389,6 +423,11 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
         t = torch.tensor([graph_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         graph_ms = float(t.item())
+
+    # per-stage split of one step, from a graph of layer 0 with timing event
+    # nodes at the stage boundaries (external events), replayed and read back
+    stages = ep_stage_times(eops, lambda xb: step(0, xb), xs[0].clone(), dev, stream, reps=20)
+    dist.barrier()
 
     stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     for evs in stage_events:
@@ -480,7 +519,9 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
                           "weighted partial rows back; no host synchronisation)",
             "launch": "eager" if graph_ms is None else "one CUDA graph per weight set (kernels + NCCL), replayed",
             "eager_ms_per_step": eager_ms,
+            "dispatch_row_bytes": ep_row_bytes_fp8(H, TOPK),
         },
+        "stages_ms": stages,
         "roofline": {
             "bound": "hbm",
             "kernel": "expert_gemv_kernel<EPI_GATE_UP> on the rank's received rows (rank 0)",
@@ -492,16 +533,186 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
                 "ms_per_step": e2e_ms},
-        # dense 2 x (activation split + tcgen05 GEMV), router, route, dispatch meta, routed experts
-        # (permute, gather, gate_up, down, combine), shared expert (the same five), combine_pairs
-        "gpu_launches": 18 * args.steps,
+        # counted from the captured step graph's kernel nodes when it could be read, else by hand:
+        # dense 2 x (activation split + tcgen05 GEMV), router, route, FP8 pack, unpack, routed
+        # experts (permute, scatter, gate_up, down, combine), shared expert (permute+quant, gate_up,
+        # down, combine), combine_pairs
+        "gpu_launches": (kernels["ours"] if kernels else 18) * args.steps,
+        "graph_kernels_per_step": kernels,
         "clocks": clocks.summary(),
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     # graphs holding NCCL work are released before the process group goes
     del graphs, x_static, y_static
     torch.cuda.synchronize(dev)
+    if not args.no_extras:
+        line["config5"] = ep_config5(args, eops, routers, experts_all, shareds, world, rank, dev, stream)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def graph_kernels(g) -> dict | None:
+    """Kernel nodes of a captured CUDA graph (created with keep_graph=True),
+    by origin: this library's (mangled names in namespace d3), NCCL's, and
+    the rest (torch copies and fills). None when the graph cannot be read."""
+    try:
+        from cuda.bindings import driver as cu
+
+        h = cu.CUgraph(g.raw_cuda_graph())
+        err, _, n = cu.cuGraphGetNodes(h, 0)
+        if err != cu.CUresult.CUDA_SUCCESS:
+            return None
+        err, nodes, n = cu.cuGraphGetNodes(h, n)
+        out = {"ours": 0, "nccl": 0, "other": 0}
+        for nd in nodes[:n]:
+            err, typ = cu.cuGraphNodeGetType(nd)
+            if err != cu.CUresult.CUDA_SUCCESS or typ != cu.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+                continue
+            err, prm = cu.cuGraphKernelNodeGetParams(nd)
+            if err != cu.CUresult.CUDA_SUCCESS:
+                return None
+            err, name = cu.cuFuncGetName(prm.func)
+            name = name.decode() if err == cu.CUresult.CUDA_SUCCESS and name else ""
+            key = "ours" if name.startswith("_ZN2d3") else "nccl" if "nccl" in name.lower() else "other"
+            out[key] += 1
+        return out
+    except Exception:  # noqa: BLE001 - reported as unavailable
+        return None
+
+
+EP_STAGES = [  # (name, from mark, to mark): one EP step split at the marks TimedOps records
+    ("dense", "step", "layer"),            # QKV + o_proj FP8 GEMVs (activation split + tcgen05 GEMV each)
+    ("route", "layer", "pack"),            # router + top-8 (+ exact mode: row plan, count exchange, host read)
+    ("dispatch", "pack", "dispatched"),    # FP8 row pack + all_to_all
+    ("unpack", "dispatched", "experts"),
+    ("local_experts", "experts", "experts_done"),
+    ("return", "experts_done", "combine"),  # partial rows all_to_all back + shared-expert join
+    ("combine", "combine", "end"),
+]
+
+
+def _stage_summary(samples: list[dict], dev) -> dict:
+    """Mean per stage over samples on this rank, then the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    names = [n for n, _, _ in EP_STAGES if all(n in smp for smp in samples)]
+    v = torch.tensor([statistics.mean(smp[n] for smp in samples) for n in names], device=dev)
+    if dist.is_initialized():
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return {n: float(x) for n, x in zip(names, v.tolist())}
+
+
+def _read_marks(marks: dict) -> dict:
+    return {n: marks[a].elapsed_time(marks[b]) for n, a, b in EP_STAGES if a in marks and b in marks}
+
+
+def ep_stage_times(eops, run, x, dev, stream, reps: int = 20) -> dict:
+    """Per-stage times (ms, max over ranks) of run(x), captured once into a
+    CUDA graph with timing event nodes at the stage marks and replayed."""
+    import torch
+
+    names = {m for _, a, b in EP_STAGES for m in (a, b)}
+    marks = {m: torch.cuda.Event(enable_timing=True, external=True) for m in names}
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        run(x)
+        g = torch.cuda.CUDAGraph()
+        eops.marks = marks
+        try:
+            with torch.cuda.graph(g, stream=cap):
+                run(x)
+        finally:
+            eops.marks = None
+    stream.wait_stream(cap)
+    torch.cuda.synchronize(dev)
+    samples = []
+    for _ in range(reps):
+        g.replay()
+        torch.cuda.synchronize(dev)
+        samples.append(_read_marks(marks))
+    del g
+    return _stage_summary(samples, dev)
+
+
+def ep_config5(args, eops, routers, experts_all, shareds, world, rank, dev, stream) -> dict:
+    """Expert-parallel layer at the job-level batch sizes of the fifth
+    benchmark configuration: 512 decode tokens (capacity mode, CUDA graph)
+    and 8192 prefill tokens (exact mode, eager) split evenly over the ranks,
+    bf16 N(0,1) inputs from seed 4. Times are the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from d3moe.ep import ExpertParallelMoE
+
+    out = {}
+    nl = len(routers)
+    for kind, total, mode in (("decode", 512, "capacity"), ("prefill", 8192, "exact")):
+        T = total // world
+        layers = [ExpertParallelMoE(routers[i], experts_all[i], shareds[i], E, TOPK, ops=eops, mode=mode)
+                  for i in range(nl)]
+        g = torch.Generator(device=dev)
+        g.manual_seed(4 + 1000 * rank)
+        xs = torch.randn((nl, T, H), generator=g, device=dev).to(torch.bfloat16)
+        steps = args.steps if mode == "capacity" else max(5, min(args.steps, 20))
+        for i in range(3):
+            layers[i % nl].forward(xs[i % nl])
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        if mode == "capacity":
+            graphs, ys = [], []
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(stream)
+            with torch.cuda.stream(cap):
+                for i in range(nl):
+                    layers[i].forward(xs[i])
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=cap):
+                        ys.append(layers[i].forward(xs[i]))
+                    graphs.append(gr)
+            stream.wait_stream(cap)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            for i in range(3):
+                graphs[i % nl].replay()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            run = lambda i: graphs[i % nl].replay()  # noqa: E731
+        else:
+            run = lambda i: layers[i % nl].forward(xs[i % nl])  # noqa: E731
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            run(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        if mode == "capacity":
+            del graphs, ys
+            torch.cuda.synchronize(dev)
+            stages = ep_stage_times(eops, layers[0].forward, xs[0], dev, stream, reps=10)
+        else:
+            samples = []
+            names = {m for _, a, b in EP_STAGES for m in (a, b)}
+            for i in range(3):
+                eops.marks = {m: torch.cuda.Event(enable_timing=True) for m in names}
+                layers[0].forward(xs[0])
+                torch.cuda.synchronize(dev)
+                samples.append(_read_marks(eops.marks))
+                eops.marks = None
+            stages = _stage_summary(samples, dev)
+        dist.barrier()
+        out[kind] = {
+            "tokens_total": total, "tokens_per_gpu": T, "mode": mode, "steps": steps,
+            "ms_per_step": ms, "tokens_per_s": total / (ms * 1e-3),
+            "launch": "CUDA graph per weight set (kernels + NCCL)" if mode == "capacity" else
+                      "eager (one host read of the row counts per call)",
+            "stages_ms": stages,
+        }
+    return out
 
 
 def prefill_lengths() -> list[int]:
@@ -1340,9 +1551,9 @@ def main() -> None:
                   None if ids_buf is None else ids_buf.data_ptr(), wts.data_ptr(),
                   ws_moe.data_ptr(), ws_moe.numel(), status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
 
-    # (activation split + tcgen05 GEMV) x 2; router, route, permute, quant_scatter, gate_up, down,
-    # combine
-    launches_per_step = 2 * 2 + 7
+    # by hand, used when the captured step graph cannot be read: (activation split + tcgen05 GEMV)
+    # x 2; router, route, permute + quant, gate_up, down, combine
+    launches_per_step = 2 * 2 + 6
 
     # per-step stage events (gate_up / down engine launches) inside the timed region
     stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
@@ -1393,18 +1604,20 @@ def main() -> None:
     # captures its decode step, src/drama3/engine.py:84-92); the timed value
     # replays them. The eager loop above gives the per-kernel stage times.
     graphs, x_static = [], []
+    step_kernels = None
     if not args.eager:
         cap = torch.cuda.Stream(dev)
         cap.wait_stream(stream)
         with torch.cuda.stream(cap):
             for li in range(args.layers):
                 xb = xs[li % len(xs)].clone()
-                g = torch.cuda.CUDAGraph()
+                g = torch.cuda.CUDAGraph(keep_graph=(li == 0))
                 with torch.cuda.graph(g, stream=cap):
                     step(li, xb, None)
                 graphs.append(g)
                 x_static.append(xb)
         stream.wait_stream(cap)
+        step_kernels = graph_kernels(graphs[0])
         # the replay must reproduce the eager step bit for bit
         step(0, x_static[0], None)
         y_eager = y.clone()
@@ -1562,7 +1775,8 @@ def main() -> None:
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": (step_kernels["ours"] if step_kernels else launches_per_step) * args.steps,
+        "graph_kernels_per_step": step_kernels,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

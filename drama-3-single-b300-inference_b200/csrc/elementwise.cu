@@ -627,21 +627,6 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, int N, 
   if (tid == 0) scales[nb * KB + kb] = scale;
 }
 
-// dst[j] = src[token(j)] with token(j) = sorted_pairs[j] / k (zero row for a
-// pair id outside [0, T*k)); one warp per row, 16-byte copies.
-__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t src_stride,
-                                   int T, int H, int k, const int32_t* __restrict__ sorted_pairs,
-                                   int rows, __nv_bfloat16* __restrict__ dst) {
-  pdl_enter();
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int p = sorted_pairs[row];
-  const int t = (p >= 0 && p < T * k) ? p / k : -1;
-  uint4* d = reinterpret_cast<uint4*>(dst + static_cast<int64_t>(row) * H);
-  const uint4* sp = t >= 0 ? reinterpret_cast<const uint4*>(src + t * src_stride) : nullptr;
-  for (int c = threadIdx.x & 31; c < H / 8; c += 32) d[c] = sp ? __ldg(sp + c) : make_uint4(0, 0, 0, 0);
-}
-
 // Expert-parallel combine on the token's own rank:
 //   routed[t] = bf16( sum_r w[t,r] * rows[inv[t*k+r]] )   (fp32, r = 0..k-1)
 //   out[t]    = routed + bf16(shared[t] * bf16(sigmoid(gate[t])))
@@ -706,64 +691,85 @@ __global__ void ep_dispatch_meta_kernel(const int64_t* __restrict__ ids,
   meta_w[idx] = mine ? w[tj] : __float2bfloat16_rn(0.f);
 }
 
-// Packed capacity-mode dispatch: for destination rank d and token t, row
-// (d, t) of `send` holds x[t] (2H bytes), the k owner-local expert ids (int64,
-// -1 where expert e is owned by another rank) and the k bf16 weights (0 there),
-// padded to ep_row_bytes. One 16-byte chunk per thread.
-__global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
-                               const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
-                               int T, int k, int H, int experts_per_rank, int ranks, int row_bytes,
-                               uint8_t* __restrict__ send) {
+// FP8 packed EP dispatch: token t is quantised once (1x128 E4M3 groups, the
+// same bytes and scales the expert pipeline's own quantiser produces) and its
+// row for destination rank d holds [q e4m3 H bytes | group scales f32 H/128 |
+// k owner-local ids int64 (-1 where another rank owns the expert) | k bf16
+// weights (0 there) | zero padding to ep_row_bytes_fp8]. The row's index in
+// `send` is slot[t*ranks + d] (no row when -1), or d*T + t without a slot map
+// (fixed capacity: every token to every rank). One CTA per token.
+__global__ void __launch_bounds__(256)
+    ep_pack_fp8_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                       const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w, int T,
+                       int k, int H, int experts_per_rank, int ranks, int row_bytes,
+                       const int32_t* __restrict__ slot, uint8_t* __restrict__ send) {
   pdl_enter();
-  const int chunks = row_bytes / 16;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t n = static_cast<int64_t>(ranks) * T * chunks;
-  if (idx >= n) return;
-  const int c = static_cast<int>(idx % chunks);
-  const int64_t rt = idx / chunks;
-  const int t = static_cast<int>(rt % T), d = static_cast<int>(rt / T);
-  uint8_t* row = send + rt * row_bytes;
-  const int xchunks = H / 8;
-  if (c < xchunks) {
-    reinterpret_cast<uint4*>(row)[c] = __ldg(reinterpret_cast<const uint4*>(x + t * x_stride) + c);
-    return;
-  }
-  // metadata chunks: k int64 ids, then k bf16 weights, then zero padding
-  uint32_t out[4] = {0u, 0u, 0u, 0u};
-  const int base = 16 * c - 2 * H;  // byte offset inside the metadata
-  for (int b = 0; b < 16; b += 2) {
-    const int off = base + b;
-    uint16_t v = 0;
-    if (off < 8 * k) {
-      const int j = off / 8, part = (off % 8) / 2;
-      const int64_t e = ids[static_cast<int64_t>(t) * k + j];
-      const bool mine = e >= 0 && e / experts_per_rank == d && e < static_cast<int64_t>(experts_per_rank) * ranks;
-      const int64_t local = mine ? e - static_cast<int64_t>(d) * experts_per_rank : -1;
-      v = static_cast<uint16_t>(static_cast<uint64_t>(local) >> (16 * part));
-    } else if (off < 10 * k) {
-      const int j = (off - 8 * k) / 2;
-      const int64_t e = ids[static_cast<int64_t>(t) * k + j];
-      const bool mine = e >= 0 && e / experts_per_rank == d && e < static_cast<int64_t>(experts_per_rank) * ranks;
-      v = mine ? __bfloat16_as_ushort(w[static_cast<int64_t>(t) * k + j]) : 0;
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto row_of = [&](int d) -> uint8_t* {
+    const int64_t r = slot ? slot[static_cast<int64_t>(t) * ranks + d] : static_cast<int64_t>(d) * T + t;
+    return r < 0 ? nullptr : send + r * row_bytes;
+  };
+  const int G = H / 128;
+  const int half = lane >> 4, hl = lane & 15;
+  for (int gp = warp; gp < (G + 1) / 2; gp += 8) {
+    const int g = 2 * gp + half;
+    const bool valid = g < G;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + t * x_stride + g * 128 + hl * 8));
+    float f[8];
+    unpack_bf16x8(v, f);
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    amax = half_warp_max(amax);
+    const float scale = act_scale_from_amax(amax);
+    const uint2 qb = quant8(f, scale);
+    if (!valid) continue;
+    for (int d = 0; d < ranks; ++d) {
+      uint8_t* row = row_of(d);
+      if (!row) continue;
+      *reinterpret_cast<uint2*>(row + g * 128 + hl * 8) = qb;
+      if (hl == 0) reinterpret_cast<float*>(row + H)[g] = scale;
     }
-    out[b / 4] |= static_cast<uint32_t>(v) << (16 * ((b / 2) & 1));
   }
-  reinterpret_cast<uint4*>(row)[c] = make_uint4(out[0], out[1], out[2], out[3]);
+  const int meta = H + 4 * G;  // byte offset of the routing metadata
+  const int64_t owned = static_cast<int64_t>(experts_per_rank) * ranks;
+  for (int i = threadIdx.x; i < ranks * k; i += blockDim.x) {
+    const int d = i / k, j = i - d * k;
+    const int64_t e = ids[static_cast<int64_t>(t) * k + j];
+    const bool mine = e >= 0 && e < owned && e / experts_per_rank == d;
+    uint8_t* row = row_of(d);
+    if (!row) continue;
+    reinterpret_cast<int64_t*>(row + meta)[j] = mine ? e - static_cast<int64_t>(d) * experts_per_rank : -1;
+    reinterpret_cast<__nv_bfloat16*>(row + meta + 8 * k)[j] =
+        mine ? w[static_cast<int64_t>(t) * k + j] : __float2bfloat16_rn(0.f);
+  }
+  for (int i = meta + 10 * k + threadIdx.x; i < row_bytes; i += blockDim.x)
+    for (int d = 0; d < ranks; ++d)
+      if (uint8_t* row = row_of(d)) row[i] = 0;
 }
 
-// The metadata of received packed rows into contiguous ids [rows, k] int64
-// and weights [rows, k] bf16.
-__global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, int rows, int k, int H,
-                                      int row_bytes, int64_t* __restrict__ ids,
-                                      __nv_bfloat16* __restrict__ w) {
+// Received FP8 packed rows: group scales [rows, H/128], ids [rows, k] and
+// weights [rows, k] copied out contiguous; the e4m3 bytes are read in place
+// (row stride ep_row_bytes_fp8).
+__global__ void ep_unpack_fp8_kernel(const uint8_t* __restrict__ recv, int rows, int k, int H,
+                                     int row_bytes, float* __restrict__ scales,
+                                     int64_t* __restrict__ ids, __nv_bfloat16* __restrict__ w) {
   pdl_enter();
+  const int G = H / 128;
+  const int per_row = G + k;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<int64_t>(rows) * k) return;
-  const int64_t r = idx / k;
-  const int j = static_cast<int>(idx % k);
-  const uint8_t* meta = recv + r * row_bytes + 2 * H;
-  ids[idx] = reinterpret_cast<const int64_t*>(meta)[j];
-  w[idx] = reinterpret_cast<const __nv_bfloat16*>(meta + 8 * k)[j];
+  if (idx >= static_cast<int64_t>(rows) * per_row) return;
+  const int64_t r = idx / per_row;
+  const int c = static_cast<int>(idx - r * per_row);
+  const uint8_t* row = recv + r * row_bytes;
+  if (c < G) {
+    scales[r * G + c] = reinterpret_cast<const float*>(row + H)[c];
+  } else {
+    const int j = c - G;
+    ids[r * k + j] = reinterpret_cast<const int64_t*>(row + H + 4 * G)[j];
+    w[r * k + j] = reinterpret_cast<const __nv_bfloat16*>(row + H + 4 * G + 8 * k)[j];
+  }
 }
 
 inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps); }
@@ -916,19 +922,6 @@ extern "C" int d3_fp8_quantize_weight(const void* w, int N, int K, uint8_t* q, f
   return check_launch("fp8_quantize_weight");
 }
 
-extern "C" int d3_gather_rows(const void* src, int64_t src_stride, int T, int H, int k,
-                              const int32_t* sorted_pairs, int rows, void* dst,
-                              d3_stream_t stream) {
-  D3_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && k > 0 && rows >= 0, "gather_rows: bad shape");
-  D3_REQUIRE(src_stride >= H && src_stride % 8 == 0, "gather_rows: src row stride must be >= H and a multiple of 8");
-  D3_REQUIRE(aligned(src, 16) && aligned(dst, 16), "gather_rows: misaligned pointer");
-  if (rows == 0) return D3_OK;
-  launch_kernel(gather_rows_kernel, dim3(row_blocks(rows)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 
-      static_cast<const __nv_bfloat16*>(src), src_stride, T, H, k, sorted_pairs, rows,
-      static_cast<__nv_bfloat16*>(dst));
-  return check_launch("gather_rows");
-}
-
 extern "C" int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const void* weights,
                                 int T, int k, int H, const void* shared, const void* gate,
                                 int64_t gate_stride, void* out, d3_stream_t stream) {
@@ -943,41 +936,40 @@ extern "C" int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const
   return check_launch("combine_pairs");
 }
 
-extern "C" int d3_ep_row_bytes(int H, int k, int* bytes) {
-  D3_REQUIRE(bytes && H > 0 && H % 8 == 0 && k > 0, "ep_row_bytes: bad arguments");
-  *bytes = (2 * H + 10 * k + 15) / 16 * 16;
+extern "C" int d3_ep_row_bytes_fp8(int H, int k, int* bytes) {
+  D3_REQUIRE(bytes && H > 0 && H % 128 == 0 && k > 0, "ep_row_bytes_fp8: bad arguments");
+  *bytes = (H + 4 * (H / 128) + 10 * k + 15) / 16 * 16;
   return D3_OK;
 }
 
-extern "C" int d3_ep_pack(const void* x, int64_t x_stride, const int64_t* ids, const void* weights,
-                          int T, int k, int H, int experts_per_rank, int ranks, uint8_t* send,
-                          d3_stream_t stream) {
-  D3_REQUIRE(T >= 0 && k > 0 && H > 0 && H % 8 == 0 && experts_per_rank > 0 && ranks > 0,
-             "ep_pack: bad shape");
+extern "C" int d3_ep_pack_fp8(const void* x, int64_t x_stride, const int64_t* ids, const void* weights,
+                              int T, int k, int H, int experts_per_rank, int ranks, const int32_t* slot,
+                              uint8_t* send, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && H > 0 && H % 128 == 0 && experts_per_rank > 0 && ranks > 0,
+             "ep_pack_fp8: bad shape (H must be a multiple of 128)");
   D3_REQUIRE(x_stride >= H && x_stride % 8 == 0 && aligned(x, 16) && aligned(send, 16),
-             "ep_pack: x must be 16-byte aligned with a row stride >= H, multiple of 8");
-  D3_REQUIRE(ids && weights, "ep_pack: null ids or weights");
-  const int row_bytes = (2 * H + 10 * k + 15) / 16 * 16;
-  const int64_t n = static_cast<int64_t>(ranks) * T * (row_bytes / 16);
-  if (n == 0) return D3_OK;
-  launch_kernel(ep_pack_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                reinterpret_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x), x_stride,
-                ids, static_cast<const __nv_bfloat16*>(weights), T, k, H, experts_per_rank, ranks,
-                row_bytes, send);
-  return check_launch("ep_pack");
+             "ep_pack_fp8: x must be 16-byte aligned with a row stride >= H, multiple of 8");
+  D3_REQUIRE(ids && weights, "ep_pack_fp8: null ids or weights");
+  if (T == 0) return D3_OK;
+  const int row_bytes = (H + 4 * (H / 128) + 10 * k + 15) / 16 * 16;
+  launch_kernel(ep_pack_fp8_kernel, dim3(T), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                static_cast<const __nv_bfloat16*>(x), x_stride, ids,
+                static_cast<const __nv_bfloat16*>(weights), T, k, H, experts_per_rank, ranks, row_bytes,
+                slot, send);
+  return check_launch("ep_pack_fp8");
 }
 
-extern "C" int d3_ep_unpack_meta(const uint8_t* recv, int rows, int k, int H, int64_t* ids,
-                                 void* weights, d3_stream_t stream) {
-  D3_REQUIRE(rows >= 0 && k > 0 && H > 0 && H % 8 == 0 && recv && ids && weights,
-             "ep_unpack_meta: bad arguments");
-  const int row_bytes = (2 * H + 10 * k + 15) / 16 * 16;
-  const int64_t n = static_cast<int64_t>(rows) * k;
+extern "C" int d3_ep_unpack_fp8(const uint8_t* recv, int rows, int k, int H, float* scales,
+                                int64_t* ids, void* weights, d3_stream_t stream) {
+  D3_REQUIRE(rows >= 0 && k > 0 && H > 0 && H % 128 == 0 && recv && scales && ids && weights,
+             "ep_unpack_fp8: bad arguments");
+  const int row_bytes = (H + 4 * (H / 128) + 10 * k + 15) / 16 * 16;
+  const int64_t n = static_cast<int64_t>(rows) * (H / 128 + k);
   if (n == 0) return D3_OK;
-  launch_kernel(ep_unpack_meta_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                reinterpret_cast<cudaStream_t>(stream), recv, rows, k, H, row_bytes, ids,
+  launch_kernel(ep_unpack_fp8_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                reinterpret_cast<cudaStream_t>(stream), recv, rows, k, H, row_bytes, scales, ids,
                 static_cast<__nv_bfloat16*>(weights));
-  return check_launch("ep_unpack_meta");
+  return check_launch("ep_unpack_fp8");
 }
 
 extern "C" int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, int k,

@@ -597,44 +597,91 @@ __global__ void __launch_bounds__(kPermuteThreads)
   }
 }
 
-// Expert-parallel dispatch plan. Experts are owned contiguously by ranks
-// (rank = id / experts_per_rank). Pairs are bucketed by destination rank with
-// the same stable counting sort as permute (ascending pair order within a
-// rank), and each bucketed slot gets the expert's id local to its rank.
-__global__ void __launch_bounds__(kPermuteThreads)
-    ep_plan_kernel(const int64_t* __restrict__ ids, int P, int experts_per_rank, int ranks,
-                   int32_t* __restrict__ send_counts, int32_t* __restrict__ send_starts,
-                   int32_t* __restrict__ total, int32_t* __restrict__ sorted_pairs,
-                   int32_t* __restrict__ scratch_tiles, int32_t* __restrict__ inv_rows,
-                   int64_t* __restrict__ local_ids) {
+constexpr int kPlanRowsThreads = 1024;
+constexpr int kPlanRowsMaxRanks = 32;
+
+// Expert-parallel dispatch plan, one packed row per (token, owning rank):
+// rank d needs token t when it owns at least one of t's k experts (owner =
+// id / experts_per_rank). Rows are ordered by destination rank, then token;
+// slot[t*ranks + d] = the row's index in the send buffer (-1 when d needs no
+// row of t) and send_counts[d] = rows for d. One CTA: pass 1 counts, pass 2
+// writes the slots (a ballot + popcount scan per rank and 1024-token chunk).
+__global__ void __launch_bounds__(kPlanRowsThreads)
+    ep_plan_rows_kernel(const int64_t* __restrict__ ids, int T, int k, int experts_per_rank,
+                        int ranks, int32_t* __restrict__ send_counts, int32_t* __restrict__ slot) {
   pdl_enter();
-  extern __shared__ int sm[];
-  const int E = experts_per_rank * ranks;
-  auto id_at = [&](int p) -> int {
-    const int64_t v = ids[p];
-    return (v >= 0 && v < E) ? static_cast<int>(v / experts_per_rank) : -1;
+  __shared__ int warp_cnt[32][kPlanRowsMaxRanks];  // rows of this chunk per (warp, rank)
+  __shared__ int warp_off[32][kPlanRowsMaxRanks];  // exclusive prefix over warps
+  __shared__ int base[kPlanRowsMaxRanks];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t owned = static_cast<int64_t>(experts_per_rank) * ranks;
+  auto need_mask = [&](int t) -> uint32_t {
+    uint32_t m = 0;
+    if (t < T)
+      for (int j = 0; j < k; ++j) {
+        const int64_t e = ids[static_cast<int64_t>(t) * k + j];
+        if (e >= 0 && e < owned) m |= 1u << static_cast<int>(e / experts_per_rank);
+      }
+    return m;
   };
-  permute_body(id_at, P, ranks, 1, sm, send_counts, send_starts, total, sorted_pairs,
-               scratch_tiles, P, inv_rows, nullptr, nullptr);
+  if (tid < ranks) base[tid] = 0;
   __syncthreads();
-  for (int j = threadIdx.x; j < P; j += kPermuteThreads) {
-    const int p = sorted_pairs[j];
-    local_ids[j] = (p >= 0 && p < P) ? ids[p] % experts_per_rank : -1;
+  for (int c0 = 0; c0 < T; c0 += kPlanRowsThreads) {  // pass 1: rows per rank
+    const uint32_t m = need_mask(c0 + tid);
+    for (int d = 0; d < ranks; ++d) {
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+      if (lane == 0) warp_cnt[warp][d] = __popc(b);
+    }
+    __syncthreads();
+    if (tid < ranks) {
+      int s = 0;
+      for (int w = 0; w < kPlanRowsThreads / 32; ++w) s += warp_cnt[w][tid];
+      base[tid] += s;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    int run = 0;
+    for (int d = 0; d < ranks; ++d) {
+      const int n = base[d];
+      send_counts[d] = n;
+      base[d] = run;
+      run += n;
+    }
+  }
+  __syncthreads();
+  for (int c0 = 0; c0 < T; c0 += kPlanRowsThreads) {  // pass 2: slots
+    const int t = c0 + tid;
+    const uint32_t m = need_mask(t);
+    for (int d = 0; d < ranks; ++d) {
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+      if (lane == 0) warp_cnt[warp][d] = __popc(b);
+    }
+    __syncthreads();
+    if (warp < ranks) {  // warp d scans rank d's per-warp counts
+      const int v = warp_cnt[lane][warp];
+      int incl = v;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      warp_off[lane][warp] = incl - v;
+    }
+    __syncthreads();
+    const unsigned lt = (1u << lane) - 1u;
+    for (int d = 0; d < ranks; ++d) {
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+      if (t < T)
+        slot[static_cast<int64_t>(t) * ranks + d] =
+            ((m >> d) & 1u) ? base[d] + warp_off[warp][d] + __popc(b & lt) : -1;
+    }
+    __syncthreads();
+    if (tid < ranks) base[tid] += warp_off[31][tid] + warp_cnt[31][tid];
+    __syncthreads();
   }
 }
 
 }  // namespace
-
-int launch_ep_plan(const int64_t* ids, int P, int experts_per_rank, int ranks,
-                   int32_t* send_counts, int32_t* send_starts, int32_t* total,
-                   int32_t* sorted_pairs, int32_t* scratch_tiles, int32_t* inv_rows,
-                   int64_t* local_ids, cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(ranks) * 35 * sizeof(int);
-  launch_kernel(ep_plan_kernel, dim3(1), dim3(kPermuteThreads), smem, s, ids, P, experts_per_rank, ranks, send_counts,
-                                                  send_starts, total, sorted_pairs, scratch_tiles,
-                                                  inv_rows, local_ids);
-  return check_launch("ep_plan");
-}
 
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
@@ -831,17 +878,14 @@ extern "C" int d3_moe_permute_chunked(const int64_t* ids, int T, int k, int E, i
                         scratch);
 }
 
-extern "C" int d3_ep_plan(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,
-                          int32_t* send_counts, int32_t* send_starts, int32_t* sorted_pairs,
-                          int32_t* inv_rows, int64_t* local_ids, int32_t* scratch,
-                          d3_stream_t stream) {
-  D3_REQUIRE(T >= 0 && k > 0 && experts_per_rank > 0 && ranks > 0 && ranks <= 1024,
-             "ep_plan: bad arguments T=%d k=%d experts_per_rank=%d ranks=%d", T, k,
-             experts_per_rank, ranks);
-  D3_REQUIRE(static_cast<int64_t>(T) * k < (1 << 24), "ep_plan: too many pairs");
-  if (T == 0) return D3_OK;
-  const int P = T * k;
-  return launch_ep_plan(ids, P, experts_per_rank, ranks, send_counts, send_starts, scratch,
-                        sorted_pairs, scratch + 1, inv_rows, local_ids,
-                        reinterpret_cast<cudaStream_t>(stream));
+extern "C" int d3_ep_plan_rows(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,
+                               int32_t* send_counts, int32_t* slot, d3_stream_t stream) {
+  D3_REQUIRE(T >= 0 && k > 0 && experts_per_rank > 0 && ranks > 0 && ranks <= kPlanRowsMaxRanks,
+             "ep_plan_rows: bad arguments T=%d k=%d experts_per_rank=%d ranks=%d (ranks <= %d)", T, k,
+             experts_per_rank, ranks, kPlanRowsMaxRanks);
+  D3_REQUIRE(ids && send_counts && slot, "ep_plan_rows: null pointer");
+  D3_REQUIRE(static_cast<int64_t>(T) * ranks < (int64_t{1} << 31), "ep_plan_rows: too many rows");
+  launch_kernel(ep_plan_rows_kernel, dim3(1), dim3(kPlanRowsThreads), 0, reinterpret_cast<cudaStream_t>(stream),
+                ids, T, k, experts_per_rank, ranks, send_counts, slot);
+  return check_launch("ep_plan_rows");
 }

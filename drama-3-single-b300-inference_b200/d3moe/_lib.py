@@ -131,24 +131,20 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "d3_set_stage_events": (_i32, [ctypes.POINTER(_c_void_p), _i32]),
     "d3_set_prefill_min_tokens": (_i32, [_i32]),
-    "d3_ep_plan": (
-        _i32,
-        [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
-         _c_void_p, _c_void_p],
-    ),
+    "d3_ep_plan_rows": (_i32, [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "d3_route_topk_rows": (
         _i32,
         [_c_void_p, _i32, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p, _i32, _i64, _c_void_p,
          _c_void_p, _i32, _c_void_p],
     ),
-    "d3_ep_row_bytes": (_i32, [_i32, _i32, ctypes.POINTER(_i32)]),
-    "d3_ep_pack": (
+    "d3_ep_row_bytes_fp8": (_i32, [_i32, _i32, ctypes.POINTER(_i32)]),
+    "d3_ep_pack_fp8": (
         _i32,
-        [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p],
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p,
+         _c_void_p],
     ),
-    "d3_ep_unpack_meta": (_i32, [_c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
+    "d3_ep_unpack_fp8": (_i32, [_c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "d3_ep_dispatch_meta": (_i32, [_c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p]),
-    "d3_gather_rows": (_i32, [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p]),
     "d3_combine_pairs": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p],

@@ -8,35 +8,35 @@ are replicated. One layer call on rank r, for its own T tokens:
   1. logits = router(x) bf16 [T, E+1]; top-k routing on the first E columns
      (identical arithmetic on every rank, so routing matches the 1-GPU layer
      bit for bit);
-  2. ep_plan buckets the T*k (token, expert) pairs by owner rank, stable;
-  3. send counts are exchanged (all_to_all, one small host read), then the
-     bf16 token rows and the owner-local expert ids (all_to_all_v);
-  4. the owner runs its experts on the rows it received (top-1 per row, weight
-     1, so each row comes back as bf16(down(...)) of one (token, expert) pair);
-  5. the rows go back with the mirror all_to_all_v;
-  6. combine_pairs: bf16(sum_r w[t,r] * row) in rank order + gated shared
-     expert, on the token's own rank.
+  2. dispatch: each token is quantised once (1x128 E4M3 groups with fp32
+     scales, the bytes the expert pipeline would produce itself) and one
+     packed row per destination rank carries those bytes, the scales and the
+     token's routing restricted to that rank (owner-local ids or -1, the
+     routing weight or 0): 2192 bytes a row at H=2048, k=8
+     (d3_ep_pack_fp8); one all_to_all moves the rows;
+  3. the owner runs its experts straight on the received bytes
+     (d3_ep_unpack_fp8, d3_moe_experts_fp8) and produces one weighted partial
+     row per received row, bf16(sum over its experts of w * down);
+  4. the partials go back with the mirror all_to_all;
+  5. d3_combine_pairs on the token's own rank: bf16(sum of its partials in
+     rank order) + the gated shared expert, which ran on a side stream while
+     the exchange was in flight.
 
-That is mode="exact": it moves only the pairs, but needs a host read of the
-send counts per call. The default, mode="capacity", has no host
-synchronisation (so the layer can be captured into a CUDA graph with its NCCL
-calls): every token row goes once to every rank together with the routing
-restricted to that rank's experts (local ids or -1, the routing weight or 0),
-packed with the row into one buffer so the dispatch is a single all_to_all
-(d3_ep_pack / d3_ep_unpack_meta); the owner runs its experts on all received
-rows with those k ids and returns one weighted partial row per token,
-bf16(sum over its experts of w * down), and the token's rank adds the N
-partials in rank order plus the gated shared expert (d3_combine_pairs with
-weight 1 per rank). The shared expert runs on a side stream while the
-exchange is in flight. All ranks must call the layer with the same T. At
-decode sizes this moves T*N rows per rank per direction, the same order as the
-exact scheme.
+Two ways to choose the destination rows:
 
-The device steps are the C ABI entry points d3_ep_plan, d3_ep_pack,
-d3_ep_unpack_meta, d3_ep_dispatch_meta, d3_gather_rows, d3_moe_experts and
-d3_combine_pairs. `ops` is injectable so the
-exchange logic can be exercised with CPU ranks (gloo) in tests; the default
-runs on the GPU.
+  mode="capacity" (default, decode): every token goes to every rank (fixed
+  buffers, [N, T] rows), so there is no host synchronisation and the layer,
+  NCCL calls included, can be captured into a CUDA graph. All ranks must call
+  it with the same T.
+
+  mode="exact" (prefill): a token goes only to the ranks that own at least
+  one of its experts (d3_ep_plan_rows: rows ordered by destination rank, a
+  slot map per (token, rank)); the row counts are exchanged first and read on
+  the host (one synchronisation per call), then the rows move with
+  all_to_all_v. Ranks may hold different T.
+
+`ops` is injectable so the exchange logic can be exercised with CPU ranks
+(gloo) in tests; the default runs on the GPU.
 """
 
 from __future__ import annotations
@@ -48,10 +48,10 @@ from . import ops as _ops
 from ._lib import call
 
 
-def ep_row_bytes(H: int, k: int) -> int:
-    """Bytes per packed dispatch row: x (2H) + k int64 ids + k bf16 weights,
-    rounded up to 16 (d3_ep_row_bytes)."""
-    return (2 * H + 10 * k + 15) // 16 * 16
+def ep_row_bytes_fp8(H: int, k: int) -> int:
+    """Bytes per FP8 packed dispatch row: e4m3 x (H) + H/128 f32 group scales
+    + k int64 ids + k bf16 weights, rounded up to 16 (d3_ep_row_bytes_fp8)."""
+    return (H + 4 * (H // 128) + 10 * k + 15) // 16 * 16
 
 
 class CudaEPOps:
@@ -63,49 +63,45 @@ class CudaEPOps:
     def route(self, logits, k, bias=None):
         return _ops.route_topk(logits, k, bias=bias, weights_dtype=torch.bfloat16)
 
-    def plan(self, ids, experts_per_rank, ranks):
+    def plan_rows(self, ids, experts_per_rank, ranks):
+        """(send_counts int32 [ranks], slot int32 [T, ranks]) of d3_ep_plan_rows."""
         T, k = ids.shape
-        P = T * k
         dev = ids.device
-        i32 = dict(dtype=torch.int32, device=dev)
-        send_counts = torch.empty(ranks, **i32)
-        send_starts = torch.empty(ranks, **i32)
-        sorted_pairs = torch.empty(max(P, 1), **i32)
-        inv = torch.empty(max(P, 1), **i32)
-        local_ids = torch.empty(max(P, 1), dtype=torch.int64, device=dev)
-        scratch = torch.empty(P + 1, **i32)
-        call("d3_ep_plan", ids.data_ptr(), T, k, experts_per_rank, ranks, send_counts.data_ptr(),
-             send_starts.data_ptr(), sorted_pairs.data_ptr(), inv.data_ptr(), local_ids.data_ptr(),
-             scratch.data_ptr(), _ops._stream(dev))
-        return send_counts, sorted_pairs[:P], inv[:P], local_ids[:P]
+        send_counts = torch.empty(ranks, dtype=torch.int32, device=dev)
+        slot = torch.empty((T, ranks), dtype=torch.int32, device=dev)
+        call("d3_ep_plan_rows", ids.data_ptr(), T, k, experts_per_rank, ranks, send_counts.data_ptr(),
+             slot.data_ptr(), _ops._stream(dev))
+        return send_counts, slot
 
-    def pack(self, x, ids, weights, experts_per_rank, ranks):
-        """Packed capacity-mode send buffer uint8 [ranks, T * row_bytes]."""
+    def pack_fp8(self, x, ids, weights, experts_per_rank, ranks, slot=None, rows=None):
+        """FP8 packed send rows, uint8 [ranks, T * row_bytes] (every token to
+        every rank), or [rows, row_bytes] placed by a plan_rows slot map."""
         T, H = x.shape
         k = ids.shape[1]
-        rb = ep_row_bytes(H, k)
-        send = torch.empty((ranks, T * rb), dtype=torch.uint8, device=x.device)
-        call("d3_ep_pack", x.data_ptr(), _ops._row_stride(x), ids.data_ptr(),
-             weights.contiguous().data_ptr(), T, k, H, experts_per_rank, ranks, send.data_ptr(),
-             _ops._stream(x.device))
+        rb = ep_row_bytes_fp8(H, k)
+        shape = (ranks, T * rb) if slot is None else (rows, rb)
+        send = torch.empty(shape, dtype=torch.uint8, device=x.device)
+        call("d3_ep_pack_fp8", x.data_ptr(), _ops._row_stride(x), ids.data_ptr(),
+             weights.contiguous().data_ptr(), T, k, H, experts_per_rank, ranks,
+             None if slot is None else slot.data_ptr(), send.data_ptr(), _ops._stream(x.device))
         return send
 
-    def unpack(self, recv, rows, k, H):
-        """Received packed rows -> (x rows bf16 [rows, H] strided view, ids, weights)."""
-        rb = ep_row_bytes(H, k)
+    def unpack_fp8(self, recv, rows, k, H):
+        """Received FP8 rows -> (q e4m3 [rows, H] strided view, scales f32
+        [rows, H/128], ids int64 [rows, k], weights bf16 [rows, k])."""
+        rb = ep_row_bytes_fp8(H, k)
+        scales = torch.empty((rows, H // 128), dtype=torch.float32, device=recv.device)
         ids = torch.empty((rows, k), dtype=torch.int64, device=recv.device)
         w = torch.empty((rows, k), dtype=torch.bfloat16, device=recv.device)
-        call("d3_ep_unpack_meta", recv.data_ptr(), rows, k, H, ids.data_ptr(), w.data_ptr(),
-             _ops._stream(recv.device))
-        return recv.view(rows, rb).view(torch.bfloat16)[:, :H], ids, w
+        call("d3_ep_unpack_fp8", recv.data_ptr(), rows, k, H, scales.data_ptr(), ids.data_ptr(),
+             w.data_ptr(), _ops._stream(recv.device))
+        q = recv.view(rows, rb)[:, :H].view(torch.float8_e4m3fn)
+        return q, scales, ids, w
 
-    def gather_rows(self, x, sorted_pairs, k):
-        T, H = x.shape
-        rows = sorted_pairs.numel()
-        out = torch.empty((rows, H), dtype=x.dtype, device=x.device)
-        call("d3_gather_rows", x.data_ptr(), x.stride(0), T, H, k, sorted_pairs.data_ptr(), rows,
-             out.data_ptr(), _ops._stream(x.device))
-        return out
+    def local_experts_fp8(self, q, scales, ids, weights, experts):
+        """Weighted sum over each received row's local experts (ids -1
+        skipped), on the received E4M3 bytes."""
+        return _ops.moe_experts_fp8(q, scales, ids, weights, experts, transposed=False)
 
     def dispatch_meta(self, ids, weights, experts_per_rank, ranks):
         T, k = ids.shape
@@ -114,17 +110,6 @@ class CudaEPOps:
         call("d3_ep_dispatch_meta", ids.data_ptr(), weights.contiguous().data_ptr(), T, k, experts_per_rank,
              ranks, meta_ids.data_ptr(), meta_w.data_ptr(), _ops._stream(ids.device))
         return meta_ids, meta_w
-
-    def local_experts_k(self, rows, ids, weights, experts):
-        """Weighted sum over each row's (up to k) local experts; ids -1 skipped."""
-        out, _ = _ops.moe_experts(rows, ids, weights, experts)
-        return out
-
-    def local_experts(self, rows, local_ids, experts):
-        M = rows.shape[0]
-        ones = torch.ones((M, 1), dtype=torch.bfloat16, device=rows.device)
-        out, _ = _ops.moe_experts(rows, local_ids.view(M, 1), ones, experts)
-        return out
 
     def shared_expert(self, x, shared):
         T = x.shape[0]
@@ -227,24 +212,11 @@ class ExpertParallelMoE:
         logits = ops.router_logits(x, self.router)
         weights, ids = ops.route(logits[:, : self.E], self.k, bias=self.router_bias)
         shared, side = self._shared_begin(x)
-        if hasattr(ops, "pack"):
-            # one exchange of packed rows (token row + per-rank routing)
-            send = ops.pack(x, ids, weights, self.E_local, N)
-            recv = torch.empty_like(send)
-            dist.all_to_all_single(recv, send, group=self.group)
-            rows, ids_recv, w_recv = ops.unpack(recv, N * T, self.k, H)
-        else:
-            meta_ids, meta_w = ops.dispatch_meta(ids, weights, self.E_local, N)
-            x_send = x.unsqueeze(0).expand(N, T, H).contiguous()
-            x_recv = torch.empty_like(x_send)
-            ids_recv = torch.empty_like(meta_ids)
-            w_recv = torch.empty_like(meta_w)
-            dist.all_to_all_single(x_recv, x_send, group=self.group)
-            dist.all_to_all_single(ids_recv, meta_ids, group=self.group)
-            dist.all_to_all_single(w_recv, meta_w, group=self.group)
-            rows = x_recv.view(N * T, H)
-        partial = ops.local_experts_k(rows, ids_recv.view(N * T, self.k), w_recv.view(N * T, self.k),
-                                      self.experts)
+        send = ops.pack_fp8(x, ids, weights, self.E_local, N)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        q, qs, ids_recv, w_recv = ops.unpack_fp8(recv, N * T, self.k, H)
+        partial = ops.local_experts_fp8(q, qs, ids_recv, w_recv, self.experts)
         partial_back = torch.empty_like(partial)
         dist.all_to_all_single(partial_back, partial, group=self.group)
         shared = self._shared_end(shared, side)
@@ -256,27 +228,31 @@ class ExpertParallelMoE:
 
     def _forward_exact(self, x, return_routing: bool):
         ops = self.ops
+        N = self.world
         T, H = x.shape
         logits = ops.router_logits(x, self.router)
         weights, ids = ops.route(logits[:, : self.E], self.k, bias=self.router_bias)
-        send_counts_dev, sorted_pairs, inv, local_ids = ops.plan(ids, self.E_local, self.world)
-        # counts: device -> all_to_all -> host (the one host synchronisation)
+        send_counts_dev, slot = ops.plan_rows(ids, self.E_local, N)
+        shared, side = self._shared_begin(x)
+        # row counts: device -> all_to_all -> host (the one host synchronisation)
         counts64 = send_counts_dev.to(torch.int64)
         recv_counts_dev = torch.empty_like(counts64)
         dist.all_to_all_single(recv_counts_dev, counts64, group=self.group)
         both = torch.stack([counts64, recv_counts_dev]).cpu()
         send_counts = [int(v) for v in both[0]]
         recv_counts = [int(v) for v in both[1]]
-        rows_send = ops.gather_rows(x, sorted_pairs, self.k)
-        rows_recv = self._exchange(rows_send, send_counts, recv_counts)
-        ids_recv = self._exchange(local_ids, send_counts, recv_counts)
-        if rows_recv.shape[0]:
-            y_recv = ops.local_experts(rows_recv, ids_recv, self.experts)
+        send = ops.pack_fp8(x, ids, weights, self.E_local, N, slot=slot, rows=sum(send_counts))
+        recv = self._exchange(send, send_counts, recv_counts)
+        R = recv.shape[0]
+        if R:
+            q, qs, ids_recv, w_recv = ops.unpack_fp8(recv, R, self.k, H)
+            partial = ops.local_experts_fp8(q, qs, ids_recv, w_recv, self.experts)
         else:
-            y_recv = rows_recv
-        rows_back = self._exchange(y_recv, recv_counts, send_counts)
-        shared = ops.shared_expert(x, self.shared)
-        out = ops.combine(rows_back, inv, weights, shared, logits[:, self.E: self.E + 1])
+            partial = torch.empty((0, H), dtype=torch.bfloat16, device=x.device)
+        rows_back = self._exchange(partial, recv_counts, send_counts)
+        shared = self._shared_end(shared, side)
+        ones = self._combine_inputs(T, x.device)[1]
+        out = ops.combine(rows_back, slot.reshape(-1), ones, shared, logits[:, self.E: self.E + 1])
         if return_routing:
             return out, ids, weights
         return out

@@ -382,15 +382,16 @@ D3_API int d3_moe_layer_rows(const void* x, int64_t x_stride, const void* router
  * and combine over NCCL all-to-all). Experts are owned contiguously: rank
  * r holds experts [r*experts_per_rank, (r+1)*experts_per_rank).
  *
- * d3_ep_plan: pairs p = t*k + r bucketed by destination rank (stable, like
- * d3_moe_permute). send_counts/send_starts int32 [ranks]; sorted_pairs,
- * inv_rows int32 [T*k]; local_ids int64 [T*k] in bucketed order = the expert
- * id on its owner rank (-1 for an id outside [0, experts_per_rank*ranks));
- * scratch int32 [T*k + 1]. */
-D3_API int d3_ep_plan(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,
-                      int32_t* send_counts, int32_t* send_starts, int32_t* sorted_pairs,
-                      int32_t* inv_rows, int64_t* local_ids, int32_t* scratch,
-                      d3_stream_t stream);
+ * d3_ep_plan_rows: one dispatch row per (token, owning rank). Rank d needs
+ * token t when it owns at least one of t's k experts (ids outside
+ * [0, experts_per_rank*ranks) are ignored). Rows are ordered by destination
+ * rank, then token: send_counts int32 [ranks] = rows for each rank, and
+ * slot int32 [T, ranks] = the row's index in the send buffer, -1 where d needs
+ * no row of t. The same slot map, flattened, is the inv_rows argument of
+ * d3_combine_pairs (k = ranks, weight 1) once the partial rows are back in
+ * the send order. ranks <= 32. */
+D3_API int d3_ep_plan_rows(const int64_t* ids, int T, int k, int experts_per_rank, int ranks,
+                           int32_t* send_counts, int32_t* slot, d3_stream_t stream);
 
 /* Fixed-capacity dispatch (no host-visible counts): for each rank d and token
  * t, meta_ids int64 [ranks, T, k] = ids[t][j] - d*experts_per_rank where rank d
@@ -400,25 +401,29 @@ D3_API int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, i
                                int experts_per_rank, int ranks, int64_t* meta_ids, void* meta_w,
                                d3_stream_t stream);
 
-/* Packed fixed-capacity dispatch: one buffer, one all_to_all. send holds
- * [ranks][T] rows of d3_ep_row_bytes(H, k) bytes: x[t] (bf16, 2H bytes), the
- * k owner-local ids of d3_ep_dispatch_meta (int64) and its k weights (bf16),
- * zero padded. A received row's x part is a bf16 row with stride
- * row_bytes / 2 elements; d3_ep_unpack_meta copies the ids [rows, k] and
- * weights [rows, k] out of `rows` received rows. */
-D3_API int d3_ep_row_bytes(int H, int k, int* bytes);
-D3_API int d3_ep_pack(const void* x, int64_t x_stride, const int64_t* ids, const void* weights, int T,
-                      int k, int H, int experts_per_rank, int ranks, uint8_t* send, d3_stream_t stream);
-D3_API int d3_ep_unpack_meta(const uint8_t* recv, int rows, int k, int H, int64_t* ids, void* weights,
-                             d3_stream_t stream);
-
-/* dst bf16 [rows, H] = src rows of token sorted_pairs[j] / k. */
-D3_API int d3_gather_rows(const void* src, int64_t src_stride, int T, int H, int k,
-                          const int32_t* sorted_pairs, int rows, void* dst, d3_stream_t stream);
+/* Packed FP8 dispatch (one buffer, one all_to_all): each token is quantised
+ * once (1x128 E4M3 groups, the bytes and scales the expert pipeline's own
+ * quantiser produces) and each of its rows holds q e4m3 (H bytes), the H/128
+ * group scales (f32), the k owner-local ids of d3_ep_dispatch_meta (int64, -1
+ * elsewhere) and its k bf16 weights, zero padded to d3_ep_row_bytes_fp8(H, k)
+ * bytes (a multiple of 16). With slot == NULL, send is [ranks][T] rows (fixed
+ * capacity: every token to every rank); with the slot map of d3_ep_plan_rows,
+ * token t's row for rank d is row slot[t*ranks + d] and no row is written
+ * where that is -1. d3_ep_unpack_fp8 copies the scales [rows, H/128], ids
+ * [rows, k] and weights [rows, k] of `rows` received rows out; the e4m3 bytes
+ * are read in place (row stride row_bytes), e.g. by d3_moe_experts_fp8 with
+ * scales_transposed = 0. H a multiple of 128. */
+D3_API int d3_ep_row_bytes_fp8(int H, int k, int* bytes);
+D3_API int d3_ep_pack_fp8(const void* x, int64_t x_stride, const int64_t* ids, const void* weights,
+                          int T, int k, int H, int experts_per_rank, int ranks, const int32_t* slot,
+                          uint8_t* send, d3_stream_t stream);
+D3_API int d3_ep_unpack_fp8(const uint8_t* recv, int rows, int k, int H, float* scales,
+                            int64_t* ids, void* weights, d3_stream_t stream);
 
 /* out bf16 [T,H] = bf16(sum_r w[t,r] * rows[inv[t*k+r]]) + bf16(shared * bf16(sigmoid(gate)))
- * with rows bf16 [T*k, H] (expert outputs returned to the token's rank),
- * the sum in fp32 in rank order; shared and gate may be NULL. */
+ * with rows bf16 [*, H] (expert outputs returned to the token's rank), the
+ * sum in fp32 in r order; an inv entry < 0 is skipped; shared and gate may
+ * be NULL. */
 D3_API int d3_combine_pairs(const void* rows, const int32_t* inv_rows, const void* weights,
                             int T, int k, int H, const void* shared, const void* gate,
                             int64_t gate_stride, void* out, d3_stream_t stream);

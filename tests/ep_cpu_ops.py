@@ -1,7 +1,8 @@
 """CPU stand-in for the device steps of d3moe.ep (test infrastructure only).
 
-It lets the expert-parallel exchange (plan, all_to_all_v dispatch, expert
-compute on the owner, return, combine) run on gloo CPU ranks. The arithmetic
+It lets the expert-parallel exchange (row plan, FP8 row packing, all_to_all
+dispatch, expert compute on the owner, return, combine) run on gloo CPU
+ranks. The arithmetic
 is the oracle's, so an EP run can be compared with the single-process oracle
 layer.
 """
@@ -38,16 +39,24 @@ class CpuEPOps:
         w, ids = O.route(_np(logits), k, None if bias is None else bias.numpy())
         return _bf16(O.bf16_round(w)), torch.from_numpy(ids)
 
-    def plan(self, ids, experts_per_rank, ranks):
-        flat = ids.reshape(-1).numpy()
-        dest = flat // experts_per_rank
-        order = np.argsort(dest, kind="stable").astype(np.int32)
-        counts = np.bincount(dest, minlength=ranks).astype(np.int32)
-        inv = np.empty_like(order)
-        inv[order] = np.arange(order.size, dtype=np.int32)
-        local = (flat[order] % experts_per_rank).astype(np.int64)
-        return (torch.from_numpy(counts), torch.from_numpy(order), torch.from_numpy(inv),
-                torch.from_numpy(local))
+    def plan_rows(self, ids, experts_per_rank, ranks):
+        """d3_ep_plan_rows: one row per (token, rank owning >= 1 of its
+        experts), ordered by rank then token."""
+        idn = ids.numpy()
+        T = idn.shape[0]
+        owned = experts_per_rank * ranks
+        need = np.zeros((T, ranks), bool)
+        for t in range(T):
+            for e in idn[t]:
+                if 0 <= e < owned:
+                    need[t, e // experts_per_rank] = True
+        counts = need.sum(axis=0).astype(np.int32)
+        starts = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int32)
+        slot = np.full((T, ranks), -1, np.int32)
+        for d in range(ranks):
+            rows = np.nonzero(need[:, d])[0]
+            slot[rows, d] = starts[d] + np.arange(rows.size, dtype=np.int32)
+        return torch.from_numpy(counts), torch.from_numpy(slot)
 
     def dispatch_meta(self, ids, weights, experts_per_rank, ranks):
         T, k = ids.shape
@@ -61,59 +70,65 @@ class CpuEPOps:
             meta_w[d][torch.from_numpy(mine)] = wn[torch.from_numpy(mine)]
         return torch.from_numpy(meta_ids), meta_w
 
-    def pack(self, x, ids, weights, experts_per_rank, ranks):
-        """The packed dispatch rows of d3_ep_pack, built from dispatch_meta."""
-        from d3moe.ep import ep_row_bytes
+    def pack_fp8(self, x, ids, weights, experts_per_rank, ranks, slot=None, rows=None):
+        """The FP8 packed dispatch rows of d3_ep_pack_fp8: the oracle's 1x128
+        quantiser bytes, group scales, then dispatch_meta's ids and weights,
+        at row d*T + t, or at slot[t, d] with a plan_rows slot map."""
+        from d3moe.ep import ep_row_bytes_fp8
         T, H = x.shape
         k = ids.shape[1]
-        rb = ep_row_bytes(H, k)
+        rb = ep_row_bytes_fp8(H, k)
+        G = H // 128
+        q, sx = O.quant_act_fp8(_np(x))
+        qb = torch.from_numpy(np.ascontiguousarray(q, np.uint8))
+        sb = torch.from_numpy(np.ascontiguousarray(sx, np.float32)).view(torch.uint8)
         meta_ids, meta_w = self.dispatch_meta(ids, weights, experts_per_rank, ranks)
-        send = torch.zeros((ranks, T, rb), dtype=torch.uint8)
-        xb = x.contiguous().view(torch.uint8).reshape(T, 2 * H)
+        n = ranks * T if slot is None else rows
+        send = torch.zeros((n, rb), dtype=torch.uint8)
+        off = H + 4 * G
         for d in range(ranks):
-            send[d, :, : 2 * H] = xb
-            send[d, :, 2 * H: 2 * H + 8 * k] = meta_ids[d].contiguous().view(torch.uint8).reshape(T, 8 * k)
-            send[d, :, 2 * H + 8 * k: 2 * H + 10 * k] = meta_w[d].contiguous().view(torch.uint8).reshape(T, 2 * k)
-        return send.reshape(ranks, T * rb)
+            for t in range(T):
+                r = d * T + t if slot is None else int(slot[t, d])
+                if r < 0:
+                    continue
+                send[r, :H] = qb[t]
+                send[r, H: off] = sb[t]
+                send[r, off: off + 8 * k] = meta_ids[d, t].contiguous().view(torch.uint8)
+                send[r, off + 8 * k: off + 10 * k] = meta_w[d, t].contiguous().view(torch.uint8)
+        return send.reshape(ranks, T * rb) if slot is None else send
 
-    def unpack(self, recv, rows, k, H):
-        from d3moe.ep import ep_row_bytes
-        rb = ep_row_bytes(H, k)
+    def unpack_fp8(self, recv, rows, k, H):
+        from d3moe.ep import ep_row_bytes_fp8
+        rb = ep_row_bytes_fp8(H, k)
+        G = H // 128
         r = recv.reshape(rows, rb)
-        x = r[:, : 2 * H].contiguous().view(torch.bfloat16)
-        ids = r[:, 2 * H: 2 * H + 8 * k].contiguous().view(torch.int64)
-        w = r[:, 2 * H + 8 * k: 2 * H + 10 * k].contiguous().view(torch.bfloat16)
-        return x, ids, w
+        q = r[:, :H].contiguous()
+        scales = r[:, H: H + 4 * G].contiguous().view(torch.float32)
+        off = H + 4 * G
+        ids = r[:, off: off + 8 * k].contiguous().view(torch.int64)
+        w = r[:, off + 8 * k: off + 10 * k].contiguous().view(torch.bfloat16)
+        return q, scales, ids, w
 
-    def local_experts_k(self, rows, ids, weights, experts):
-        """Oracle expert sum over each row's valid ids (-1 = not routed here)."""
-        r = _np(rows)
+    def local_experts_fp8(self, q, scales, ids, weights, experts):
+        """Oracle expert sum over each row's valid ids, on the received bytes."""
+        qn = q.numpy()
+        sx = scales.numpy()
         idn = ids.numpy()
         w = _np(weights)
         M, k = idn.shape
         ex = experts.ex
-        q, sx = O.quant_act_fp8(r)
-        acc = np.zeros_like(r)
+        acc = np.zeros((M, qn.shape[1]), np.float32)
         for j in range(k):
             valid = idn[:, j] >= 0
             if not valid.any():
                 continue
             sel = np.nonzero(valid)[0]
             e_ids = idn[sel, j].reshape(-1, 1)
-            gu = O.expert_gate_up(q[sel], sx[sel], ex.w13, ex.s13, e_ids)
+            gu = O.expert_gate_up(qn[sel], sx[sel], ex.w13, ex.s13, e_ids)
             a, sa = O.silu_mul_quant(gu)
             d = O.expert_down_rows(a, sa, ex.w2, ex.s2, e_ids)
             acc[sel] = (acc[sel] + d * w[sel, j: j + 1]).astype(np.float32)
         return _bf16(O.bf16_round(acc))
-
-    def gather_rows(self, x, sorted_pairs, k):
-        return x[sorted_pairs.long() // k].clone()
-
-    def local_experts(self, rows, local_ids, experts):
-        M = rows.shape[0]
-        out, _ = O.moe_experts(_np(rows), local_ids.numpy().reshape(M, 1), np.ones((M, 1), np.float32),
-                               experts.ex)
-        return _bf16(out)
 
     def shared_expert(self, x, shared):
         T = x.shape[0]
@@ -125,8 +140,10 @@ class CpuEPOps:
         r = _np(rows)
         w = _np(weights)
         acc = np.zeros((T, r.shape[1]), np.float32)
-        invn = inv.numpy()
+        invn = inv.numpy().reshape(T, k)
         for j in range(k):
-            acc = (acc + r[invn[np.arange(T) * k + j]] * w[:, j: j + 1]).astype(np.float32)
+            idx = invn[:, j]
+            term = np.where((idx >= 0)[:, None], r[np.maximum(idx, 0)] * w[:, j: j + 1], 0.0)
+            acc = np.where((idx >= 0)[:, None], acc + term, acc).astype(np.float32)
         routed = O.bf16_round(acc)
         return _bf16(O.combine_experts(routed, _np(shared), _np(gate).reshape(-1)))

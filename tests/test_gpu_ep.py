@@ -85,24 +85,112 @@ def test_ep_multi_rank_matches_fused_layer(tmp_path, world, mode):
     _check(tmp_path, world)
 
 
-def test_ep_pack_unpack_matches_dispatch_meta():
-    """The packed dispatch rows carry exactly dispatch_meta's per-rank routing
-    and the token rows (d3_ep_pack / d3_ep_unpack_meta round trip)."""
+@pytest.mark.parametrize("mode,total", [("capacity", 512), ("exact", 8192)])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_config5_batches_match_fused_layer(tmp_path, world, mode, total):
+    """The fifth benchmark configuration's job-level batches, split evenly
+    over the ranks: 512 decode tokens through the capacity mode and 8192
+    prefill tokens through the exact mode (the owners' expert calls take the
+    tcgen05 prefill path there)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), total // world, mode), nprocs=world,
+             join=True)
+    _check(tmp_path, world)
+
+
+def test_ep_pack_fp8_matches_quantiser_and_dispatch_meta():
+    """The FP8 dispatch rows carry the pipeline quantiser's bytes and group
+    scales for each token and dispatch_meta's per-rank routing
+    (d3_ep_pack_fp8 / d3_ep_unpack_fp8 round trip)."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    from d3moe.ep import CudaEPOps
+    from d3moe import ops as d3ops
+    from d3moe.ep import CudaEPOps, ep_row_bytes_fp8
     ops = CudaEPOps()
     T, H, k, N, epr = 37, 2048, 8, 4, 32
     g = torch.Generator(device="cuda")
-    g.manual_seed(5)
+    g.manual_seed(6)
     x = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    x[5, :128] = 0  # an all-zero group
     ids = torch.randint(0, N * epr, (T, k), generator=g, device="cuda")
-    ids[3, 2] = -1  # an empty slot
+    ids[3, 2] = -1
     w = torch.rand((T, k), generator=g, device="cuda").to(torch.bfloat16)
-    send = ops.pack(x, ids, w, epr, N)
-    rows, ids_u, w_u = ops.unpack(send, N * T, k, H)
+    send = ops.pack_fp8(x, ids, w, epr, N)
+    assert send.shape == (N, T * ep_row_bytes_fp8(H, k))
+    q, sc, ids_u, w_u = ops.unpack_fp8(send, N * T, k, H)
+    q_ref, sc_ref = d3ops.quant_act_fp8(x)
     meta_ids, meta_w = ops.dispatch_meta(ids, w, epr, N)
     torch.cuda.synchronize()
+    qb = q.view(torch.uint8).reshape(N, T, H)
+    for d in range(N):
+        assert torch.equal(qb[d], q_ref.view(torch.uint8))
+        assert torch.equal(sc.view(N, T, -1)[d], sc_ref)
     assert torch.equal(ids_u, meta_ids.view(N * T, k))
     assert torch.equal(w_u, meta_w.view(N * T, k))
-    assert torch.equal(rows, x.unsqueeze(0).expand(N, T, H).reshape(N * T, H))
+
+
+def test_ep_local_experts_fp8_matches_bf16_rows():
+    """Experts on received FP8 rows equal the bf16 expert call on the tokens
+    they were quantised from, with dispatch_meta's routing (the expert
+    pipeline quantises with the same function)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from d3moe import ops as d3ops
+    from d3moe import synth
+    from d3moe.ep import CudaEPOps, shard_experts
+    ops = CudaEPOps()
+    T, N = 48, 2
+    lw = synth.make_layer(E, I, H, seed=9, device="cuda")
+    local = shard_experts(lw.experts, 1, N)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(8)
+    x = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    ids = torch.randint(0, E, (T, K), generator=g, device="cuda")
+    w = torch.rand((T, K), generator=g, device="cuda").to(torch.bfloat16)
+    epr = E // N
+    q, sc, ids_u, w_u = ops.unpack_fp8(ops.pack_fp8(x, ids, w, epr, N), N * T, K, H)
+    got = ops.local_experts_fp8(q[T:], sc[T:], ids_u[T:], w_u[T:], local)
+    meta_ids, meta_w = ops.dispatch_meta(ids, w, epr, N)
+    ref, _ = d3ops.moe_experts(x, meta_ids[1].contiguous(), meta_w[1].contiguous(), local)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got.float(), ref.float(), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("T,N", [(1, 2), (37, 4), (1500, 8), (4096, 2), (3000, 32)])
+def test_ep_plan_rows_matches_host_plan(T, N):
+    """d3_ep_plan_rows: row counts and the (token, rank) slot map equal the
+    host restatement (rows ordered by rank, then token), including ids
+    outside [0, E) and tokens that need no rank; the slotted FP8 pack puts
+    each token's row where the map says."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    sys.path.insert(0, str(ROOT / "tests"))
+    from ep_cpu_ops import CpuEPOps
+    from d3moe.ep import CudaEPOps, ep_row_bytes_fp8
+    ops = CudaEPOps()
+    epr = max(1, E // N)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(T + N)
+    ids = torch.randint(0, epr * N, (T, K), generator=g, device="cuda")
+    ids[T // 2, :] = -1             # a token routed nowhere
+    ids[0, 0] = epr * N + 3         # outside the owned range
+    counts, slot = ops.plan_rows(ids, epr, N)
+    c_ref, s_ref = CpuEPOps().plan_rows(ids.cpu(), epr, N)
+    torch.cuda.synchronize()
+    assert torch.equal(counts.cpu(), c_ref)
+    assert torch.equal(slot.cpu(), s_ref)
+    if T > 64:
+        return
+    x = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    w = torch.rand((T, K), generator=g, device="cuda").to(torch.bfloat16)
+    rows = int(c_ref.sum())
+    send = ops.pack_fp8(x, ids, w, epr, N, slot=slot, rows=rows)
+    full = ops.pack_fp8(x, ids, w, epr, N).view(N, T, ep_row_bytes_fp8(H, K))
+    torch.cuda.synchronize()
+    for t in range(T):
+        for d in range(N):
+            r = int(s_ref[t, d])
+            if r >= 0:
+                assert torch.equal(send[r], full[d, t]), (t, d)
