@@ -284,10 +284,12 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
         records the library's stage events around the routed-expert call."""
 
         marks = None  # name -> torch.cuda.Event while stage timing is on
+        recorded: set = set()
 
         def mark(self, name):
             if self.marks is not None:
                 self.marks[name].record(torch.cuda.current_stream(dev))
+                self.recorded.add(name)
 
         def router_logits(self, x, router_weight):
             self.mark("layer")
@@ -602,8 +604,8 @@ def _stage_summary(samples: list[dict], dev) -> dict:
     return {n: float(x) for n, x in zip(names, v.tolist())}
 
 
-def _read_marks(marks: dict) -> dict:
-    return {n: marks[a].elapsed_time(marks[b]) for n, a, b in EP_STAGES if a in marks and b in marks}
+def _read_marks(marks: dict, recorded: set) -> dict:
+    return {n: marks[a].elapsed_time(marks[b]) for n, a, b in EP_STAGES if a in recorded and b in recorded}
 
 
 def ep_stage_times(eops, run, x, dev, stream, reps: int = 20) -> dict:
@@ -615,6 +617,7 @@ def ep_stage_times(eops, run, x, dev, stream, reps: int = 20) -> dict:
     marks = {m: torch.cuda.Event(enable_timing=True, external=True) for m in names}
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(stream)
+    eops.recorded = set()
     with torch.cuda.stream(cap):
         run(x)
         g = torch.cuda.CUDAGraph()
@@ -630,7 +633,7 @@ def ep_stage_times(eops, run, x, dev, stream, reps: int = 20) -> dict:
     for _ in range(reps):
         g.replay()
         torch.cuda.synchronize(dev)
-        samples.append(_read_marks(marks))
+        samples.append(_read_marks(marks, eops.recorded))
     del g
     return _stage_summary(samples, dev)
 
@@ -699,9 +702,10 @@ def ep_config5(args, eops, routers, experts_all, shareds, world, rank, dev, stre
             names = {m for _, a, b in EP_STAGES for m in (a, b)}
             for i in range(3):
                 eops.marks = {m: torch.cuda.Event(enable_timing=True) for m in names}
+                eops.recorded = set()
                 layers[0].forward(xs[0])
                 torch.cuda.synchronize(dev)
-                samples.append(_read_marks(eops.marks))
+                samples.append(_read_marks(eops.marks, eops.recorded))
                 eops.marks = None
             stages = _stage_summary(samples, dev)
         dist.barrier()

@@ -92,11 +92,17 @@ int launch_combine_rows_add_norm(const float* d, int W, const int32_t* inv_rows,
                                  void* out, cudaStream_t s, const int64_t* inverse = nullptr,
                                  int T_out = 0, int32_t* status = nullptr, bool rows_bf16 = false);
 
-// Router projection (fixed fp32 summation order); from 256 tokens a tiled
-// kernel (same order) streams 32-token x 16-row tiles.
+// Router projection. Below 256 tokens CUDA-core kernels with one fixed fp32
+// summation order (the oracle's); from 256 tokens a tcgen05 bf16 GEMM (fp32
+// accumulation in the tensor core's own order, like the reference's F.linear).
+// Rows named by a keep map are first copied into `gather_scratch` (bf16
+// [T, H], nullable: without it they stay on the CUDA-core kernels), so a
+// gathered call and a call on the materialised rows give the same logits.
+// `status` (nullable) receives a bounded-wait timeout or a bad keep row.
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
-                          cudaStream_t s, const RowGather& rg = RowGather{});
+                          cudaStream_t s, const RowGather& rg = RowGather{},
+                          int32_t* status = nullptr, void* gather_scratch = nullptr);
 
 void launch_route_topk(const void* logits, int logits_dtype, int64_t stride, int T, int E, int k,
                        const float* bias, int64_t* ids, void* weights, int weights_dtype,

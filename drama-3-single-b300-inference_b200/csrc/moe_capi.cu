@@ -695,7 +695,9 @@ static int moe_layer_impl(const void* x, int64_t x_stride, const void* router_w,
     an.status = st;
   }
   stage_mark(0, s);
-  launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s, rg);
+  // b.d (expert rows, written only by the down step) holds the kept rows
+  // for the tensor-core router when a keep map is given
+  launch_router_logits(x, x_stride, router_w, router_bias, E, E + 1, H, T, b.logits, E + 1, s, rg, st, b.d);
   if ((rc = check_launch("router_logits"))) return rc;
   const int P = T * k;
   const bool fused = fused_permute(T, k, E);

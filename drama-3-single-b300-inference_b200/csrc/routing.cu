@@ -3,6 +3,7 @@
 #include "d3_common.cuh"
 #include "d3_host.h"
 #include "d3_internal.h"
+#include "router_tc.cuh"
 
 namespace d3 {
 
@@ -96,6 +97,9 @@ constexpr int kRtTok = 32, kRtRows = 16, kRtStages = 4, kRtThreads = 256;
 constexpr int kRtStageElems = (kRtTok + kRtRows) * 256;
 constexpr size_t kRtSmem = static_cast<size_t>(kRtStages) * kRtStageElems * 2;  // 96 KB
 constexpr int kRouterTiledMinTokens = 256;
+// From this many tokens the projection runs on the tensor cores (router_tc.cuh)
+// unless the rows are gathered through a keep map.
+constexpr int kRouterTcMinTokens = 256;
 
 __global__ void __launch_bounds__(kRtThreads)
     router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
@@ -683,10 +687,82 @@ __global__ void __launch_bounds__(kPlanRowsThreads)
 
 }  // namespace
 
+namespace {
+
+// dst bf16 [T, H] = x[keep[t]] (a keep value outside [0, x_rows) records
+// kDevBadRow and reads row 0, as every row-map reader does). The tensor-core
+// router reads its rows by TMA, which cannot follow the map; the reference
+// materialises the kept rows the same way (x.index_select) before its router.
+__global__ void gather_keep_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
+                                        int H, RowGather rg, __nv_bfloat16* __restrict__ dst) {
+  pdl_enter();
+  const int per_row = H / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(T) * per_row) return;
+  const int64_t t = idx / per_row;
+  const int c = static_cast<int>(idx - t * per_row);
+  const uint4* src = reinterpret_cast<const uint4*>(x + gather_row(rg, t) * x_stride);
+  reinterpret_cast<uint4*>(dst + t * H)[c] = __ldg(src + c);
+}
+
+bool router_tc_fits(const void* x, int64_t x_stride, const void* w, int R, int H) {
+  return H % 64 == 0 && x_stride % 8 == 0 && aligned(x, 16) && aligned(w, 16) && R <= 4 * kRtcMaxN;
+}
+
+// The tensor-core router (router_tc.cuh) for contiguous x with a TMA-able
+// layout; false when the layout does not allow it (the caller then runs the
+// CUDA-core kernel).
+bool launch_router_tc(const void* x, int64_t x_stride, const void* w, const float* bias, int nbias,
+                      int R, int H, int T, void* logits, int64_t logits_stride, cudaStream_t s,
+                      int32_t* status) {
+  if (!router_tc_fits(x, x_stride, w, R, H)) return false;
+  const int ntiles = (R + kRtcMaxN - 1) / kRtcMaxN;
+  const int nt = ((R + ntiles - 1) / ntiles + 15) / 16 * 16;
+  CUtensorMap tx, tw;
+  if (encode_tmap_2d(&tx, x, 2, H, T, static_cast<uint64_t>(x_stride) * 2, 64, kRtcTokens)) return false;
+  if (encode_tmap_2d(&tw, w, 2, H, R, static_cast<uint64_t>(H) * 2, 64, nt)) return false;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(RtcSmem::bytes(kRtcMaxN)));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  RouterTcArgs a{};
+  a.bias = bias;
+  a.nbias = nbias;
+  a.R = R;
+  a.T = T;
+  a.KB = H / 64;
+  a.nt = nt;
+  a.out = static_cast<__nv_bfloat16*>(logits);
+  a.out_stride = logits_stride;
+  a.status = status;
+  launch_kernel(router_tc_kernel, dim3((T + kRtcTokens - 1) / kRtcTokens, ntiles), dim3(kRtcThreads),
+                RtcSmem::bytes(nt), s, tx, tw, a);
+  return true;
+}
+
+}  // namespace
+
 void launch_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
                           int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
-                          cudaStream_t s, const RowGather& rg) {
+                          cudaStream_t s, const RowGather& rg, int32_t* status,
+                          void* gather_scratch) {
   if (T <= 0 || R <= 0) return;
+  if (T >= kRouterTcMinTokens && rg.keep == nullptr &&
+      launch_router_tc(x, x_stride, w, bias, nbias, R, H, T, logits, logits_stride, s, status))
+    return;
+  if (T >= kRouterTcMinTokens && rg.keep != nullptr && gather_scratch &&
+      router_tc_fits(gather_scratch, H, w, R, H)) {
+    const int64_t n = static_cast<int64_t>(T) * (H / 8);
+    launch_kernel(gather_keep_rows_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+                  static_cast<const __nv_bfloat16*>(x), x_stride, T, H, rg,
+                  static_cast<__nv_bfloat16*>(gather_scratch));
+    if (launch_router_tc(gather_scratch, H, w, bias, nbias, R, H, T, logits, logits_stride, s, status))
+      return;
+  }
   if (T >= kRouterTiledMinTokens) {
     static bool configured[64] = {false};
     int dev = 0;
@@ -789,8 +865,9 @@ int launch_permute(const int64_t* ids, int T, int k, int E, int block_m, int32_t
 
 using namespace d3;
 
-extern "C" int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H,
-                                int T, void* logits, int64_t logits_stride, d3_stream_t stream) {
+extern "C" int d3_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
+                                int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
+                                d3_stream_t stream) {
   D3_REQUIRE(T >= 0 && R > 0 && H > 0 && H % 128 == 0, "router_logits: bad shape R=%d H=%d", R, H);
   D3_REQUIRE(T >= kRouterTiledMinTokens || H <= 256 * kRouterMaxIters,
              "router_logits: H=%d above the %d the decode kernel holds in registers", H,
@@ -798,7 +875,9 @@ extern "C" int d3_router_logits(const void* x, int64_t x_stride, const void* w, 
   D3_REQUIRE(x_stride >= H && x_stride % 8 == 0, "router_logits: x row stride must be >= H and a multiple of 8");
   D3_REQUIRE(logits_stride >= R, "router_logits: logits row stride must be >= R");
   D3_REQUIRE(aligned(x, 16) && aligned(w, 16), "router_logits: misaligned pointer");
-  launch_router_logits(x, x_stride, w, nullptr, 0, R, H, T, logits, logits_stride,
+  D3_REQUIRE(nbias >= 0 && nbias <= R && (bias != nullptr || nbias == 0),
+             "router_logits: nbias=%d must be in [0, R] with a bias pointer", nbias);
+  launch_router_logits(x, x_stride, w, bias, nbias, R, H, T, logits, logits_stride,
                        reinterpret_cast<cudaStream_t>(stream));
   return check_launch("router_logits");
 }

@@ -76,7 +76,9 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _i64,
          _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
-    "d3_router_logits": (_i32, [_c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _c_void_p, _i64, _c_void_p]),
+    "d3_router_logits": (
+        _i32, [_c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _i64, _c_void_p]
+    ),
     "d3_route_topk": (
         _i32,
         [_c_void_p, _i32, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],

@@ -94,8 +94,11 @@ def quant_act_fp8(x: torch.Tensor, transposed: bool = False):
     return q, s
 
 
-def router_logits(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """bf16 logits [T,R] = x . weight^T with the fixed summation order."""
+def router_logits(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 logits [T,R] = bf16(x . weight^T + bias) with fp32 accumulation
+    (bias f32 on the first len(bias) columns, before the rounding). Below 256
+    tokens the sum runs in the oracle's fixed order; from 256 tokens on the
+    tensor cores (the kernels d3_moe_layer uses at the same T)."""
     _require_cuda(x, weight)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise ValueError("router projection takes bf16 x and weight")
@@ -103,8 +106,14 @@ def router_logits(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     R = weight.shape[0]
     if weight.shape[1] != H or not weight.is_contiguous():
         raise ValueError("router weight must be contiguous [R, H]")
+    nbias = 0
+    if bias is not None:
+        _require_cuda(bias)
+        if bias.dtype != torch.float32 or bias.dim() != 1 or not bias.is_contiguous() or bias.numel() > R:
+            raise ValueError("router bias must be a contiguous float32 vector of at most R entries")
+        nbias = bias.numel()
     out = torch.empty((T, R), dtype=torch.bfloat16, device=x.device)
-    call("d3_router_logits", x.data_ptr(), _row_stride(x), weight.data_ptr(), R, H, T,
+    call("d3_router_logits", x.data_ptr(), _row_stride(x), weight.data_ptr(), _ptr(bias), nbias, R, H, T,
          out.data_ptr(), out.stride(0), _stream(x.device))
     return out
 

@@ -86,13 +86,20 @@ D3_API int d3_prepare_moe_input(const void* x, int64_t x_stride, const void* rou
                          float* logits, d3_stream_t stream);
 
 /* --------------------------------------------------- (a1) router projection --
- * logits bf16 [T, R] = x bf16 [T,H] . W bf16 [R,H]^T with a fixed fp32
- * summation order (see oracle.moe_oracle.router_logits), rounded to bf16.
- * Replaces linear(x, layer.gate.weight) / the packed router slice
- * (src/drama3/model.py:496-504, kernels.py:274-287). R = E (+1 for the
- * shared-expert gate row). */
-D3_API int d3_router_logits(const void* x, int64_t x_stride, const void* w, int R, int H, int T,
-                     void* logits, int64_t logits_stride, d3_stream_t stream);
+ * logits bf16 [T, R] = bf16(x bf16 [T,H] . W bf16 [R,H]^T + bias[r]) with
+ * fp32 accumulation; bias f32 [nbias] (nullable) is added to the first nbias
+ * columns before the rounding. Replaces linear(x, layer.gate.weight) / the
+ * packed router slice (src/drama3/model.py:496-504, kernels.py:274-287).
+ * R = E (+1 for the shared-expert gate row). Below 256 tokens the sum runs
+ * in one fixed fp32 order (restated by oracle.moe_oracle.router_logits); from
+ * 256 tokens, with H a multiple of 64, it is a tcgen05 bf16 GEMM whose fp32
+ * accumulation order is the tensor core's own (as in the reference's bf16
+ * F.linear), deterministic from call to call. d3_moe_layer and its variants
+ * use the same kernels, so this call reproduces a layer's logits bit for bit
+ * at the same T. */
+D3_API int d3_router_logits(const void* x, int64_t x_stride, const void* w, const float* bias,
+                            int nbias, int R, int H, int T, void* logits, int64_t logits_stride,
+                            d3_stream_t stream);
 
 
 /* ------------------------------------------------------------ (a2) route --

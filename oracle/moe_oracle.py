@@ -124,11 +124,14 @@ def prepare_moe_input(x, router, row_slots=None, padding_start=None, values=Fals
 
 
 def router_logits(x, w, bias=None, nbias=None):
-    """bf16 logits = x . w^T in the fixed fp32 order of the CUDA kernel:
-    lane l (of 32) accumulates k = 256*i + 8*l + j sequentially (i, then
-    j = 0..7), then lanes combine by xor-butterfly 16, 8, 4, 2, 1; + bias;
-    rounded to bf16. Replaces linear(x, layer.gate.weight)
-    (src/drama3/model.py:496-504) with a reproducible order."""
+    """bf16 logits = x . w^T in the fixed fp32 order of the CUDA-core router
+    kernels (used below 256 tokens): lane l (of 32) accumulates
+    k = 256*i + 8*l + j sequentially (i, then j = 0..7), then lanes combine by
+    xor-butterfly 16, 8, 4, 2, 1; + bias; rounded to bf16. Replaces
+    linear(x, layer.gate.weight) (src/drama3/model.py:496-504) with a
+    reproducible order. The tensor-core router used from 256 tokens sums in
+    the hardware's order and is held to one bf16 ulp of this value (or the
+    fp32 noise floor where the sum cancels to near zero)."""
     x = np.asarray(x, dtype=np.float32)
     w = np.asarray(w, dtype=np.float32)
     T, H = x.shape

@@ -60,3 +60,47 @@ def experts_to_oracle(ex) -> "O.Experts":
     s13 = ex.w13_scale_inv.cpu().numpy()
     s2 = ex.w2_scale_inv.cpu().numpy()
     return O.Experts(w13, s13, w2, s2)
+
+
+def assert_logits_close(got, ref, what: str):
+    """Two roundings to bf16 of the same fp32-accumulated dot products in
+    different summation orders: within one bf16 ulp of each other, or, for
+    logits near zero where the sum cancels, within the fp32 accumulation noise
+    floor (2^-16 of the row's RMS logit)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    if not got.size:
+        return
+    mag = np.maximum(np.abs(got), np.abs(ref))
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(mag, 1e-30))) - 7)
+    floor = np.sqrt((ref ** 2).mean(axis=-1, keepdims=True)) * 2.0 ** -16
+    excess = np.abs(got - ref) - np.maximum(ulp, floor)
+    bad = np.argwhere(excess > 0)
+    assert not len(bad), (f"{what}: {len(bad)} logits beyond one bf16 ulp / the noise floor, e.g. "
+                          f"{[(tuple(i), float(got[tuple(i)]), float(ref[tuple(i)])) for i in bad[:4]]}")
+
+
+def device_logits_routing(x: np.ndarray, router, E: int, k: int, bias: np.ndarray | None = None,
+                          chunk: int = 1024):
+    """Routing parity for a layer call on x (bf16 values as float32).
+
+    From 256 tokens the router projection runs on the tensor cores, whose fp32
+    accumulation order is the hardware's own (the reference's bf16 F.linear is
+    the same), so the check is in two parts: (1) the device logits, from the
+    same kernel the layer runs at this T, lie within one bf16 ulp of the
+    oracle's fixed-order logits (or within the fp32 noise floor for logits
+    that cancel to near zero, assert_logits_close); (2) the oracle's top-k of
+    the DEVICE logits is what the layer must return, bit for bit. Below 256
+    tokens the two logits are identical. Returns (device logits, oracle ids,
+    oracle weights) as numpy arrays."""
+    from d3moe import ops
+
+    bt = None if bias is None else torch.from_numpy(np.asarray(bias, np.float32)).cuda()
+    lg_dev = from_bf16(ops.router_logits(to_bf16(x), router, bias=bt))
+    rw = from_bf16(router)
+    lg_o = np.concatenate([O.router_logits(x[i:i + chunk], rw, bias, nbias=E)
+                           for i in range(0, len(x), chunk)])
+    assert_logits_close(lg_dev, lg_o, "router logits vs the oracle's")
+    w, ids = O.route(lg_dev[:, :E], k)
+    return lg_dev, ids, O.bf16_round(w)
+

@@ -13,7 +13,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from helpers import experts_to_oracle, from_bf16, rel_l2, to_bf16, ulps_bf16  # noqa: E402
+from helpers import device_logits_routing, experts_to_oracle, from_bf16, rel_l2, to_bf16, ulps_bf16  # noqa: E402
 from oracle import moe_oracle as O  # noqa: E402
 
 
@@ -117,9 +117,8 @@ def test_fused_layer_exit_matches_two_step(d3, layer, T, prefill):
     torch.cuda.synchronize()
     assert torch.equal(r_fused, r_two)
     assert torch.equal(out_fused, out_two)
-    logits = O.router_logits(x, from_bf16(lw.router))
-    w_o, ids_o = O.route(logits[:, :128], 8)
-    routed_o, sh_o = O.moe_experts(x, ids_o, O.bf16_round(w_o), ex, sh, rows_bf16=prefill)
+    logits, ids_o, w_o = device_logits_routing(x, lw.router, 128, 8)
+    routed_o, sh_o = O.moe_experts(x, ids_o, w_o, ex, sh, rows_bf16=prefill)
     out_o, res_o = O.combine_experts_add_norm(routed_o, sh_o, logits[:, 128:129], res0, nw, 1e-6)
     # the residual (|v| up to ~8) and the normalised rows carry the MoE output's
     # tolerance-level differences (max-abs 2e-2) through one more bf16 rounding

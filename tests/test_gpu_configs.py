@@ -25,7 +25,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from helpers import assert_close, experts_to_oracle, from_bf16, to_bf16, ulps_bf16  # noqa: E402
+from helpers import assert_close, device_logits_routing, experts_to_oracle, from_bf16, to_bf16, ulps_bf16  # noqa: E402
 from oracle import moe_oracle as O  # noqa: E402
 
 E, I, H, K = 128, 768, 2048, 8
@@ -51,13 +51,6 @@ def _layer(seed: int, router_bias=None):
     return lw, experts_to_oracle(lw.experts), experts_to_oracle(lw.shared)
 
 
-def _oracle_routing(x, router, bias, chunk=1024):
-    """Oracle router projection (fixed fp32 order, bias added before the bf16
-    rounding) and top-k over every token, in token chunks."""
-    logits = np.concatenate([O.router_logits(x[i:i + chunk], router, bias, nbias=E)
-                             for i in range(0, len(x), chunk)])
-    w, ids = O.route(logits[:, :E], K)
-    return logits, ids, O.bf16_round(w)
 
 
 def _check_prefill(lw, ex, sh, x: np.ndarray, bias: np.ndarray | None, seed: int, what: str):
@@ -74,8 +67,7 @@ def _check_prefill(lw, ex, sh, x: np.ndarray, bias: np.ndarray | None, seed: int
                                     return_routing=True, status=status)
     torch.cuda.synchronize()
     assert int(status[0]) == 0
-    router = from_bf16(lw.router)
-    logits, ids_o, w_o = _oracle_routing(x, router, bias)
+    logits, ids_o, w_o = device_logits_routing(x, lw.router, E, K, bias=bias)
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o, err_msg=f"{what}: routing ids")
     assert ulps_bf16(from_bf16(w), w_o).max() <= 1, f"{what}: routing weights"
     rng = np.random.default_rng(seed)

@@ -9,8 +9,8 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from helpers import (assert_close, fp8_bytes, from_bf16, to_bf16,  # noqa: E402
-                     to_fp8, ulps_bf16)
+from helpers import (assert_close, assert_logits_close, fp8_bytes, from_bf16,  # noqa: E402
+                     to_bf16, to_fp8, ulps_bf16)
 from oracle import moe_oracle as O  # noqa: E402
 
 
@@ -66,18 +66,77 @@ def test_quant_act_matches_oracle_bytes(d3, T):
 
 
 # ------------------------------------------------------------------- (a1) --
-# T >= 256 runs the tiled prefill kernel (32-token x 16-row tiles through a
-# cp.async ring) in the same summation order; 300 and 129/33 rows leave ragged
-# tiles, H=384 a half-filled last 256-wide block, H=4096 is beyond the decode
-# kernel's register-held weight row.
+# Below 256 tokens the CUDA-core kernel sums in the oracle's fixed order (bit
+# for bit); 129/33 rows leave ragged tiles and H=384 a half-filled last
+# 256-wide block.
 @pytest.mark.parametrize("T,R,H", [(1, 129, 2048), (64, 129, 2048), (13, 257, 2048), (5, 33, 384),
-                                   (256, 129, 2048), (300, 129, 2048), (513, 33, 384), (260, 17, 4096)])
+                                   (255, 129, 2048)])
 def test_router_logits_bit_exact(d3, T, R, H):
     rng = np.random.default_rng(R + T)
     x = O.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
     w = O.bf16_round((rng.standard_normal((R, H)) * 0.02).astype(np.float32))
     got = from_bf16(d3["ops"].router_logits(to_bf16(x), to_bf16(w)))
     np.testing.assert_array_equal(got, O.router_logits(x, w))
+
+
+def test_router_logits_gathered_rows_match_materialised_rows(d3):
+    """A layer call through a keep map (rows gathered in the library) routes
+    exactly like the call on the materialised rows x[keep] (the reference's
+    index_select), on both router paths (kept rows below and from 256)."""
+    from d3moe import synth
+    lw = synth.make_layer(128, 768, 2048, seed=4, device="cuda")
+    rng = np.random.default_rng(12)
+    x = to_bf16(O.bf16_round(rng.standard_normal((340, 2048)).astype(np.float32)))
+    for n in (200, 300):
+        keep = torch.from_numpy(np.sort(rng.choice(340, n, replace=False)).astype(np.int64)).cuda()
+        out_k, ids_k, w_k = d3["ops"].moe_layer(x, lw.router, lw.experts, lw.shared, 8, keep=keep,
+                                                return_routing=True)
+        out_m, ids_m, w_m = d3["ops"].moe_layer(x.index_select(0, keep), lw.router, lw.experts, lw.shared,
+                                                8, return_routing=True)
+        torch.cuda.synchronize()
+        assert torch.equal(ids_k, ids_m) and torch.equal(w_k, w_m), n
+        assert torch.equal(out_k, out_m), n
+
+
+def _router_exact(x, w, bias=None):
+    """float64 value of x . w^T (+ bias) before the bf16 rounding."""
+    v = x.astype(np.float64) @ w.astype(np.float64).T
+    if bias is not None:
+        v[:, : len(bias)] += bias
+    return v
+
+
+# From 256 tokens the projection is a tcgen05 bf16 GEMM (fp32 accumulation in
+# the tensor core's order): every logit is the float64 value rounded to bf16 up
+# to fp32 accumulation noise, within one bf16 ulp (or the noise floor) of the
+# oracle, and bit-identical from call to call. 300 tokens and 129/33 rows
+# leave ragged tiles; 257 rows take two 144-row tiles; H=384 and 4096 change
+# the K loop; a bias on the first R-1 columns is added before the rounding.
+@pytest.mark.parametrize("T,R,H,biased", [(256, 129, 2048, False), (300, 129, 2048, True),
+                                          (513, 33, 384, False), (260, 17, 4096, False),
+                                          (300, 257, 2048, True), (4100, 129, 2048, True)])
+def test_router_logits_tensor_core(d3, T, R, H, biased):
+    rng = np.random.default_rng(R + T + H)
+    x = O.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    w = O.bf16_round((rng.standard_normal((R, H)) * 0.02).astype(np.float32))
+    bias = rng.standard_normal(R - 1).astype(np.float32) if biased else None
+    bt = None if bias is None else torch.from_numpy(bias).cuda()
+    got = d3["ops"].router_logits(to_bf16(x), to_bf16(w), bias=bt)
+    again = d3["ops"].router_logits(to_bf16(x), to_bf16(w), bias=bt)
+    torch.cuda.synchronize()
+    assert torch.equal(got, again)
+    g = from_bf16(got)
+    exact = _router_exact(x, w, bias)
+    # the float64 value rounded once to bf16, up to fp32 accumulation noise
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exact), 1e-30))) - 7)
+    noise = np.sqrt((exact ** 2).mean(axis=1, keepdims=True)) * 2.0 ** -16
+    excess = np.abs(g - exact) - (0.5 * ulp + noise)
+    bad = np.argwhere(excess > 0)
+    assert not len(bad), (f"{len(bad)} logits above the rounding bound, e.g. "
+                          f"{[(tuple(i), float(g[tuple(i)]), float(exact[tuple(i)])) for i in bad[:4]]}")
+    s = slice(0, min(T, 600))
+    assert_logits_close(g[s], O.router_logits(x[s], w, bias, nbias=None if bias is None else R - 1),
+                        "tensor-core router vs the oracle")
 
 
 # ------------------------------------------------------------------- (a2) --

@@ -14,7 +14,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from helpers import assert_close, experts_to_oracle, from_bf16, to_bf16  # noqa: E402
+from helpers import assert_close, device_logits_routing, experts_to_oracle, from_bf16, to_bf16  # noqa: E402
 from oracle import moe_oracle as O  # noqa: E402
 
 E, I, H, K = 128, 768, 2048, 8
@@ -43,7 +43,9 @@ def test_prefill_layer_matches_oracle(layer, T):
     with ops.prefill_min_tokens(1):
         out, ids, w = ops.moe_layer(to_bf16(x), lw.router, lw.experts, lw.shared, K,
                                     return_routing=True, status=status)
-    ref, ids_o, _ = O.moe_layer(x, from_bf16(lw.router), ex, sh, K, rows_bf16=True)
+    lg, ids_o, w_o = device_logits_routing(x, lw.router, E, K)
+    routed, shared = O.moe_experts(x, ids_o, w_o, ex, sh, rows_bf16=True)
+    ref = O.combine_experts(routed, shared, lg[:, E])
     assert int(status[0]) == 0
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
     assert_close(from_bf16(out), ref, what=f"prefill layer T={T}")
@@ -61,7 +63,9 @@ def test_prefill_hot_experts_span_tiles(layer):
     with ops.prefill_min_tokens(1):
         out, ids, _ = ops.moe_layer(to_bf16(x), lw.router, lw.experts, lw.shared, K,
                                     router_bias=torch.from_numpy(bias).cuda(), return_routing=True)
-    ref, ids_o, _ = O.moe_layer(x, from_bf16(lw.router), ex, sh, K, bias=bias, rows_bf16=True)
+    lg, ids_o, w_o = device_logits_routing(x, lw.router, E, K, bias=bias)
+    routed, shared = O.moe_experts(x, ids_o, w_o, ex, sh, rows_bf16=True)
+    ref = O.combine_experts(routed, shared, lg[:, E])
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
     assert_close(from_bf16(out), ref, what="prefill hot experts")
 
