@@ -1013,6 +1013,29 @@ def _load_flashinfer_moe():
     return trtllm_fp8_block_scale_moe
 
 
+def _moe_float64(q, qs_t, ids, w, w13, s13, w2, s2):
+    """float64 value of the routed experts on the dequantised operands, with
+    no intermediate quantisation: sum_j w_j * W2_e (silu(G_e x) * (U_e x)),
+    W13 in [up | gate] order. The yardstick both FP8 implementations are
+    measured against (each rounds its SiLU*mul output to E4M3 its own way)."""
+    import torch
+
+    def deq(wq, sc):  # e4m3 [.., N, K] with [.., N/128, K/128] block scales
+        wf = wq.to(torch.float64)
+        return wf * sc.to(torch.float64).repeat_interleave(128, -2).repeat_interleave(128, -1)
+
+    T, Hh = q.shape
+    x = q.to(torch.float64) * qs_t.t().to(torch.float64).repeat_interleave(128, -1)
+    out = torch.zeros((T, Hh), dtype=torch.float64, device=q.device)
+    for e in torch.unique(ids).tolist():
+        rows, slot = (ids == e).nonzero(as_tuple=True)
+        h = x[rows] @ deq(w13[e], s13[e]).t()
+        up, gate = h.chunk(2, dim=1)
+        a = gate / (1.0 + torch.exp(-gate)) * up
+        out.index_add_(0, rows, (a @ deq(w2[e], s2[e]).t()) * w[rows, slot].to(torch.float64)[:, None])
+    return out
+
+
 def flashinfer_comparison(dev, sizes=(64, 1344, 8192), iters: int = 20, warmup: int = 3) -> dict:
     """Same-box comparison with the reference's own Blackwell MoE kernel:
     FlashInfer trtllm_fp8_block_scale_moe called exactly as
@@ -1086,9 +1109,15 @@ def flashinfer_comparison(dev, sizes=(64, 1344, 8192), iters: int = 20, warmup: 
             our_ms, our_y = timed(lambda: fc.trtllm_fp8_block_scale_moe(**kw))
             d = (fi_y.float() - our_y.float())
             rel = float(d.norm() / our_y.float().norm().clamp_min(1e-30))
-            out["sizes"][str(T)] = {"flashinfer_ms": fi_ms, "ours_ms": our_ms,
-                                    "speedup_vs_flashinfer": fi_ms / our_ms,
-                                    "rel_l2_between_outputs": rel}
+            row = {"flashinfer_ms": fi_ms, "ours_ms": our_ms, "speedup_vs_flashinfer": fi_ms / our_ms,
+                   "rel_l2_between_outputs": rel}
+            if T <= 1344:
+                wts, ids = ops.route_topk(logits, TOPK, weights_dtype=torch.bfloat16)
+                ref = _moe_float64(q, qs, ids, wts, w13, s13, w2, s2)
+                nrm = ref.norm().clamp_min(1e-30)
+                row["rel_l2_vs_float64"] = {"flashinfer": float((fi_y.double() - ref).norm() / nrm),
+                                            "ours": float((our_y.double() - ref).norm() / nrm)}
+            out["sizes"][str(T)] = row
         except Exception as e:  # noqa: BLE001
             out["sizes"][str(T)] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     del ex, w13, s13
