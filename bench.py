@@ -640,9 +640,10 @@ def ep_stage_times(eops, run, x, dev, stream, reps: int = 20) -> dict:
 
 def ep_config5(args, eops, routers, experts_all, shareds, world, rank, dev, stream) -> dict:
     """Expert-parallel layer at the job-level batch sizes of the fifth
-    benchmark configuration: 512 decode tokens (capacity mode, CUDA graph)
-    and 8192 prefill tokens (exact mode, eager) split evenly over the ranks,
-    bf16 N(0,1) inputs from seed 4. Times are the max over ranks."""
+    benchmark configuration: 512 decode tokens and 8192 prefill tokens split
+    evenly over the ranks, bf16 N(0,1) inputs from seed 4; capacity mode
+    replayed from CUDA graphs, exact mode eager. Times are the max over
+    ranks."""
     import torch
     import torch.distributed as dist
 
@@ -650,7 +651,11 @@ def ep_config5(args, eops, routers, experts_all, shareds, world, rank, dev, stre
 
     out = {}
     nl = len(routers)
-    for kind, total, mode in (("decode", 512, "capacity"), ("prefill", 8192, "exact")):
+    # prefill both ways: capacity (every token to every rank, no host read,
+    # graph-captured) and exact (only the owning ranks, one host read of the
+    # row counts per call)
+    for kind, total, mode in (("decode", 512, "capacity"), ("prefill", 8192, "capacity"),
+                              ("prefill_exact", 8192, "exact")):
         T = total // world
         layers = [ExpertParallelMoE(routers[i], experts_all[i], shareds[i], E, TOPK, ops=eops, mode=mode)
                   for i in range(nl)]
