@@ -1130,6 +1130,91 @@ def flashinfer_comparison(dev, sizes=(64, 1344, 8192), iters: int = 20, warmup: 
     return out
 
 
+def reference_triton_comparison(dev, sizes=(1, 8), iters: int = 50, warmup: int = 3) -> dict:
+    """Same-box comparison with the reference's own Triton decode kernels
+    (src/drama3/kernels.py:290-357, small_batch_moe: the routed MoE for
+    T <= 8 tokens, model.py:520-530), imported from the unmodified reference
+    installed in baseline/_ref. They are hard-wired to the reference model's
+    expert shapes (E=256, I=512, H=2048, top-8), so both sides run there. The
+    reference's activation quantisers come from Fish Speech's fp8_moe module,
+    which is not in this image; this library's byte-identical quantisers
+    (d3_quant_act_fp8, d3_silu_mul_quant) stand in for them, and only the two
+    reference Triton kernels plus those two quantisers are timed. Ours:
+    d3moe.ops.moe_experts (routed experts only) on the same routing. Both are
+    replayed from CUDA graphs; CUDA events on the launching stream."""
+    import torch
+
+    from d3moe import ops, synth
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "drama3" / "kernels.py").exists():
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    sys.path.insert(0, str(ref_root))
+    try:
+        from drama3 import kernels as rk
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference import failed: {type(e).__name__}: {e}"[:300]}
+    Er, Ir = 256, 512
+    ex = synth.make_experts(Er, Ir, H, seed=91, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(6)
+    stream = torch.cuda.current_stream(dev)
+    out = {"kernels": "drama3.kernels.expert_up_kernel + expert_down_kernel (Triton, the reference's "
+                      "small_batch_moe), quantisers from this library",
+           "ours": "d3moe.ops.moe_experts (routed experts only)",
+           "shapes": f"E={Er} I={Ir} H={H} top-8 (the reference model's expert shapes)", "sizes": {}}
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                res = fn()
+        stream.wait_stream(cap)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / iters, res.clone()
+
+    for T in sizes:
+        try:
+            x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+            logits = torch.randn((T, Er), generator=g, device=dev).to(torch.bfloat16)
+            w, ids = ops.route_topk(logits, TOPK, weights_dtype=torch.bfloat16)
+
+            def run_ref():
+                q, qs = ops.quant_act_fp8(x)
+                gate_up = torch.empty((T * TOPK, 2 * Ir), dtype=x.dtype, device=dev)
+                rk.expert_up_kernel[(T, TOPK, 2 * Ir // 4)](q, qs, ex.w13_weight, ex.w13_scale_inv, ids,
+                                                            gate_up, 4, num_warps=4)
+                a, sa = ops.silu_mul_quant(gate_up)
+                y = torch.empty_like(x)
+                rk.expert_down_kernel[(T, H // 4)](a, sa, ex.w2_weight, ex.w2_scale_inv, ids, w, y, 4,
+                                                   num_warps=8)
+                return y
+
+            ref_ms, ref_y = timed(run_ref)
+            our_ms, our_y = timed(lambda: ops.moe_experts(x, ids, w, ex)[0])
+            d = ref_y.float() - our_y.float()
+            out["sizes"][str(T)] = {"reference_triton_ms": ref_ms, "ours_ms": our_ms,
+                                    "speedup_vs_reference": ref_ms / our_ms,
+                                    "rel_l2_between_outputs": float(d.norm() / our_y.float().norm())}
+        except Exception as e:  # noqa: BLE001
+            out["sizes"][str(T)] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    del ex
+    torch.cuda.empty_cache()
+    return out
+
+
 def mixed_rows(reuse: bool):
     """Rows of the mixed decode + packed-prefill call of the reference's D64/P1280
     graph (src/drama3/mixed_graph.py:33-50): 64 decode rows (the last 6 padding
@@ -1842,6 +1927,7 @@ def main() -> None:
         }
         line["stack24"] = measure_stack24(dev, replays=args.stack_replays)
         line["vs_flashinfer"] = flashinfer_comparison(dev)
+        line["vs_reference_triton"] = reference_triton_comparison(dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

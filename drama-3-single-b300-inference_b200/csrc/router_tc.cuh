@@ -5,7 +5,8 @@
 // (F.linear, src/drama3/model.py:496-504), so the fp32 summation order inside
 // the tensor core is as unspecified there as here.
 //
-// One CTA per 128-token x NT-row tile (NT <= 256, a multiple of 16): warp 0
+// One CTA per 128-token x NT-row tile (NT <= 256, a multiple of 16; the rows
+// are split into enough tiles that the grid covers the SMs): warp 0
 // streams 64-wide K blocks of x and W through a 4-stage TMA ring (128-byte
 // swizzled, K-major), warp 1 issues tcgen05.mma kind::f16 (bf16 x bf16 ->
 // fp32, M=128, N=NT, K=16) into one TMEM accumulator, and all four warps read
@@ -29,6 +30,7 @@ struct RouterTcArgs {
   int nbias;
   int R, T, KB;       // rows of W, tokens, 64-wide K blocks
   int nt;             // rows of W per tile (multiple of 16, <= 256)
+  int tmem_cols;      // TMEM columns allocated (power of two >= max(32, nt))
   __nv_bfloat16* out;
   int64_t out_stride;
   int32_t* status;    // nullable
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kRtcThreads, 1)
     }
   }
   if (warp == 1) {
-    tc::tmem_alloc(tslot, kRtcMaxN);
+    tc::tmem_alloc(tslot, static_cast<uint32_t>(args.tmem_cols));
     tc::tmem_relinquish();
   }
   tc::fence_before_thread_sync();
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(kRtcThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc::fence_after_thread_sync();
-    tc::tmem_dealloc(tmem, kRtcMaxN);
+    tc::tmem_dealloc(tmem, static_cast<uint32_t>(args.tmem_cols));
   }
 }
 

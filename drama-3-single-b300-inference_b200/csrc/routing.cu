@@ -716,8 +716,16 @@ bool launch_router_tc(const void* x, int64_t x_stride, const void* w, const floa
                       int R, int H, int T, void* logits, int64_t logits_stride, cudaStream_t s,
                       int32_t* status) {
   if (!router_tc_fits(x, x_stride, w, R, H)) return false;
-  const int ntiles = (R + kRtcMaxN - 1) / kRtcMaxN;
+  // enough row tiles for the grid to cover the SMs (every CTA streams its
+  // token tile's x once, so splitting the rows multiplies only L2 reads of x)
+  const int mtiles = (T + kRtcTokens - 1) / kRtcTokens;
+  const int min_tiles = (R + kRtcMaxN - 1) / kRtcMaxN;
+  const int max_tiles = (R + 15) / 16;
+  const int want = (sm_count() + mtiles - 1) / mtiles;
+  const int ntiles = want < min_tiles ? min_tiles : (want > max_tiles ? max_tiles : want);
   const int nt = ((R + ntiles - 1) / ntiles + 15) / 16 * 16;
+  int cols = 32;
+  while (cols < nt) cols <<= 1;
   CUtensorMap tx, tw;
   if (encode_tmap_2d(&tx, x, 2, H, T, static_cast<uint64_t>(x_stride) * 2, 64, kRtcTokens)) return false;
   if (encode_tmap_2d(&tw, w, 2, H, R, static_cast<uint64_t>(H) * 2, 64, nt)) return false;
@@ -736,10 +744,11 @@ bool launch_router_tc(const void* x, int64_t x_stride, const void* w, const floa
   a.T = T;
   a.KB = H / 64;
   a.nt = nt;
+  a.tmem_cols = cols;
   a.out = static_cast<__nv_bfloat16*>(logits);
   a.out_stride = logits_stride;
   a.status = status;
-  launch_kernel(router_tc_kernel, dim3((T + kRtcTokens - 1) / kRtcTokens, ntiles), dim3(kRtcThreads),
+  launch_kernel(router_tc_kernel, dim3(mtiles, (R + nt - 1) / nt), dim3(kRtcThreads),
                 RtcSmem::bytes(nt), s, tx, tw, a);
   return true;
 }
