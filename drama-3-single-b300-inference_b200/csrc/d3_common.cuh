@@ -331,6 +331,15 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Gated projection input (src/drama3/fused_projection.py:22-29): with a gate,
+// x becomes bf16(x * a) where a = bf16(silu(g)) (mode 1, GATE_SWIGLU) or
+// bf16(sigmoid(g)) (mode 2, GATE_SIGMOID), sigmoid(g) = 1 / (1 + exp(-g)) in
+// fp32.
+__device__ __forceinline__ float gate_activation(float g, int mode) {
+  const float sg = 1.0f / (1.0f + expf(-g));
+  return bf16_round(mode == 1 ? g * sg : sg);
+}
+
 // Activation FP8 quantiser for one 128-element group: scale = max(amax,1e-10)/448
 // (IEEE division), element = clamp(x/scale, -448, 448) rounded to E4M3.
 __device__ __forceinline__ float act_scale_from_amax(float amax) {
@@ -375,6 +384,27 @@ __device__ __forceinline__ uint32_t act_quant4(float x0, float x1, float x2, flo
          (static_cast<uint32_t>(f32x2_to_e4m3x2(act_quant_value(x2, scale, rs),
                                                 act_quant_value(x3, scale, rs)))
           << 16);
+}
+
+// Exact split of a bf16 activation group for the FP8 tensor cores: with s
+// chosen so that the group's max magnitude lies in [2^7, 2^8) after scaling
+// by 2^s, x * 2^s = hi + lo / 16 with hi = e4m3(x * 2^s) and
+// lo = e4m3((x * 2^s - hi) * 16), exact for |x * 2^s| >= 2^-6 (error below
+// 2^-21 of the group max otherwise). shift_for_amax returns s.
+__device__ __forceinline__ int shift_for_amax(float amax) {
+  int e = 8;
+  if (amax > 0.f && isfinite(amax)) frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+  return 8 - e;
+}
+// Four scaled values -> their hi and lo E4M3 bytes (little-endian order).
+__device__ __forceinline__ void split_e4m3x4(const float (&xs)[4], uint32_t& hi, uint32_t& lo) {
+  const uint16_t h01 = f32x2_to_e4m3x2(xs[0], xs[1]), h23 = f32x2_to_e4m3x2(xs[2], xs[3]);
+  const uint32_t hh01 = e4m3x2_to_f16x2(h01), hh23 = e4m3x2_to_f16x2(h23);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hh01));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hh23));
+  hi = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
+  lo = static_cast<uint32_t>(f32x2_to_e4m3x2((xs[0] - a.x) * 16.0f, (xs[1] - a.y) * 16.0f)) |
+       (static_cast<uint32_t>(f32x2_to_e4m3x2((xs[2] - b.x) * 16.0f, (xs[3] - b.y) * 16.0f)) << 16);
 }
 
 }  // namespace d3

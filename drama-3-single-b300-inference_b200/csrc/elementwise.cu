@@ -284,13 +284,6 @@ __global__ void prequant_scatter_kernel(const uint8_t* __restrict__ q, int64_t q
 // so that the group amax lands in [2^14, 2^15); the GEMV multiplies by 2^-s.
 // Within each 128-element block, element k is stored at dense_act_position(k)
 // (expert_gemv.cuh).
-// Gated projection input (src/drama3/fused_projection.py:22-29): with a gate,
-// x becomes bf16(x * a) where a = bf16(silu(g)) (GATE_SWIGLU) or
-// bf16(sigmoid(g)) (GATE_SIGMOID), sigmoid(g) = 1 / (1 + exp(-g)) in fp32.
-__device__ __forceinline__ float gate_activation(float g, int mode) {
-  const float sg = 1.0f / (1.0f + expf(-g));
-  return bf16_round(mode == GATE_SWIGLU ? g * sg : sg);
-}
 
 __global__ void dense_act_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T,
                                       int K, __half* __restrict__ xh, float* __restrict__ inv,
@@ -384,30 +377,16 @@ __global__ void dense_split_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
 #pragma unroll
   for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
   amax = half_warp_max(amax);
-  int e = 8;
-  if (amax > 0.f && isfinite(amax)) frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
-  const int sh = 8 - e;
+  const int sh = shift_for_amax(amax);
   const float mul = ldexpf(1.0f, sh);
   if (!valid) return;
   uint32_t h[2], l[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    float xs[4], hf[4], lv[4];
+    float xs[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) xs[j] = f[4 * i + j] * mul;
-    const uint16_t h01 = f32x2_to_e4m3x2(xs[0], xs[1]), h23 = f32x2_to_e4m3x2(xs[2], xs[3]);
-    const uint32_t hh01 = e4m3x2_to_f16x2(h01), hh23 = e4m3x2_to_f16x2(h23);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hh01));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hh23));
-    hf[0] = a.x;
-    hf[1] = a.y;
-    hf[2] = b.x;
-    hf[3] = b.y;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) lv[j] = (xs[j] - hf[j]) * 16.0f;
-    h[i] = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
-    l[i] = static_cast<uint32_t>(f32x2_to_e4m3x2(lv[0], lv[1])) |
-           (static_cast<uint32_t>(f32x2_to_e4m3x2(lv[2], lv[3])) << 16);
+    split_e4m3x4(xs, h[i], l[i]);
   }
   const int64_t off = static_cast<int64_t>(row) * K + g * 128 + hl * 8;
   *reinterpret_cast<uint2*>(hi + off) = make_uint2(h[0], h[1]);
