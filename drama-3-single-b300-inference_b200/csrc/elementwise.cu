@@ -171,12 +171,20 @@ __global__ void __launch_bounds__(256)
   __shared__ int hist[kFusedPermuteMaxExperts];
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = T * k;
+  // this thread's first activation chunk, loaded while the pairs are counted
+  const int G = H / 128;
+  const int half = lane >> 4, hl = lane & 15;
+  const int64_t src = gather_row(rg, t);
+  uint4 v0 = make_uint4(0, 0, 0, 0);
+  if (warp < (G + 1) / 2 && 2 * warp + half < G)
+    v0 = __ldg(reinterpret_cast<const uint4*>(x + src * x_stride + (2 * warp + half) * 128 + hl * 8));
   for (int j = warp; j < k; j += 8) {
     const int p = t * k + j;
     const int64_t e = __ldg(ids + p);
     const bool ok = e >= 0 && e < E;
     int c = 0;
     if (ok)
+#pragma unroll 8
       for (int q = lane; q < P; q += 32) {
         const int64_t f = __ldg(ids + q);
         c += (f >= 0 && f < E && (f < e || (f == e && q < p))) ? 1 : 0;
@@ -224,14 +232,14 @@ __global__ void __launch_bounds__(256)
     }
   }
   __syncthreads();
-  const int G = H / 128;
-  const int half = lane >> 4, hl = lane & 15;
-  const int64_t src = gather_row(rg, t);
   for (int gp = warp; gp < (G + 1) / 2; gp += 8) {
     const int g = 2 * gp + half;
     const bool valid = g < G;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + src * x_stride + g * 128 + hl * 8));
+    uint4 v = v0;
+    if (gp != warp) {
+      v = make_uint4(0, 0, 0, 0);
+      if (valid) v = __ldg(reinterpret_cast<const uint4*>(x + src * x_stride + g * 128 + hl * 8));
+    }
     float f[8];
     unpack_bf16x8(v, f);
     float amax = 0.f;

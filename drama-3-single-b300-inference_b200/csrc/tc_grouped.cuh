@@ -191,25 +191,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int ngroups = args.E + args.has_shared;
 
   pdl_wait();  // counts, activations and outputs belong to earlier kernels
-  // tiles per group and their exclusive prefix (serial in one warp: <= 1025 groups)
+  // tiles per group and their exclusive prefix (serial in one warp: <= 1025
+  // groups). The counts of 8 x 32 groups are loaded together before the scan
+  // consumes them (one L2 round trip per 256 groups instead of per 32).
   if (warp == 0) {
+    constexpr int kPass = 8;
     int running = 0;
-    for (int base = 0; base < ngroups; base += 32) {
-      const int g = base + lane;
-      int nt = 0;
-      if (g < ngroups) {
-        const int cnt = (args.has_shared && g == 0) ? args.shared_count
-                                                    : args.counts[g - args.has_shared];
-        nt = ((cnt + 127) / 128) * args.ntiles;
-      }
-      int incl = nt;
+    for (int b0 = 0; b0 < ngroups; b0 += 32 * kPass) {
+      int cnt[kPass];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
+      for (int j = 0; j < kPass; ++j) {
+        const int g = b0 + 32 * j + lane;
+        cnt[j] = g >= ngroups ? 0
+                 : (args.has_shared && g == 0) ? args.shared_count
+                                               : args.counts[g - args.has_shared];
       }
-      if (g < ngroups) prefix[g] = running + incl - nt;
-      running += __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+      for (int j = 0; j < kPass; ++j) {
+        const int g = b0 + 32 * j + lane;
+        const int nt = g < ngroups ? ((cnt[j] + 127) / 128) * args.ntiles : 0;
+        int incl = nt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        if (g < ngroups) prefix[g] = running + incl - nt;
+        running += __shfl_sync(0xffffffffu, incl, 31);
+      }
     }
     if (lane == 0) prefix[ngroups] = running;
   }
