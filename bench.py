@@ -44,7 +44,7 @@ N_QKV, N_O = 4096, 2048
 
 # DRAM traffic of one gate_up launch of the default decode step, as ncu
 # measured it (not measured by this script; see the profile named here).
-GATE_UP_TRAFFIC_BYTES = 404.28e6
+GATE_UP_TRAFFIC_BYTES = 404.70e6
 GATE_UP_TRAFFIC_SOURCE = ("profiles/expert_gemv_T64_full.md: dram__bytes_read.sum + "
                           "dram__bytes_write.sum of the gate_up launch, ncu --set full")
 
