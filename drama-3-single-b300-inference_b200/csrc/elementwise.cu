@@ -950,6 +950,8 @@ extern "C" int d3_ep_unpack_fp8(const uint8_t* recv, int rows, int k, int H, flo
                                 int64_t* ids, void* weights, d3_stream_t stream) {
   D3_REQUIRE(rows >= 0 && k > 0 && H > 0 && H % 128 == 0 && recv && scales && ids && weights,
              "ep_unpack_fp8: bad arguments");
+  // the rows are read in place afterwards by TMA (16-byte aligned rows)
+  D3_REQUIRE(aligned(recv, 16), "ep_unpack_fp8: the received rows must be 16-byte aligned");
   const int row_bytes = (H + 4 * (H / 128) + 10 * k + 15) / 16 * 16;
   const int64_t n = static_cast<int64_t>(rows) * (H / 128 + k);
   if (n == 0) return D3_OK;

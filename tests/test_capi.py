@@ -97,6 +97,27 @@ def test_invalid_arguments_fail_before_launch(lib):
     assert b"multiples of 128" in lib.d3_last_error_string()
 
 
+def test_expert_parallel_entry_points_check_arguments(lib):
+    from d3moe import _lib
+    n = ctypes.c_int(0)
+    assert lib.d3_ep_row_bytes_fp8(2048, 8, ctypes.byref(n)) == _lib.D3_OK
+    assert n.value == 2192 and n.value % 16 == 0
+    assert lib.d3_ep_row_bytes_fp8(2000, 8, ctypes.byref(n)) == _lib.D3_EINVAL
+    # more ranks than the planner supports
+    rc = lib.d3_ep_plan_rows(ctypes.c_void_p(16), 4, 8, 16, 4096, ctypes.c_void_p(16),
+                             ctypes.c_void_p(16), None)
+    assert rc == _lib.D3_EINVAL
+    # pack: H not a multiple of 128
+    rc = lib.d3_ep_pack_fp8(ctypes.c_void_p(256), 100, ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 8,
+                            100, 16, 2, None, ctypes.c_void_p(256), None)
+    assert rc == _lib.D3_EINVAL
+    # unpack: received rows not 16-byte aligned
+    rc = lib.d3_ep_unpack_fp8(ctypes.c_void_p(264), 4, 8, 2048, ctypes.c_void_p(256),
+                              ctypes.c_void_p(256), ctypes.c_void_p(256), None)
+    assert rc == _lib.D3_EINVAL
+    assert b"16-byte aligned" in lib.d3_last_error_string()
+
+
 def test_down_stage_refuses_an_unfilled_workspace(lib):
     """d3_moe_down_combine checks its host-side record of the first stage
     before anything reaches the device."""
