@@ -419,7 +419,8 @@ D3_API int d3_ep_dispatch_meta(const int64_t* ids, const void* weights, int T, i
  * where that is -1. d3_ep_unpack_fp8 copies the scales [rows, H/128], ids
  * [rows, k] and weights [rows, k] of `rows` received rows out; the e4m3 bytes
  * are read in place (row stride row_bytes), e.g. by d3_moe_experts_fp8 with
- * scales_transposed = 0. H a multiple of 128. */
+ * scales_transposed = 0. H a multiple of 128; send and recv 16-byte aligned
+ * (D3_EINVAL otherwise). */
 D3_API int d3_ep_row_bytes_fp8(int H, int k, int* bytes);
 D3_API int d3_ep_pack_fp8(const void* x, int64_t x_stride, const int64_t* ids, const void* weights,
                           int T, int k, int H, int experts_per_rank, int ranks, const int32_t* slot,
