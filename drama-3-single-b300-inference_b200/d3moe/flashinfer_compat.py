@@ -57,11 +57,14 @@ def unshuffle_block_major_k(weight: torch.Tensor) -> torch.Tensor:
     """Inverse of the reference's blocked_moe_weight (model.py:41-52): e4m3
     [E, K/128, rows, 128] (the shape blocked_moe_weight returns) or the same
     bytes as [E, rows, K] -> the MajorK tensor [E, rows, K] it was made from.
-    Cached per input tensor (data_ptr, shape)."""
-    key = (weight.data_ptr(), tuple(weight.shape))
+    Cached per input (address, shape, dtype). The entry holds a reference to
+    the input, so no other tensor can take its address while it is cached,
+    and the input's version counter, so an in-place write to the weights (or
+    to any view of them) makes the next call un-shuffle again."""
+    key = (weight.data_ptr(), tuple(weight.shape), weight.dtype)
     hit = _unshuffled.get(key)
-    if hit is not None:
-        return hit
+    if hit is not None and hit[1] == weight._version:
+        return hit[2]
     from flashinfer.utils import get_shuffle_matrix_a_row_indices
 
     if weight.dim() == 4:
@@ -79,7 +82,7 @@ def unshuffle_block_major_k(weight: torch.Tensor) -> torch.Tensor:
     blocks = weight.view(torch.uint8).reshape(E, K // 128, rows, 128)
     out = blocks[:, :, inverse.to(weight.device), :].permute(0, 2, 1, 3).contiguous()
     out = out.view(E, rows, K).view(weight.dtype)
-    _unshuffled[key] = out
+    _unshuffled[key] = (weight, weight._version, out)
     return out
 
 

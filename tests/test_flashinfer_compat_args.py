@@ -77,3 +77,32 @@ def test_block_major_k_unshuffle_inverts_the_reference_shuffle():
             back = unshuffle_block_major_k(shaped.view(torch.float8_e4m3fn))
             assert back.shape == (E_, rows, K)
             assert torch.equal(back.view(torch.uint8), w)
+
+
+def test_block_major_k_cache_follows_in_place_writes():
+    """The un-shuffled copy is cached per weight tensor; writing the weights in
+    place (through any view) must not return the stale copy, and the cache
+    keeps its input alive so that no other tensor can take its address."""
+    pytest.importorskip("flashinfer")
+    from flashinfer.utils import get_shuffle_matrix_a_row_indices
+
+    from d3moe import flashinfer_compat as fc
+
+    g = torch.Generator().manual_seed(1)
+    E_, rows, K = 2, 256, 256
+    w = torch.randint(0, 256, (E_, rows, K), generator=g, dtype=torch.uint8)
+    order = get_shuffle_matrix_a_row_indices(w[0], 64)
+
+    def shuffle(m):
+        return m.view(E_, rows, K // 128, 128).permute(0, 2, 1, 3)[:, :, order, :].contiguous()
+
+    blocked = shuffle(w).view(torch.float8_e4m3fn)
+    first = fc.unshuffle_block_major_k(blocked)
+    assert fc.unshuffle_block_major_k(blocked) is first  # cached
+    w2 = torch.randint(0, 256, (E_, rows, K), generator=g, dtype=torch.uint8)
+    blocked.view(torch.uint8).copy_(shuffle(w2))  # in place, through a view
+    again = fc.unshuffle_block_major_k(blocked)
+    assert again is not first
+    assert torch.equal(again.view(torch.uint8), w2)
+    key = (blocked.data_ptr(), tuple(blocked.shape), blocked.dtype)
+    assert fc._unshuffled[key][0] is blocked
