@@ -134,12 +134,14 @@ class MoE:
         """Returns (routed, shared, shared_gate) like model.py:490-518."""
         layer = layer_view(layer)
         E = layer.experts.w13_weight.shape[0]
-        logits = ops.router_logits(x, layer.router_weight)
-        router, shared_gate = logits[:, :E], logits[:, E:E + 1]
+        # the bias enters before the bf16 rounding of the logits, as in moe()
         bias = getattr(layer, "router_bias", None)
+        if bias is not None:
+            bias = bias.to(torch.float32).contiguous()
+        logits = ops.router_logits(x, layer.router_weight, bias)
+        router, shared_gate = logits[:, :E], logits[:, E:E + 1]
         slots, start = self._padding(row_slots)
-        weights, ids = ops.route_topk(router, self.top_k, bias=bias, row_slots=slots,
-                                      padding_start=start)
+        weights, ids = ops.route_topk(router, self.top_k, row_slots=slots, padding_start=start)
         routed, shared = ops.moe_experts(x, ids, weights, layer.experts, layer.shared_expert,
                                          workspace=self._workspace(len(x), layer))
         return routed, shared, shared_gate

@@ -64,6 +64,22 @@ def test_reference_layer_object_matches_oracle(ref_layer, T):
     assert (deq - w13.float()).abs().max() <= w13.float().abs().max() / 16
 
 
+def test_biased_router_moe_parts_match_moe(ref_layer):
+    """With a per-expert router bias (N(0,1), as in the 24-layer benchmark
+    stack) moe_parts routes on the same biased bf16 logits as moe(), so
+    moe_parts + combine_experts equals moe() bit for bit."""
+    from d3moe import model, ops
+    view = model.layer_view(ref_layer)
+    bias = torch.randn(E, generator=torch.Generator(device="cpu").manual_seed(5)).cuda()
+    layer = SimpleNamespace(experts=view.experts, shared_expert=view.shared_expert,
+                            router_weight=view.router_weight, router_bias=bias)
+    m = model.MoE()
+    x = torch.randn((64, H), generator=torch.Generator(device="cpu").manual_seed(6)).to(torch.bfloat16).cuda()
+    out = m.moe(x, layer)
+    routed, shared, gate = m.moe_parts(x, layer)
+    assert torch.equal(ops.combine_experts(routed, shared, gate), out)
+
+
 def test_linear_is_the_fp8_projection(ref_layer):
     """kernels.linear(x, weight) (kernels.py:274-287): the weight is quantised
     once on first use and every call is the FP8 GEMV of that registration."""
