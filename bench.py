@@ -291,9 +291,9 @@ def run_ep(args, world: int, rank: int, local: int, dev) -> None:
                 self.marks[name].record(torch.cuda.current_stream(dev))
                 self.recorded.add(name)
 
-        def router_logits(self, x, router_weight):
+        def router_logits(self, x, router_weight, bias=None):
             self.mark("layer")
-            return super().router_logits(x, router_weight)
+            return super().router_logits(x, router_weight, bias)
 
         def pack_fp8(self, *a, **kw):
             self.mark("pack")

@@ -57,8 +57,9 @@ def ep_row_bytes_fp8(H: int, k: int) -> int:
 class CudaEPOps:
     """Device steps of the EP layer on the current CUDA stream."""
 
-    def router_logits(self, x, router_weight):
-        return _ops.router_logits(x, router_weight)
+    def router_logits(self, x, router_weight, bias=None):
+        """bf16 logits [T, E+1]; bias f32 [E] enters before the bf16 rounding."""
+        return _ops.router_logits(x, router_weight, bias)
 
     def route(self, logits, k, bias=None):
         return _ops.route_topk(logits, k, bias=bias, weights_dtype=torch.bfloat16)
@@ -133,7 +134,9 @@ class ExpertParallelMoE:
 
     router_weight: bf16 [E+1, H] (router rows + shared-expert gate row),
     replicated. experts_local: this rank's experts (w13_weight [E/N, 2I, H],
-    ...). shared: the shared expert (E = 1), replicated."""
+    ...). shared: the shared expert (E = 1), replicated. router_bias:
+    optional per-expert f32 [E], added to the router logits before their bf16
+    rounding (as d3_moe_layer does), so routing matches the 1-GPU layer."""
 
     def __init__(self, router_weight, experts_local, shared, num_experts: int, top_k: int = 8,
                  group=None, ops=None, router_bias=None, mode: str = "capacity"):
@@ -151,7 +154,9 @@ class ExpertParallelMoE:
         if experts_local.w13_weight.shape[0] != self.E_local:
             raise ValueError("experts_local must hold exactly num_experts / world_size experts")
         self.router = router_weight
-        self.router_bias = router_bias
+        # f32 [E], added to the router logits before their bf16 rounding, as
+        # in the single-GPU layer
+        self.router_bias = None if router_bias is None else router_bias.to(torch.float32).contiguous()
         self.experts = experts_local
         self.shared = shared
         self.k = top_k
@@ -209,8 +214,8 @@ class ExpertParallelMoE:
         ops = self.ops
         N = self.world
         T, H = x.shape
-        logits = ops.router_logits(x, self.router)
-        weights, ids = ops.route(logits[:, : self.E], self.k, bias=self.router_bias)
+        logits = ops.router_logits(x, self.router, self.router_bias)
+        weights, ids = ops.route(logits[:, : self.E], self.k)
         shared, side = self._shared_begin(x)
         send = ops.pack_fp8(x, ids, weights, self.E_local, N)
         recv = torch.empty_like(send)
@@ -230,8 +235,8 @@ class ExpertParallelMoE:
         ops = self.ops
         N = self.world
         T, H = x.shape
-        logits = ops.router_logits(x, self.router)
-        weights, ids = ops.route(logits[:, : self.E], self.k, bias=self.router_bias)
+        logits = ops.router_logits(x, self.router, self.router_bias)
+        weights, ids = ops.route(logits[:, : self.E], self.k)
         send_counts_dev, slot = ops.plan_rows(ids, self.E_local, N)
         shared, side = self._shared_begin(x)
         # row counts: device -> all_to_all -> host (the one host synchronisation)

@@ -32,8 +32,10 @@ class CpuExperts:
 
 
 class CpuEPOps:
-    def router_logits(self, x, router_weight):
-        return _bf16(O.router_logits(_np(x), _np(router_weight)))
+    def router_logits(self, x, router_weight, bias=None):
+        if bias is None:
+            return _bf16(O.router_logits(_np(x), _np(router_weight)))
+        return _bf16(O.router_logits(_np(x), _np(router_weight), bias.numpy(), nbias=bias.numel()))
 
     def route(self, logits, k, bias=None):
         w, ids = O.route(_np(logits), k, None if bias is None else bias.numpy())

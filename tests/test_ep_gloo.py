@@ -46,7 +46,7 @@ def _layer():
     return ex, sh, router
 
 
-def _worker(rank, world, port, result_dir, mode):
+def _worker(rank, world, port, result_dir, mode, biased=False):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "drama-3-single-b300-inference_b200")]
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -62,27 +62,45 @@ def _worker(rank, world, port, result_dir, mode):
     rng = np.random.default_rng(100 + rank)
     rows = T + rank if mode == "exact" else T  # ragged token counts where the mode allows them
     x = O.bf16_round(rng.standard_normal((rows, H)).astype(np.float32))
+    # per-expert router bias, N(0,1) like the 24-layer benchmark stack's
+    bias = np.random.default_rng(7).standard_normal(E).astype(np.float32) if biased else None
     layer = ExpertParallelMoE(_bf16(router), CpuExperts(local, n, I, H), CpuExperts(sh, 1, I, H), E, K,
-                              ops=CpuEPOps(), mode=mode)
+                              ops=CpuEPOps(), mode=mode,
+                              router_bias=None if bias is None else torch.from_numpy(bias))
     out, ids, w = layer.forward(_bf16(x), return_routing=True)
-    ref, ids_ref, _ = O.moe_layer(x, router, ex, sh, K)
+    ref, ids_ref, w_ref = O.moe_layer(x, router, ex, sh, K, bias=bias)
     np.save(Path(result_dir) / f"r{rank}.npy", np.stack([out.float().numpy(), ref]))
     np.save(Path(result_dir) / f"ids{rank}.npy", np.stack([ids.numpy(), ids_ref]))
+    np.save(Path(result_dir) / f"w{rank}.npy", np.stack([w.float().numpy(), w_ref]))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def _check_ranks(tmp_path, world):
+    for r in range(world):
+        out, ref = np.load(tmp_path / f"r{r}.npy")
+        ids, ids_ref = np.load(tmp_path / f"ids{r}.npy")
+        np.testing.assert_array_equal(ids, ids_ref)
+        w, w_ref = np.load(tmp_path / f"w{r}.npy")  # bf16 routing weights, bit-exact
+        np.testing.assert_array_equal(w, w_ref)
+        err = np.abs(out - ref).max()
+        rel = np.sqrt(((out - ref) ** 2).sum() / (ref ** 2).sum())
+        assert err <= 2e-2 and rel <= 1e-2, (r, err, rel)
 
 
 @pytest.mark.parametrize("mode", ["capacity", "exact"])
 @pytest.mark.parametrize("world", [2, 4])
 def test_ep_layer_matches_single_process_oracle(tmp_path, world, mode):
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world, join=True)
-    for r in range(world):
-        out, ref = np.load(tmp_path / f"r{r}.npy")
-        ids, ids_ref = np.load(tmp_path / f"ids{r}.npy")
-        np.testing.assert_array_equal(ids, ids_ref)
-        err = np.abs(out - ref).max()
-        rel = np.sqrt(((out - ref) ** 2).sum() / (ref ** 2).sum())
-        assert err <= 2e-2 and rel <= 1e-2, (r, err, rel)
+    _check_ranks(tmp_path, world)
+
+
+@pytest.mark.parametrize("mode", ["capacity", "exact"])
+def test_ep_layer_with_router_bias_matches_oracle(tmp_path, mode):
+    """The router bias enters before the bf16 rounding of the logits on every
+    rank, as in the single-GPU layer, so routing stays exact."""
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), mode, True), nprocs=2, join=True)
+    _check_ranks(tmp_path, 2)
 
 
 def _lonely_worker(rank, world, port, result_dir):
