@@ -16,8 +16,9 @@ Weights in FlashInfer's BlockMajorK layout (use_shuffled_weight=True,
 weight_layout=BlockMajorK: what the reference passes when
 DRAMA3_MOE_LAYOUT=blocked, model.py:152, 203-206, 574-576, shuffled by
 blocked_moe_weight, model.py:41-52) are brought back to the MajorK
-checkpoint layout once per weight tensor (a copy, cached per input tensor until it is written in place) and
-then run like MajorK weights. The shuffle moves 128-byte K blocks to the
+checkpoint layout once per weight tensor (a copy, cached per input tensor
+until that tensor is written in place) and then run like MajorK weights.
+The shuffle moves 128-byte K blocks to the
 front ([E, K/128, rows, 128]) and permutes the rows inside each K block by
 FlashInfer's epilogue row map for a 64-row tile
 (flashinfer.utils.get_shuffle_matrix_a_row_indices); the scales keep their
