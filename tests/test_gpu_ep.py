@@ -27,7 +27,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result_dir, T, mode="capacity"):
+def _worker(rank, world, port, result_dir, T, mode="capacity", biased=False):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "drama-3-single-b300-inference_b200")]
     import torch.distributed as dist
 
@@ -42,16 +42,23 @@ def _worker(rank, world, port, result_dir, T, mode="capacity"):
     from d3moe.ep import ExpertParallelMoE, shard_experts
 
     lw = synth.make_layer(E, I, H, seed=5, device=dev)
-    layer = ExpertParallelMoE(lw.router, shard_experts(lw.experts, rank, world), lw.shared, E, K, mode=mode)
+    # per-expert N(0,1) router bias (the 24-layer benchmark stack's), the same on every rank
+    bias = (torch.randn(E, generator=torch.Generator(device="cpu").manual_seed(9)).to(dev)
+            if biased else None)
+    layer = ExpertParallelMoE(lw.router, shard_experts(lw.experts, rank, world), lw.shared, E, K, mode=mode,
+                              router_bias=bias)
     g = torch.Generator(device=dev)
     g.manual_seed(77 + rank)
     rows = T + 3 * rank if mode == "exact" else T
     x = torch.randn((rows, H), generator=g, device=dev).to(torch.bfloat16)
     out, ids, w = layer.forward(x, return_routing=True)
-    ref, ids_ref, w_ref = ops.moe_layer(x, lw.router, lw.experts, lw.shared, K, return_routing=True)
+    ref, ids_ref, w_ref = ops.moe_layer(x, lw.router, lw.experts, lw.shared, K, router_bias=bias,
+                                        return_routing=True)
     torch.cuda.synchronize()
     np.save(Path(result_dir) / f"r{rank}.npy", np.stack([out.float().cpu().numpy(), ref.float().cpu().numpy()]))
     np.save(Path(result_dir) / f"ids{rank}.npy", np.stack([ids.cpu().numpy(), ids_ref.cpu().numpy()]))
+    if biased:
+        np.save(Path(result_dir) / f"w{rank}.npy", np.stack([w.float().cpu().numpy(), w_ref.float().cpu().numpy()]))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -61,6 +68,9 @@ def _check(result_dir, world):
         out, ref = np.load(Path(result_dir) / f"r{r}.npy")
         ids, ids_ref = np.load(Path(result_dir) / f"ids{r}.npy")
         np.testing.assert_array_equal(ids, ids_ref)
+        if (Path(result_dir) / f"w{r}.npy").exists():  # bf16 routing weights, bit-exact
+            w, w_ref = np.load(Path(result_dir) / f"w{r}.npy")
+            np.testing.assert_array_equal(w, w_ref)
         err = np.abs(out - ref).max()
         rel = np.sqrt(((out - ref) ** 2).sum() / (ref ** 2).sum())
         assert err <= 2e-2 and rel <= 1e-2, (r, err, rel)
@@ -72,6 +82,17 @@ def test_ep_one_rank_matches_fused_layer(tmp_path, mode):
         pytest.skip("no CUDA device")
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(1, _free_port(), str(tmp_path), 64, mode), nprocs=1, join=True)
+    _check(tmp_path, 1)
+
+
+@pytest.mark.parametrize("mode", ["capacity", "exact"])
+def test_ep_one_rank_with_router_bias_matches_fused_layer(tmp_path, mode):
+    """With a per-expert router bias the EP layer routes on the same biased
+    bf16 logits as the fused layer: ids and routing weights bit for bit."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import torch.multiprocessing as mp
+    mp.spawn(_worker, args=(1, _free_port(), str(tmp_path), 64, mode, True), nprocs=1, join=True)
     _check(tmp_path, 1)
 
 
